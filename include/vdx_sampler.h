@@ -1,0 +1,241 @@
+/*
+ * vdx_sampler.h - C ABI of the B200 (sm_100a) token sampler.
+ *
+ * Drop-in for the sampling hot path of VindexLLM: TVdxSampler in
+ * src/VindexLLM.Sampler.pas. The reference samples on the host after
+ * TVdxInference.RunUnembedding (src/VindexLLM.Inference.pas:327-339) has mapped and
+ * copied the fp32 logits row out of GPU memory (src/VindexLLM.Compute.pas:718-725).
+ * This library samples directly from device-resident [batch, vocab] fp32 or bf16
+ * logits, so only token IDs cross PCIe.
+ *
+ * Conventions
+ *   - Every entry point is extern "C", cdecl, and takes plain pointers and sizes.
+ *   - Functions return VDXS_OK (0) or a negative VDXS_E_* code; nothing traps or
+ *     aborts. vdxs_last_error() returns a readable message for the last failure.
+ *   - Pointers named d_* are device pointers on the context's device; h_* are host
+ *     pointers. `stream` is a cudaStream_t (NULL = legacy default stream). Work on
+ *     device buffers is enqueued on `stream` and is asynchronous unless stated.
+ *   - The library never writes the caller's logits. The reference applies the
+ *     repetition penalty in place (Sampler.pas:285-303); the result is the same.
+ *   - One context per host thread (or serialise calls on a context yourself).
+ */
+#ifndef VDX_SAMPLER_H
+#define VDX_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define VDXS_API __declspec(dllexport)
+#else
+#define VDXS_API __attribute__((visibility("default")))
+#endif
+
+#define VDXS_ABI_VERSION 1
+
+/* ------------------------------------------------------------------------------
+ * Configuration record.
+ * Mirrors TVdxSamplerConfig (src/VindexLLM.Sampler.pas:26-34) field by field under
+ * the reference's {$A8} record alignment (src/VindexLLM.Defines.inc:13): offsets
+ * 0,4,8,12,16,20,24, size 32 bytes, so a Pascal record can be passed by pointer.
+ * ---------------------------------------------------------------------------- */
+typedef struct vdxs_config {
+    float   temperature;    /* 0 = greedy argmax; > 0 = logits are divided by it   */
+    int32_t top_k;          /* 0 (or >= vocab) = full-softmax path                 */
+    float   top_p;          /* >= 1 = nucleus filter off                           */
+    float   min_p;          /* 0 = off; > 0 = floor relative to the top probability */
+    float   repeat_penalty; /* 1 = off; x>0 -> x/p, x<0 -> x*p per history entry    */
+    int32_t repeat_window;  /* history ring length                                  */
+    int64_t seed;           /* 0 = time seeded; > 0 = deterministic                 */
+} vdxs_config;
+
+/* Status codes. */
+#define VDXS_OK              0
+#define VDXS_E_INVALID_ARG  (-1)
+#define VDXS_E_CUDA         (-2)
+#define VDXS_E_NCCL         (-3)
+#define VDXS_E_TIMEOUT      (-4)
+#define VDXS_E_UNSUPPORTED  (-5)
+#define VDXS_E_NO_MEMORY    (-6)
+#define VDXS_E_DEVICE_STATE (-7)
+
+/* Logits element types. bf16 is widened exactly to fp32, then fp32 semantics apply. */
+#define VDXS_DTYPE_F32   0
+#define VDXS_DTYPE_BF16  1
+
+/* Tie modes.
+ * FAITHFUL (default): the token equals what TVdxSampler.Process returns. Rows whose
+ *   result depends on the reference's K-slot min-buffer order (a draw that lands in a
+ *   run of equal probabilities, top_p >= 1 with top_k > 1, or a probability sum whose
+ *   double rounding depends on order) are re-resolved on the GPU by an exact emulation
+ *   of the min-buffer scan (Sampler.pas:341-383) and of its sequential double sums.
+ * CANONICAL: top-k ties and equal-probability order are broken by lowest index; no
+ *   emulation pass. This is the order used by the vocab-sharded path. */
+#define VDXS_TIES_FAITHFUL   0
+#define VDXS_TIES_CANONICAL  1
+
+/* Per-row result flags (optional output of vdxs_sample_ex). */
+#define VDXS_FLAG_GREEDY         (1u << 0)  /* temperature == 0: argmax, no uniform used   */
+#define VDXS_FLAG_TOPK           (1u << 1)  /* 0 < top_k < vocab path                      */
+#define VDXS_FLAG_FULL           (1u << 2)  /* full-softmax path                           */
+#define VDXS_FLAG_BOUNDARY_TIE   (1u << 3)  /* more elements equal the k-th value than fit */
+#define VDXS_FLAG_DRAW_TIE_RUN   (1u << 4)  /* drawn position lies in a run of equal probs */
+#define VDXS_FLAG_NEAR_BOUNDARY  (1u << 5)  /* |t - CDF edge| <= 1e-6 * sum                */
+#define VDXS_FLAG_INEXACT_SUM    (1u << 6)  /* a double sum could depend on summation order */
+#define VDXS_FLAG_FALLBACK       (1u << 7)  /* no cumulative sum exceeded t: fallback token */
+#define VDXS_FLAG_SLOT_ORDER     (1u << 8)  /* reference walks min-buffer slot order        */
+#define VDXS_FLAG_FAITHFUL_PASS  (1u << 9)  /* row re-resolved by the min-buffer emulation  */
+
+/* ------------------------------------------------------------------------------
+ * Library and context.
+ * ---------------------------------------------------------------------------- */
+typedef struct vdxs_context vdxs_context;
+
+/* Returns VDXS_ABI_VERSION. */
+VDXS_API int32_t vdxs_abi_version(void);
+
+/* TVdxSampler.DefaultConfig (Sampler.pas:100-109): 0 / 0 / 1 / 0 / 1 / 64 / 0. */
+VDXS_API void vdxs_default_config(vdxs_config* out);
+
+/* Creates a context bound to CUDA device `device`. The context owns a lazily grown
+ * device workspace (TVdxSampler.EnsureWorkspace, Sampler.pas:250-263). */
+VDXS_API int32_t vdxs_create(int32_t device, vdxs_context** out);
+VDXS_API int32_t vdxs_destroy(vdxs_context* ctx);
+
+/* Message for the last failing call on `ctx` (ctx may be NULL: message of the last
+ * failing call on this thread). Never NULL; "" when there was no error. */
+VDXS_API const char* vdxs_last_error(const vdxs_context* ctx);
+
+/* VDXS_TIES_FAITHFUL or VDXS_TIES_CANONICAL (default FAITHFUL). */
+VDXS_API int32_t vdxs_set_tie_mode(vdxs_context* ctx, int32_t mode);
+VDXS_API int32_t vdxs_get_tie_mode(const vdxs_context* ctx, int32_t* mode);
+
+/* ------------------------------------------------------------------------------
+ * Stateless batched sampling: replaces TVdxSampler.Process (Sampler.pas:265-528)
+ * for `batch` independent rows, with the penalty history and the uniform supplied
+ * by the caller instead of the object's ring and PRNG.
+ *
+ *   d_logits        [batch, row_stride] fp32 or bf16, first `vocab` entries used
+ *   d_history       [batch, history_stride] int32 token ids (ring slots 0..count-1)
+ *                   or NULL; ids outside [0, vocab) are ignored (Sampler.pas:292)
+ *   d_history_count [batch] int32 entries used per row (NULL = no history)
+ *   d_uniform       [batch] fp32 in [0,1): the value NextFloat() would return
+ *                   (Sampler.pas:243-248); ignored when temperature == 0
+ *   d_out_tokens    [batch] int32
+ * ---------------------------------------------------------------------------- */
+VDXS_API int32_t vdxs_sample(vdxs_context* ctx, const vdxs_config* cfg,
+                             const void* d_logits, int32_t dtype, int32_t batch,
+                             int32_t vocab, int64_t row_stride,
+                             const int32_t* d_history, int64_t history_stride,
+                             const int32_t* d_history_count,
+                             const float* d_uniform, int32_t* d_out_tokens,
+                             void* stream);
+
+/* As vdxs_sample, plus optional diagnostics (any may be NULL):
+ *   d_out_flags  [batch] VDXS_FLAG_* bits
+ *   d_out_idx    [batch, out_k] survivor token ids in draw-walk order (-1 padded)
+ *   d_out_prob   [batch, out_k] their unnormalised probabilities after min-p and
+ *                before the top-p cut (the values the reference sums, Sampler.pas:389)
+ * On the full-softmax path d_out_idx/d_out_prob are filled with -1 / 0. */
+VDXS_API int32_t vdxs_sample_ex(vdxs_context* ctx, const vdxs_config* cfg,
+                                const void* d_logits, int32_t dtype, int32_t batch,
+                                int32_t vocab, int64_t row_stride,
+                                const int32_t* d_history, int64_t history_stride,
+                                const int32_t* d_history_count,
+                                const float* d_uniform, int32_t* d_out_tokens,
+                                uint32_t* d_out_flags, int32_t* d_out_idx,
+                                float* d_out_prob, int32_t out_k, void* stream);
+
+/* Host-buffer variant with Process's calling shape: host logits/history/uniforms in,
+ * host tokens out. Copies inputs to the context's device workspace on `stream`,
+ * samples, copies the tokens back and synchronises `stream` before returning.
+ * Pinned host memory gives the fastest copies. */
+VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg,
+                                  const void* h_logits, int32_t dtype, int32_t batch,
+                                  int32_t vocab, int64_t row_stride,
+                                  const int32_t* h_history, int64_t history_stride,
+                                  const int32_t* h_history_count,
+                                  const float* h_uniform, int32_t* h_out_tokens,
+                                  void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Stateful mirror of TVdxSampler: one sampler state (config, xoshiro256** PRNG,
+ * repeat-history ring) per batch row, kept on the host exactly as the reference
+ * keeps it; Process draws the row uniforms from the PRNGs and samples on the GPU.
+ * ---------------------------------------------------------------------------- */
+typedef struct vdxs_sampler vdxs_sampler;
+
+/* TVdxSampler.Create (Sampler.pas:111-122): default config, window 64, time seed. */
+VDXS_API int32_t vdxs_sampler_create(vdxs_context* ctx, int32_t batch, vdxs_sampler** out);
+VDXS_API int32_t vdxs_sampler_destroy(vdxs_sampler* s);
+/* TVdxSampler.SetConfig (Sampler.pas:132-150) applied to every row: reseeds only
+ * if the seed changed; resizes and clears the ring only if the window changed. */
+VDXS_API int32_t vdxs_sampler_set_config(vdxs_sampler* s, const vdxs_config* cfg);
+/* TVdxSampler.GetConfig (Sampler.pas:152-155). */
+VDXS_API int32_t vdxs_sampler_get_config(const vdxs_sampler* s, vdxs_config* out);
+/* TVdxSampler.AddToHistory (Sampler.pas:530-539) for one row, or for every row
+ * (h_tokens[batch]). */
+VDXS_API int32_t vdxs_sampler_add_to_history(vdxs_sampler* s, int32_t row, int32_t token);
+VDXS_API int32_t vdxs_sampler_add_to_history_batch(vdxs_sampler* s, const int32_t* h_tokens);
+/* TVdxSampler.ResetHistory (Sampler.pas:541-549); row = -1 resets every row. */
+VDXS_API int32_t vdxs_sampler_reset_history(vdxs_sampler* s, int32_t row);
+/* TVdxSampler.Process (Sampler.pas:265-528) for all rows on device logits
+ * [batch, row_stride]. Writes the tokens to h_out_tokens (host) and returns after
+ * `stream` has completed. One uniform per row is drawn unless temperature == 0. */
+VDXS_API int32_t vdxs_sampler_process(vdxs_sampler* s, const void* d_logits,
+                                      int32_t dtype, int32_t vocab, int64_t row_stride,
+                                      int32_t* h_out_tokens, void* stream);
+/* The same with host fp32 logits: the exact calling shape of Process(PSingle, V)
+ * used by RunUnembedding today (Inference.pas:336-337). */
+VDXS_API int32_t vdxs_sampler_process_host(vdxs_sampler* s, const float* h_logits,
+                                           int32_t vocab, int64_t row_stride,
+                                           int32_t* h_out_tokens);
+/* PRNG access for resume and tests: NextFloat (Sampler.pas:243-248) of one row, and
+ * the 4-word xoshiro256** state (Sampler.pas:42-45) of one row. */
+VDXS_API int32_t vdxs_sampler_next_float(vdxs_sampler* s, int32_t row, float* out);
+VDXS_API int32_t vdxs_sampler_get_prng_state(const vdxs_sampler* s, int32_t row, uint64_t out_state[4]);
+VDXS_API int32_t vdxs_sampler_set_prng_state(vdxs_sampler* s, int32_t row, const uint64_t state[4]);
+/* Copies one row's ring (slots 0..count-1 in slot order) into h_ids (capacity
+ * `capacity`), sets *count and *pos (Sampler.pas:48-50). */
+VDXS_API int32_t vdxs_sampler_get_history(const vdxs_sampler* s, int32_t row, int32_t* h_ids,
+                                          int32_t capacity, int32_t* count, int32_t* pos);
+
+/* ------------------------------------------------------------------------------
+ * Vocab-sharded sampling over several GPUs (one process or thread per GPU).
+ * Each rank holds a contiguous vocab shard [vocab_offset, vocab_offset + vocab_shard)
+ * of every row. Each rank selects its local top-k (lowest global index wins ties),
+ * the (value, global index) candidates are all-gathered with NCCL, and every rank
+ * runs the identical merge, top-p and draw, so all ranks return the same tokens.
+ * Ties are canonical (lowest global index); history ids are global.
+ * NCCL is loaded at run time (libnccl.so.2) on the first communicator creation.
+ * ---------------------------------------------------------------------------- */
+typedef struct vdxs_comm vdxs_comm;
+
+#define VDXS_NCCL_UNIQUE_ID_BYTES 128
+/* Creates an NCCL unique id on one rank; broadcast the 128 bytes to the others. */
+VDXS_API int32_t vdxs_comm_unique_id(uint8_t out_id[VDXS_NCCL_UNIQUE_ID_BYTES]);
+VDXS_API int32_t vdxs_comm_create(vdxs_context* ctx, int32_t nranks, int32_t rank,
+                                  const uint8_t unique_id[VDXS_NCCL_UNIQUE_ID_BYTES],
+                                  vdxs_comm** out);
+VDXS_API int32_t vdxs_comm_destroy(vdxs_comm* comm);
+
+VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm,
+                                     const vdxs_config* cfg,
+                                     const void* d_logits_shard, int32_t dtype,
+                                     int32_t batch, int32_t vocab_shard,
+                                     int64_t row_stride, int64_t vocab_offset,
+                                     int64_t vocab_total,
+                                     const int32_t* d_history, int64_t history_stride,
+                                     const int32_t* d_history_count,
+                                     const float* d_uniform, int32_t* d_out_tokens,
+                                     uint32_t* d_out_flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VDX_SAMPLER_H */

@@ -1,0 +1,95 @@
+"""The C++ oracle against the golden fixtures (made by the independent Python
+restatement) and against that restatement directly on random inputs."""
+import numpy as np
+from hypothesis import given, settings, strategies as st, HealthCheck
+
+from oracle import pyref
+from vindexllm_b200.abi import default_config, TIES_FAITHFUL, TIES_CANONICAL, FLAG_DRAW_TIE_RUN, \
+    FLAG_SLOT_ORDER, FLAG_INEXACT_SUM, FLAG_GREEDY
+from golden_cases import load_cases
+
+
+def test_oracle_matches_golden(oracle_mod):
+    cases = load_cases()
+    assert len(cases) > 400
+    for cfg, logits, hist, u, tok in cases:
+        got, _, _, _ = oracle_mod.process_row(cfg, logits, hist if len(hist) else None, u, TIES_FAITHFUL)
+        assert got == tok, (cfg, logits.tolist(), hist.tolist(), u)
+
+
+@st.composite
+def row_case(draw):
+    V = draw(st.integers(1, 80))
+    ties = draw(st.booleans())
+    vals = draw(st.lists(st.floats(-8, 8, allow_nan=False, width=32), min_size=V, max_size=V))
+    x = np.array(vals, np.float32)
+    if ties:
+        x = (np.round(x * 2) / 2).astype(np.float32)
+    cfg = default_config(
+        temperature=draw(st.sampled_from([0.0, 0.25, 0.7, 1.0, 1.5])),
+        top_k=draw(st.integers(0, V + 2)),
+        top_p=draw(st.sampled_from([1.0, 0.95, 0.6, 0.0])),
+        min_p=draw(st.sampled_from([0.0, 0.1, 0.6])),
+        repeat_penalty=draw(st.sampled_from([1.0, 1.3, 0.7])))
+    hist = np.array(draw(st.lists(st.integers(-2, V + 1), max_size=10)), np.int32)
+    u = float(np.float32(draw(st.integers(0, (1 << 24) - 1)) / 16777216.0))
+    return cfg, x, hist, u
+
+
+@settings(max_examples=400, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(row_case())
+def test_oracle_matches_pyref(oracle_mod, c):
+    cfg, x, hist, u = c
+    got, _, _, _ = oracle_mod.process_row(cfg, x, hist if len(hist) else None, u, TIES_FAITHFUL)
+    want = pyref.process_row(cfg.as_dict(), [float(v) for v in x], len(x), hist.tolist(), lambda: u)
+    assert got == want
+
+
+@settings(max_examples=300, deadline=None)
+@given(row_case())
+def test_canonical_equals_faithful_when_order_free(oracle_mod, c):
+    """Canonical and faithful differ only in rows flagged as order-dependent."""
+    cfg, x, hist, u = c
+    f_tok, f_fl, _, _ = oracle_mod.process_row(cfg, x, hist if len(hist) else None, u, TIES_FAITHFUL)
+    c_tok, c_fl, _, _ = oracle_mod.process_row(cfg, x, hist if len(hist) else None, u, TIES_CANONICAL)
+    if not (c_fl & (FLAG_DRAW_TIE_RUN | FLAG_SLOT_ORDER | FLAG_INEXACT_SUM)):
+        assert f_tok == c_tok
+
+
+def test_faithful_slot_order_example(oracle_mod):
+    """Sampler.pas:341-383 min-buffer: K=2 over [5,5,7] keeps slots {7@2, 5@1}; the
+    canonical set is {7@2, 5@0}. With top_p=1 the draw walks slot order."""
+    x = np.array([5, 5, 7], np.float32)
+    cfg = default_config(temperature=1.0, top_k=2, top_p=0.5)
+    _, _, fi, _ = oracle_mod.process_row(cfg, x, None, 0.0, TIES_FAITHFUL, out_k=2)
+    _, _, ci, _ = oracle_mod.process_row(cfg, x, None, 0.0, TIES_CANONICAL, out_k=2)
+    assert sorted(fi.tolist()) == [1, 2]
+    assert sorted(ci.tolist()) == [0, 2]
+
+
+def test_batch_matches_rows(oracle_mod):
+    rng = np.random.default_rng(3)
+    B, V = 16, 300
+    x = (rng.normal(size=(B, V)) * 2).astype(np.float32)
+    u = rng.random(B).astype(np.float32)
+    hist = rng.integers(0, V, size=(B, 20)).astype(np.int32)
+    cnt = rng.integers(0, 21, size=B).astype(np.int32)
+    cfg = default_config(temperature=0.8, top_k=10, top_p=0.9, repeat_penalty=1.2)
+    for mode in (TIES_FAITHFUL, TIES_CANONICAL):
+        for nt in (1, 4):
+            toks, fl, _, _ = oracle_mod.sample_batch(cfg, x, u, hist, cnt, mode, nthreads=nt)
+            for r in range(B):
+                t, f, _, _ = oracle_mod.process_row(cfg, x[r], hist[r, :cnt[r]], float(u[r]), mode)
+                assert toks[r] == t and fl[r] == f
+    # bf16 rows are widened exactly
+    xb = (x.view(np.uint32) >> 16).astype(np.uint16)
+    toks, _, _, _ = oracle_mod.sample_batch(cfg, xb, u, hist, cnt, TIES_FAITHFUL)
+    xw = (xb.astype(np.uint32) << 16).view(np.float32)
+    toks2, _, _, _ = oracle_mod.sample_batch(cfg, xw, u, hist, cnt, TIES_FAITHFUL)
+    assert (toks == toks2).all()
+
+
+def test_greedy_flag_and_no_uniform(oracle_mod):
+    x = np.array([1, 3, 3, 2], np.float32)
+    t, f, _, _ = oracle_mod.process_row(default_config(temperature=0.0), x, None, 0.7)
+    assert t == 1 and f & FLAG_GREEDY

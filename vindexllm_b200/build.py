@@ -1,0 +1,72 @@
+"""Build recipe for the sampler library: nvcc, sm_100a only, in-tree output.
+
+``python -m vindexllm_b200.build`` (or ``build()``) compiles csrc/*.cu and csrc/*.cpp
+into vindexllm_b200/libvdxsampler.so. The CUDA runtime is linked statically and its
+symbols are hidden, so the library does not interfere with a host framework's runtime.
+NCCL is not linked: the sharded entry points resolve it with dlopen at run time.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+LIB = os.path.join(HERE, "libvdxsampler.so")
+BUILD_DIR = os.path.join(HERE, "_build")
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+              "-I" + INCLUDE, "--expt-relaxed-constexpr"]
+SOURCES = ["vdxs_kernels.cu", "vdxs_api.cpp"]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def _inputs():
+    files = [os.path.join(CSRC, f) for f in os.listdir(CSRC)]
+    files.append(os.path.join(INCLUDE, "vdx_sampler.h"))
+    return files
+
+
+def stale() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    return any(os.path.getmtime(f) > t for f in _inputs())
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not stale():
+        return LIB
+    nvcc = _nvcc()
+    os.makedirs(BUILD_DIR, exist_ok=True)
+    objs = []
+    for src in SOURCES:
+        obj = os.path.join(BUILD_DIR, os.path.splitext(src)[0] + ".o")
+        lang = [] if src.endswith(".cu") else ["-x", "cu"]
+        cmd = [nvcc, *ARCH, *NVCC_FLAGS, *lang, "-c", os.path.join(CSRC, src), "-o", obj]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        subprocess.run(cmd, check=True)
+        objs.append(obj)
+    tmp = LIB + ".tmp"
+    cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-ldl", "-lpthread",
+           "-Xlinker", "--exclude-libs,ALL"]
+    if verbose:
+        print(" ".join(cmd), file=sys.stderr)
+    subprocess.run(cmd, check=True)
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,101 @@
+// vdxs_internal.h - declarations shared by the C-ABI layer (vdxs_api.cpp) and the
+// sm_100a kernels (vdxs_kernels.cu). Not part of the public ABI.
+#pragma once
+
+#include <cstdint>
+#include <string>
+
+#include <cuda_runtime.h>
+
+namespace vdxs {
+
+constexpr int kThreads = 512;        // threads per CTA in every sampling kernel
+constexpr int kMaxTopK = 1024;       // largest top_k served by the top-k path
+constexpr int kMaxHistory = 8192;    // largest history stride served by the penalty prep
+constexpr int kFaithfulTile = 8192;  // elements per tile of the min-buffer emulation
+
+enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
+
+// Device workspace owned by a context (TVdxSampler.EnsureWorkspace analogue,
+// Sampler.pas:250-263). Grown on demand; never shrunk until the context dies.
+struct Workspace {
+    uint2* cand = nullptr;          // [rows * nchunks * K] stage-1 (key, index) candidates
+    size_t cand_cap = 0;            // elements
+    uint2* chunk_info = nullptr;    // [rows * nchunks] (chunk k-th key, tie-cut flag)
+    size_t chunk_info_cap = 0;
+    uint32_t* row_counter = nullptr;  // [rows] completion counters, self-resetting
+    size_t row_counter_cap = 0;
+    int32_t* pen_ids = nullptr;     // [rows * pen_stride] sorted unique history ids
+    float* pen_vals = nullptr;      // [rows * pen_stride] penalised values
+    int32_t* pen_cnt = nullptr;     // [rows]
+    size_t pen_cap = 0;             // rows * pen_stride
+    size_t pen_rows_cap = 0;
+    uint32_t* fmax = nullptr;       // [rows * nchunks] full path: chunk max keys
+    double* fsum = nullptr;         // [rows * nchunks] full path: chunk sums
+    size_t full_cap = 0;
+    uint2* shard_send = nullptr;    // [rows * K] sharded: local candidates
+    uint2* shard_recv = nullptr;    // [ranks * rows * K]
+    size_t shard_send_cap = 0, shard_recv_cap = 0;
+    int32_t* err = nullptr;         // device error word (0 = ok)
+    // host-buffer entry point staging
+    void* d_logits = nullptr;
+    size_t d_logits_cap = 0;
+    int32_t* d_hist = nullptr;
+    size_t d_hist_cap = 0;
+    int32_t* d_hcnt = nullptr;
+    float* d_unif = nullptr;
+    int32_t* d_tok = nullptr;
+    size_t d_rows_cap = 0;
+    int32_t* h_tok_pinned = nullptr;
+};
+
+// Everything one sampling call needs, already validated by the API layer.
+struct SampleArgs {
+    const void* logits = nullptr;
+    int dtype = 0;
+    int B = 0;
+    int V = 0;                       // local vocab (the shard size when sharded)
+    int64_t stride = 0;              // elements between rows
+    const int32_t* hist = nullptr;
+    int64_t hist_stride = 0;
+    const int32_t* hist_count = nullptr;
+    const float* uniform = nullptr;
+    int32_t* tokens = nullptr;
+    uint32_t* flags = nullptr;
+    int32_t* out_idx = nullptr;
+    float* out_prob = nullptr;
+    int out_k = 0;
+    // resolved configuration
+    int path = kGreedy;
+    int K = 1;
+    float inv_temp = 1.0f;
+    float min_p = 0.0f;
+    float top_p = 1.0f;
+    float penalty = 1.0f;
+    bool penalty_on = false;
+    int tie_mode = 0;
+    // sharding
+    int64_t vocab_offset = 0;
+    int64_t vocab_total = 0;
+    bool local_emit = false;         // emit local top-K candidates instead of drawing
+    cudaStream_t stream = nullptr;
+};
+
+struct LaunchPlan {
+    int chunk = 0;
+    int nchunks = 0;
+    size_t smem = 0;
+};
+
+// Host-side launchers (vdxs_kernels.cu). Return cudaSuccess or the launch error;
+// `err` receives a message for argument/capacity problems (returned as
+// cudaErrorInvalidValue).
+cudaError_t plan_topk(const SampleArgs& a, int device_smem_optin, LaunchPlan* plan, std::string* err);
+cudaError_t plan_full(const SampleArgs& a, LaunchPlan* plan, std::string* err);
+cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPlan& plan, int ranks,
+                             cudaStream_t stream, std::string* err);
+cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err);
+cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std::string* err);
+void free_workspace(Workspace& ws);
+
+}  // namespace vdxs

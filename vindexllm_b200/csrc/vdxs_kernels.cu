@@ -1,0 +1,1618 @@
+// vdxs_kernels.cu - sm_100a kernels of the token sampler.
+//
+// Hot path: TVdxSampler.Process (src/VindexLLM.Sampler.pas:265-528) for a batch of
+// [B, V] device-resident logits.
+//
+//   penalty_prep_kernel   Sampler.pas:285-303  history ids -> sorted unique (id, f^n(x))
+//   topk_fused_kernel     Sampler.pas:305-459  one CTA per (row, chunk): stream the chunk
+//                         once from HBM with 128-bit loads, keep it in shared memory as
+//                         order-preserving keys, radix-select the chunk top-K; the last
+//                         CTA of a row merges the chunk candidates plus the penalised
+//                         history entries, then applies exp / min-p / sort / top-p / draw.
+//                         Rows whose token depends on the reference's min-buffer slot
+//                         order are re-resolved in the same CTA by an exact emulation of
+//                         the scan (faithful mode).
+//   full_max_kernel,      Sampler.pas:461-527  full-softmax path: max pass, then an
+//   full_sum_kernel       exp/sum pass whose last CTA per row locates the draw.
+//   merge_draw_kernel     vocab-sharded path: merge the all-gathered candidates, draw.
+//
+// Ordering: every top-k decision uses the composite order (value desc, index asc) on
+// order-preserving 32-bit keys of the fp32 value (-0 folded onto +0), so ties go to
+// the lowest index. Probabilities are computed as the reference stores them:
+// Single((x - max) * invT evaluated in Double, exp in Double).
+#include "vdxs_internal.h"
+#include "../../include/vdx_sampler.h"
+
+#include <cuda_runtime.h>
+#include <algorithm>
+#include <climits>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+namespace vdxs {
+
+constexpr int NT = kThreads;
+constexpr int NWARPS = NT / 32;
+constexpr unsigned FULL = 0xFFFFFFFFu;
+constexpr int kHistBins = 464;   // log-bins of the distance to the maximum key
+constexpr int kHistWords = 512;
+constexpr int kShWords = 64;
+constexpr size_t kHeadBytes = (kHistWords + kShWords) * 4;  // hist + scalars at smem start
+
+enum ErrCode : int32_t { kErrNone = 0, kErrSelect = 1, kErrFaithful = 2 };
+
+struct KParams {
+    const void* logits;
+    int64_t stride;
+    int V;
+    int B;
+    int chunk;
+    int nchunks;
+    int K;
+    int path;
+    // penalty list (sorted unique local ids and their penalised values); null when off
+    const int32_t* pen_ids;
+    const float* pen_vals;
+    const int32_t* pen_cnt;
+    int pen_stride;
+    // workspace
+    uint2* cand;
+    uint2* chunk_info;
+    uint32_t* row_counter;
+    int32_t* err;
+    uint32_t* fmax;
+    double* fsum;
+    uint2* fstat;  // full path: per chunk (nonzero count, min exponent + 1024 | pmax key)
+    // results
+    const float* uniform;
+    int32_t* tokens;
+    uint32_t* flags;
+    int32_t* out_idx;
+    float* out_prob;
+    int out_k;
+    float inv_temp;
+    float min_p;
+    float top_p;
+    int tie_mode;
+    // sharding
+    int64_t vocab_offset;
+    int local_emit;
+    uint2* emit_out;  // [B][K+1]
+};
+
+// ---------------------------------------------------------------------------------
+// Keys and loads
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t f2key(float f) {
+    uint32_t u = __float_as_uint(f);
+    if (u == 0x80000000u) u = 0u;  // -0.0 compares equal to +0.0
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
+    return __uint_as_float(u);
+}
+__device__ __forceinline__ float ld_elem(const float* p, int64_t i) { return __ldg(p + i); }
+__device__ __forceinline__ float ld_elem(const uint16_t* p, int64_t i) {
+    return __uint_as_float(((uint32_t)__ldg(p + i)) << 16);
+}
+// 128-bit streaming load; the data is read once, so it bypasses L1 allocation.
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+template <typename T> struct VecTraits;
+template <> struct VecTraits<float> { static constexpr int N = 4; };
+template <> struct VecTraits<uint16_t> { static constexpr int N = 8; };
+
+__device__ __forceinline__ void unpack(const uint4& r, float* out, float) {
+    out[0] = __uint_as_float(r.x);
+    out[1] = __uint_as_float(r.y);
+    out[2] = __uint_as_float(r.z);
+    out[3] = __uint_as_float(r.w);
+}
+__device__ __forceinline__ void unpack(const uint4& r, float* out, uint16_t) {
+    out[0] = __uint_as_float(r.x << 16);
+    out[1] = __uint_as_float(r.x & 0xFFFF0000u);
+    out[2] = __uint_as_float(r.y << 16);
+    out[3] = __uint_as_float(r.y & 0xFFFF0000u);
+    out[4] = __uint_as_float(r.z << 16);
+    out[5] = __uint_as_float(r.z & 0xFFFF0000u);
+    out[6] = __uint_as_float(r.w << 16);
+    out[7] = __uint_as_float(r.w & 0xFFFF0000u);
+}
+
+// Log-scale bin of the distance d = kmax - key: exact for d < 16, then 4 mantissa
+// bits per power of two. Monotone in d, 464 bins.
+__device__ __forceinline__ int logbin(uint32_t d) {
+    if (d < 16u) return (int)d;
+    int e = 31 - __clz(d);
+    return 16 + ((e - 4) << 4) + (int)((d >> (e - 4)) & 15u);
+}
+__device__ __forceinline__ void logbin_range(int b, uint32_t* lo, int* bits) {
+    if (b < 16) {
+        *lo = (uint32_t)b;
+        *bits = 0;
+        return;
+    }
+    int e = ((b - 16) >> 4) + 4;
+    int m = (b - 16) & 15;
+    *lo = (uint32_t)(16 + m) << (e - 4);
+    *bits = e - 4;
+}
+
+__device__ __forceinline__ unsigned lanemask_lt() {
+    unsigned m;
+    asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+    return m;
+}
+
+// ---------------------------------------------------------------------------------
+// Block primitives (NT threads)
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, uint32_t* sh) {
+    v = __reduce_max_sync(FULL, v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = (threadIdx.x & 31) < NWARPS ? sh[threadIdx.x & 31] : 0u;
+    return __reduce_max_sync(FULL, r);
+}
+__device__ __forceinline__ uint32_t block_min_u32(uint32_t v, uint32_t* sh) {
+    v = __reduce_min_sync(FULL, v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = (threadIdx.x & 31) < NWARPS ? sh[threadIdx.x & 31] : 0xFFFFFFFFu;
+    return __reduce_min_sync(FULL, r);
+}
+__device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, uint32_t* sh) {
+    v = __reduce_add_sync(FULL, v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = (threadIdx.x & 31) < NWARPS ? sh[threadIdx.x & 31] : 0u;
+    return __reduce_add_sync(FULL, r);
+}
+// Exclusive scan of one int per thread; *total receives the block sum.
+__device__ __forceinline__ int block_excl_scan(int v, int* sh, int* total) {
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(FULL, x, o);
+        if (l >= o) x += y;
+    }
+    __syncthreads();
+    if (l == 31) sh[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        int s = l < NWARPS ? sh[l] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(FULL, s, o);
+            if (l >= o) s += y;
+        }
+        if (l < NWARPS) sh[l] = s;
+    }
+    __syncthreads();
+    *total = sh[NWARPS - 1];
+    return (w > 0 ? sh[w - 1] : 0) + x - v;
+}
+// Exclusive scan of one double per thread (sums of non-negative terms).
+__device__ __forceinline__ double block_excl_scan_d(double v, double* sh, double* total) {
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5;
+    double x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        double y = __shfl_up_sync(FULL, x, o);
+        if (l >= o) x += y;
+    }
+    __syncthreads();
+    if (l == 31) sh[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        double s = l < NWARPS ? sh[l] : 0.0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            double y = __shfl_up_sync(FULL, s, o);
+            if (l >= o) s += y;
+        }
+        if (l < NWARPS) sh[l] = s;
+    }
+    __syncthreads();
+    *total = sh[NWARPS - 1];
+    double r = (w > 0 ? sh[w - 1] : 0.0) + (x - v);
+    return r;
+}
+
+// Descending bitonic sort of n (power of two) 64-bit keys in shared memory.
+__device__ void bitonic_sort_desc(uint64_t* a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += NT) {
+                int ixj = i ^ j;
+                if (ixj > i) {
+                    uint64_t x = a[i], y = a[ixj];
+                    bool desc = (i & k) == 0;
+                    if (desc ? (x < y) : (x > y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+// Warp 0 only: first bin g of hist[0..nb) whose inclusive prefix reaches `need`.
+// Writes sh[0] = g (or -1), sh[1] = count before g, sh[2] = total.
+__device__ void warp_find(const uint32_t* hist, int nb, uint32_t need, uint32_t* sh) {
+    const int l = threadIdx.x & 31;
+    const int seg = (nb + 31) >> 5;
+    const int b0 = min(l * seg, nb), b1 = min(b0 + seg, nb);
+    uint32_t s = 0;
+    for (int b = b0; b < b1; ++b) s += hist[b];
+    uint32_t incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        uint32_t y = __shfl_up_sync(FULL, incl, o);
+        if (l >= o) incl += y;
+    }
+    const uint32_t total = __shfl_sync(FULL, incl, 31);
+    const unsigned m = __ballot_sync(FULL, incl >= need);
+    if (m == 0u) {
+        if (l == 0) {
+            sh[0] = 0xFFFFFFFFu;
+            sh[1] = total;
+        }
+    } else {
+        const int L = __ffs(m) - 1;
+        if (l == L) {
+            uint32_t c = incl - s;
+            int g = b0;
+            for (; g < b1; ++g) {
+                if (c + hist[g] >= need) break;
+                c += hist[g];
+            }
+            sh[0] = (uint32_t)g;
+            sh[1] = c;
+        }
+    }
+    if (l == 0) sh[2] = total;
+}
+
+// ---------------------------------------------------------------------------------
+// Block top-K select on (key desc, tb asc). Keys equal to 0 are invalid and ignored.
+// Finds the K-th best element; the caller emits every element that is not worse.
+// ---------------------------------------------------------------------------------
+struct SelectOut {
+    uint32_t kth_key;  // 0 = every valid element is selected
+    uint32_t kth_tb;
+    uint32_t n_valid;
+    int tie_cut;       // elements equal to kth_key were left out
+};
+
+struct SmemKeySrc {  // stage 1: keys in shared memory, tie-break = position
+    const uint32_t* k;
+    __device__ __forceinline__ uint32_t key(int i) const { return k[i]; }
+    __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
+};
+struct SmemPairSrc {  // stage 2: (key, index) pairs in shared memory, tie-break = index
+    const uint32_t* k;
+    const uint32_t* t;
+    __device__ __forceinline__ uint32_t key(int i) const { return k[i]; }
+    __device__ __forceinline__ uint32_t tb(int i) const { return t[i]; }
+};
+
+template <class Src>
+__device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, int tb_bits,
+                                  uint32_t* hist, uint32_t* sh) {
+    const int tid = threadIdx.x;
+    SelectOut r;
+    r.tie_cut = 0;
+    for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+        uint32_t k = src.key(i);
+        if (k) atomicAdd(&hist[logbin(kmax - k)], 1u);
+    }
+    __syncthreads();
+    if (tid < 32) warp_find(hist, kHistBins, (uint32_t)K, sh);
+    __syncthreads();
+    const uint32_t total = sh[2];
+    r.n_valid = total;
+    if (total <= (uint32_t)K) {
+        r.kth_key = 0u;
+        r.kth_tb = 0xFFFFFFFFu;
+        __syncthreads();
+        return r;
+    }
+    const int g0 = (int)sh[0];
+    uint32_t need = (uint32_t)K - sh[1];
+    uint32_t dlo;
+    int bits;
+    logbin_range(g0, &dlo, &bits);
+    uint32_t n_eq = hist[g0];
+    __syncthreads();
+    while (bits > 0) {
+        const int w = bits < 8 ? bits : 8;
+        const int shift = bits - w;
+        const uint32_t width = 1u << bits;
+        for (int i = tid; i < 256; i += NT) hist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < n; i += NT) {
+            uint32_t k = src.key(i);
+            if (k) {
+                uint32_t dd = (kmax - k) - dlo;
+                if (dd < width) atomicAdd(&hist[dd >> shift], 1u);
+            }
+        }
+        __syncthreads();
+        if (tid < 32) warp_find(hist, 1 << w, need, sh);
+        __syncthreads();
+        const int g = (int)sh[0];
+        const uint32_t before = sh[1];
+        n_eq = hist[g];
+        __syncthreads();
+        dlo += (uint32_t)g << shift;
+        need -= before;
+        bits = shift;
+    }
+    r.kth_key = kmax - dlo;
+    if (need == n_eq) {
+        r.kth_tb = 0xFFFFFFFFu;
+        return r;
+    }
+    r.tie_cut = 1;
+    // The `need` lowest tie-breaks among elements whose key equals kth_key.
+    uint32_t tlo = 0u;
+    int tbits = tb_bits;
+    while (tbits > 0) {
+        const int w = tbits < 8 ? tbits : 8;
+        const int shift = tbits - w;
+        const uint32_t hi_mask = tbits >= 32 ? 0u : (0xFFFFFFFFu << tbits);
+        for (int i = tid; i < 256; i += NT) hist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < n; i += NT) {
+            if (src.key(i) == r.kth_key) {
+                uint32_t t = src.tb(i);
+                if (((t ^ tlo) & hi_mask) == 0u) atomicAdd(&hist[(t >> shift) & ((1u << w) - 1u)], 1u);
+            }
+        }
+        __syncthreads();
+        if (tid < 32) warp_find(hist, 1 << w, need, sh);
+        __syncthreads();
+        const int g = (int)sh[0];
+        const uint32_t before = sh[1];
+        __syncthreads();
+        tlo |= (uint32_t)g << shift;
+        need -= before;
+        tbits = shift;
+    }
+    r.kth_tb = tlo;
+    return r;
+}
+
+__device__ __forceinline__ bool selected(uint32_t k, uint32_t t, const SelectOut& s) {
+    return k != 0u && (k > s.kth_key || (k == s.kth_key && t <= s.kth_tb));
+}
+
+__device__ __forceinline__ int bits_for(uint32_t maxval) { return maxval == 0u ? 1 : 32 - __clz(maxval); }
+
+// Binary search in a sorted id list: index of the first element >= v.
+__device__ __forceinline__ int lower_bound_i32(const int32_t* a, int n, int64_t v) {
+    int lo = 0, hi = n;
+    while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if ((int64_t)a[mid] < v) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// ---------------------------------------------------------------------------------
+// Penalty prep (Sampler.pas:285-303): per row, the history ids that fall in
+// [vocab_offset, vocab_offset + V) are sorted, deduplicated, and each distinct id gets
+// f^n(x) where n is its multiplicity and f(x) = x>0 ? x/p : (x<0 ? x*p : x) in fp32.
+// ---------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(NT) penalty_prep_kernel(const T* logits, int64_t stride, int V,
+                                                          int64_t lo, const int32_t* hist,
+                                                          int64_t hist_stride,
+                                                          const int32_t* hist_count, float penalty,
+                                                          int32_t* pen_ids, float* pen_vals,
+                                                          int32_t* pen_cnt, int pen_stride) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    int32_t* a = (int32_t*)smem_raw;  // [P2]
+    __shared__ int sh[NWARPS + 1];
+    const int b = blockIdx.x, tid = threadIdx.x;
+    int cnt = hist_count[b];
+    cnt = cnt < 0 ? 0 : cnt;
+    if (cnt > pen_stride) cnt = pen_stride;
+    int P2 = 1;
+    while (P2 < cnt) P2 <<= 1;
+    const int32_t* h = hist + (int64_t)b * hist_stride;
+    for (int i = tid; i < P2; i += NT) {
+        int32_t v = INT_MAX;
+        if (i < cnt) {
+            int64_t local = (int64_t)h[i] - lo;
+            if (local >= 0 && local < V) v = (int32_t)local;
+        }
+        a[i] = v;
+    }
+    __syncthreads();
+    for (int k = 2; k <= P2; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < P2; i += NT) {
+                int ixj = i ^ j;
+                if (ixj > i) {
+                    int32_t x = a[i], y = a[ixj];
+                    bool asc = (i & k) == 0;
+                    if (asc ? (x > y) : (x < y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    // Each thread owns a contiguous segment so the output keeps ascending id order.
+    const int seg = (P2 + NT - 1) / NT;
+    const int s0 = min(tid * seg, P2), s1 = min(s0 + seg, P2);
+    int firsts = 0;
+    for (int i = s0; i < s1; ++i)
+        if (a[i] != INT_MAX && (i == 0 || a[i - 1] != a[i])) ++firsts;
+    int total;
+    int off = block_excl_scan(firsts, sh, &total);
+    const T* row = logits + (int64_t)b * stride;
+    const float p = penalty;
+    for (int i = s0; i < s1; ++i) {
+        int32_t id = a[i];
+        if (id == INT_MAX || (i > 0 && a[i - 1] == id)) continue;
+        int n = 1;
+        while (i + n < P2 && a[i + n] == id) ++n;
+        float v = ld_elem(row, id);
+        for (int r = 0; r < n; ++r) {
+            if (v > 0.0f) v = __fdiv_rn(v, p);
+            else if (v < 0.0f) v = __fmul_rn(v, p);
+        }
+        pen_ids[(int64_t)b * pen_stride + off] = id;
+        pen_vals[(int64_t)b * pen_stride + off] = v;
+        ++off;
+    }
+    if (tid == 0) pen_cnt[b] = total;
+}
+
+// ---------------------------------------------------------------------------------
+// Stage 2, canonical: survivors sk/si (nsel of them, nsel <= K <= 1024) -> exp,
+// min-p, sort by (prob desc, index asc), top-p, draw. Returns true when the row has to
+// be re-resolved by the faithful emulation (token not written in that case).
+// `work` must hold 24 * 1024 + 8 bytes.
+// ---------------------------------------------------------------------------------
+__device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, const uint32_t* si,
+                                 int nsel, uint32_t kmax, uint32_t flags_in, unsigned char* work,
+                                 uint32_t* shu, uint32_t* flags_out) {
+    __shared__ double s_dsh[NWARPS];
+    __shared__ double s_d[4];
+    __shared__ int s_i[4];
+    const int tid = threadIdx.x;
+    int P2 = 32;
+    while (P2 < nsel) P2 <<= 1;
+    uint64_t* sortb = (uint64_t*)work;
+    float* q = (float*)(sortb + P2);
+    int32_t* qid = (int32_t*)(q + P2);
+    double* pre = (double*)(qid + P2);  // [P2 + 1]
+
+    const float M = key2f(kmax);
+    const double Md = (double)M, it = (double)p.inv_temp;
+    for (int s = tid; s < P2; s += NT) q[s] = s < nsel ? (float)exp(((double)key2f(sk[s]) - Md) * it) : 0.0f;
+    __syncthreads();
+    if (p.min_p > 0.0f) {
+        uint32_t mk = 0u;
+        for (int s = tid; s < nsel; s += NT) mk = max(mk, f2key(q[s]));
+        mk = block_max_u32(mk, shu);
+        const float thr = __fmul_rn(key2f(mk), p.min_p);
+        for (int s = tid; s < nsel; s += NT)
+            if (q[s] < thr) q[s] = 0.0f;
+        __syncthreads();
+    }
+    for (int s = tid; s < P2; s += NT)
+        sortb[s] = s < nsel ? (((uint64_t)__float_as_uint(q[s]) << 32) | (uint64_t)(~si[s])) : 0ull;
+    __syncthreads();
+    bitonic_sort_desc(sortb, P2);
+    uint32_t cnt = 0u, emin = 0xFFFFFFFFu;
+    for (int s = tid; s < P2; s += NT) {
+        float v = s < nsel ? __uint_as_float((uint32_t)(sortb[s] >> 32)) : 0.0f;
+        q[s] = v;
+        qid[s] = s < nsel ? (int32_t)(~(uint32_t)sortb[s]) : -1;
+        if (v > 0.0f) {
+            ++cnt;
+            int e = ilogbf(v);
+            e = e < -126 ? -126 : e;
+            emin = min(emin, (uint32_t)(e + 1024));
+        }
+    }
+    cnt = block_sum_u32(cnt, shu);
+    emin = block_min_u32(emin, shu);
+    bool exact = true;
+    if (cnt > 0u) {
+        int E = ilogb((double)cnt * (double)q[0]);
+        exact = (int)emin - 1024 >= E - 29;
+    }
+    const float u = p.uniform ? p.uniform[b] : 0.0f;
+    // Each thread owns two consecutive walk positions (P2 <= 1024 = 2 * NT).
+    const int i0 = 2 * tid;
+    if (exact) {
+        double a0 = i0 < P2 ? (double)q[i0] : 0.0, a1 = i0 + 1 < P2 ? (double)q[i0 + 1] : 0.0;
+        double tot;
+        double off = block_excl_scan_d(a0 + a1, s_dsh, &tot);
+        if (i0 < P2) pre[i0] = off;
+        if (i0 + 1 < P2) pre[i0 + 1] = off + a0;
+        if (tid == 0) pre[P2] = tot;
+        __syncthreads();
+        double lsum = tot;
+        int m = nsel;
+        if (p.top_p < 1.0f) {
+            const double target = (double)p.top_p * tot;
+            uint32_t mm = (uint32_t)nsel;
+            for (int i = i0; i < i0 + 2 && i < nsel; ++i)
+                if (!(pre[i] < target && q[i] > 0.0f)) mm = min(mm, (uint32_t)i);
+            m = (int)block_min_u32(mm, shu);
+            lsum = pre[m];
+        }
+        const double t = (double)u * lsum;
+        uint32_t jj = 0xFFFFFFFFu;
+        for (int i = i0; i < i0 + 2 && i < m; ++i)
+            if (pre[i] + (double)q[i] > t) jj = min(jj, (uint32_t)i);
+        jj = block_min_u32(jj, shu);
+        if (tid == 0) {
+            s_i[0] = (int)jj;
+            s_d[0] = t;
+            s_d[1] = lsum;
+            s_d[2] = jj != 0xFFFFFFFFu ? pre[jj] : 0.0;
+        }
+    } else if (tid == 0) {
+        // Sequential walk, exactly the reference's arithmetic on the canonical order.
+        double lsum = 0.0;
+        for (int i = 0; i < nsel; ++i) lsum += q[i];
+        int m = nsel;
+        if (p.top_p < 1.0f) {
+            const double target = (double)p.top_p * lsum;
+            double cum = 0.0;
+            lsum = 0.0;
+            m = 0;
+            for (int i = 0; i < nsel; ++i) {
+                if (cum < target && q[i] > 0.0f) {
+                    cum += q[i];
+                    lsum += q[i];
+                    m = i + 1;
+                } else break;
+            }
+        }
+        const double t = (double)u * lsum;
+        double cum = 0.0, before = 0.0;
+        int j = -1;
+        for (int i = 0; i < m; ++i) {
+            before = cum;
+            cum += q[i];
+            if (cum > t) {
+                j = i;
+                break;
+            }
+        }
+        s_i[0] = j;
+        s_d[0] = t;
+        s_d[1] = lsum;
+        s_d[2] = before;
+    }
+    __syncthreads();
+    int j = s_i[0];
+    const bool fallback = j < 0 || j >= nsel;
+    if (fallback) j = nsel - 1;
+    uint32_t f = flags_in | VDXS_FLAG_TOPK;
+    if (!exact) f |= VDXS_FLAG_INEXACT_SUM;
+    if (!(p.top_p < 1.0f) && p.K > 1) f |= VDXS_FLAG_SLOT_ORDER;
+    if (fallback) f |= VDXS_FLAG_FALLBACK;
+    if (nsel > 1 && ((j > 0 && q[j - 1] == q[j]) || (j + 1 < nsel && q[j + 1] == q[j])))
+        f |= VDXS_FLAG_DRAW_TIE_RUN;
+    {
+        const double t = s_d[0], lsum = s_d[1], before = s_d[2];
+        const double after = before + (double)q[j];
+        const double eps = 1e-6 * lsum;
+        if (fallback || (t - before) <= eps || (after - t) <= eps) f |= VDXS_FLAG_NEAR_BOUNDARY;
+    }
+    *flags_out = f;
+    const bool need_faithful = p.tie_mode == VDXS_TIES_FAITHFUL && p.K > 1 &&
+                               (f & (VDXS_FLAG_DRAW_TIE_RUN | VDXS_FLAG_INEXACT_SUM | VDXS_FLAG_SLOT_ORDER));
+    if (!need_faithful) {
+        if (tid == 0) {
+            p.tokens[b] = qid[j];
+            if (p.flags) p.flags[b] = f;
+        }
+        if (p.out_k > 0) {
+            for (int s = tid; s < p.out_k; s += NT) {
+                if (p.out_idx) p.out_idx[(int64_t)b * p.out_k + s] = s < nsel ? qid[s] : -1;
+                if (p.out_prob) p.out_prob[(int64_t)b * p.out_k + s] = s < nsel ? q[s] : 0.0f;
+            }
+        }
+    }
+    __syncthreads();
+    return need_faithful;
+}
+
+// ---------------------------------------------------------------------------------
+// Faithful emulation of the reference min-buffer (Sampler.pas:341-383) over one row,
+// followed by the reference's sequential double arithmetic (Sampler.pas:385-459).
+// Tiles of the row are staged in shared memory; all threads pre-filter each tile
+// against the current buffer minimum (it only grows, so nothing that the reference
+// would insert is filtered out) and warp 0 replays the candidates in index order.
+// `work` must hold 8*K + 6*kFaithfulTile + 24*1024 + 64 bytes.
+// ---------------------------------------------------------------------------------
+template <typename T>
+__device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigned char* work,
+                             uint32_t* shu) {
+    __shared__ float s_mv;
+    __shared__ int s_isum[NWARPS + 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K, V = p.V;
+    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+    float* sval = (float*)work;
+    int32_t* sidx = (int32_t*)(sval + K);
+    float* tile = (float*)(sidx + K);
+    uint16_t* cpos = (uint16_t*)(tile + kFaithfulTile);
+    unsigned char* tail = (unsigned char*)(cpos + kFaithfulTile);
+    tail = (unsigned char*)(((uintptr_t)tail + 15) & ~(uintptr_t)15);
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+    const float* pvl = p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr;
+    constexpr int R = kFaithfulTile / NT;
+
+    // Warp-0 state: per-lane minimum over slots {lane, lane+32, ...} and the global one.
+    float mv = -INFINITY;
+    int ms = 0;
+    if (tid == 0) s_mv = -INFINITY;
+    __syncthreads();
+    for (int64_t base = 0; base < V; base += kFaithfulTile) {
+        const int n = (int)min((int64_t)kFaithfulTile, (int64_t)V - base);
+        for (int i = tid; i < n; i += NT) tile[i] = ld_elem(row, base + i);
+        __syncthreads();
+        if (npen) {
+            const int j0 = lower_bound_i32(pid, npen, base);
+            for (int j = j0 + tid; j < npen && pid[j] < base + n; j += NT) tile[pid[j] - base] = pvl[j];
+            __syncthreads();
+        }
+        const float tau = s_mv;
+        int cnt = 0;
+        for (int r = 0; r < R; ++r) {
+            const int i = tid * R + r;
+            if (i < n && (base + i < K || tile[i] > tau)) ++cnt;
+        }
+        int total;
+        int off = block_excl_scan(cnt, s_isum, &total);
+        for (int r = 0; r < R; ++r) {
+            const int i = tid * R + r;
+            if (i < n && (base + i < K || tile[i] > tau)) cpos[off++] = (uint16_t)i;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            for (int c0 = 0; c0 < total; c0 += 32) {
+                const int c = c0 + lane;
+                const bool valid = c < total;
+                float v = 0.0f;
+                int64_t gi = -1;
+                if (valid) {
+                    const int i = cpos[c];
+                    v = tile[i];
+                    gi = base + i;
+                }
+                unsigned pend = __ballot_sync(FULL, valid && (gi < K || v > mv));
+                while (pend) {
+                    const int l = __ffs(pend) - 1;
+                    const float vl = __shfl_sync(FULL, v, l);
+                    const int64_t gl = __shfl_sync(FULL, gi, l);
+                    bool changed = false;
+                    if (gl < K) {
+                        if (lane == 0) {
+                            sval[gl] = vl;
+                            sidx[gl] = (int32_t)gl;
+                        }
+                        changed = gl == K - 1;
+                    } else if (vl > mv) {
+                        if (lane == 0) {
+                            sval[ms] = vl;
+                            sidx[ms] = (int32_t)gl;
+                        }
+                        changed = true;
+                    }
+                    __syncwarp();
+                    if (changed) {
+                        // Recompute per-lane minima (first slot with strict '<' wins ties).
+                        float bv = 0.0f;
+                        int bs = INT_MAX;
+                        for (int s = lane; s < K; s += 32) {
+                            const float x = sval[s];
+                            if (bs == INT_MAX || x < bv) {
+                                bv = x;
+                                bs = s;
+                            }
+                        }
+                        const uint32_t kv = bs == INT_MAX ? 0xFFFFFFFFu : f2key(bv);
+                        const uint32_t mk = __reduce_min_sync(FULL, kv);
+                        const uint32_t cs = kv == mk ? (uint32_t)bs : 0xFFFFFFFFu;
+                        ms = (int)__reduce_min_sync(FULL, cs);
+                        mv = sval[ms];
+                    }
+                    pend &= ~(1u << l);
+                    pend &= __ballot_sync(FULL, valid && (gi < K || v > mv));
+                }
+            }
+            if (lane == 0) s_mv = mv;
+        }
+        __syncthreads();
+    }
+
+    // Sequential stage 2 in slot order (Sampler.pas:385-459).
+    int P2 = 32;
+    while (P2 < K) P2 <<= 1;
+    uint64_t* sortb = (uint64_t*)tail;
+    float* prob = (float*)(sortb + P2);
+    int32_t* wid = (int32_t*)(prob + P2);
+    uint32_t mk = 0u;
+    for (int s = tid; s < K; s += NT) mk = max(mk, f2key(sval[s]));
+    mk = block_max_u32(mk, shu);
+    const double Md = (double)key2f(mk), it = (double)p.inv_temp;
+    for (int s = tid; s < K; s += NT) prob[s] = (float)exp(((double)sval[s] - Md) * it);
+    __syncthreads();
+    __shared__ double s_lsum;
+    if (tid == 0) {
+        double lsum = 0.0;
+        for (int s = 0; s < K; ++s) lsum += prob[s];
+        if (p.min_p > 0.0f) {
+            float best = prob[0];
+            for (int s = 1; s < K; ++s)
+                if (prob[s] > best) best = prob[s];
+            const float thr = __fmul_rn(best, p.min_p);
+            lsum = 0.0;
+            for (int s = 0; s < K; ++s)
+                if (prob[s] < thr) prob[s] = 0.0f;
+                else lsum += prob[s];
+        }
+        s_lsum = lsum;
+    }
+    __syncthreads();
+    const bool sorted = p.top_p < 1.0f;
+    if (sorted) {
+        // Stable descending insertion sort == sort by (prob desc, slot asc).
+        for (int s = tid; s < P2; s += NT)
+            sortb[s] = s < K ? (((uint64_t)__float_as_uint(prob[s]) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)s)) : 0ull;
+        __syncthreads();
+        bitonic_sort_desc(sortb, P2);
+        for (int s = tid; s < K; s += NT) {
+            const uint32_t slot = 0xFFFFFFFFu - (uint32_t)sortb[s];
+            wid[s] = sidx[slot];
+        }
+        __syncthreads();
+        for (int s = tid; s < K; s += NT) prob[s] = __uint_as_float((uint32_t)(sortb[s] >> 32));
+    } else {
+        for (int s = tid; s < K; s += NT) wid[s] = sidx[s];
+    }
+    __syncthreads();
+    if (p.out_k > 0) {
+        for (int s = tid; s < p.out_k; s += NT) {
+            if (p.out_idx) p.out_idx[(int64_t)b * p.out_k + s] = s < K ? wid[s] : -1;
+            if (p.out_prob) p.out_prob[(int64_t)b * p.out_k + s] = s < K ? prob[s] : 0.0f;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double lsum = s_lsum;
+        int m = K;
+        if (sorted) {
+            const double target = (double)p.top_p * lsum;
+            double cum = 0.0;
+            lsum = 0.0;
+            m = 0;
+            for (int i = 0; i < K; ++i) {
+                if (cum < target && prob[i] > 0.0f) {
+                    cum += prob[i];
+                    lsum += prob[i];
+                    m = i + 1;
+                } else break;
+            }
+        }
+        const float u = p.uniform ? p.uniform[b] : 0.0f;
+        const double t = (double)u * lsum;
+        double cum = 0.0, before = 0.0;
+        int j = -1;
+        for (int i = 0; i < m; ++i) {
+            before = cum;
+            cum += prob[i];
+            if (cum > t) {
+                j = i;
+                break;
+            }
+        }
+        const bool fallback = j < 0;
+        if (fallback) j = K - 1;
+        uint32_t f = (flags_in & (VDXS_FLAG_BOUNDARY_TIE | VDXS_FLAG_INEXACT_SUM)) | VDXS_FLAG_TOPK |
+                     VDXS_FLAG_FAITHFUL_PASS;
+        if (!sorted && K > 1) f |= VDXS_FLAG_SLOT_ORDER;
+        if (fallback) f |= VDXS_FLAG_FALLBACK;
+        if (sorted && K > 1 && ((j > 0 && prob[j - 1] == prob[j]) || (j + 1 < K && prob[j + 1] == prob[j])))
+            f |= VDXS_FLAG_DRAW_TIE_RUN;
+        const double after = before + (fallback ? 0.0 : (double)prob[j]);
+        const double eps = 1e-6 * lsum;
+        if (fallback || (t - before) <= eps || (after - t) <= eps) f |= VDXS_FLAG_NEAR_BOUNDARY;
+        p.tokens[b] = wid[j];
+        if (p.flags) p.flags[b] = f;
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------------
+// Stage 1 + stage 2 (top-k and greedy paths).
+// Shared memory: [hist 512 | scalars 64] then
+//   stage 1: keys[chunk] | bitmap[chunk/32]
+//   stage 2: sk[K] | si[K] | ckey[n2] | cidx[n2]   (math work aliases ckey)
+//   faithful: its own layout from the same base.
+// ---------------------------------------------------------------------------------
+template <typename T, bool VEC>
+__global__ void __launch_bounds__(NT) topk_fused_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    const int tid = threadIdx.x;
+    const int c = blockIdx.x, b = blockIdx.y;
+    const int K = p.K;
+    const int64_t start = (int64_t)c * p.chunk;
+    const int n = (int)min((int64_t)p.chunk, (int64_t)p.V - start);
+    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+    uint32_t* keys = (uint32_t*)region;
+    uint32_t* bitmap = keys + p.chunk;
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+
+    // History entries are excluded here and re-enter stage 2 with penalised values.
+    if (npen > 0) {
+        for (int i = tid; i < (p.chunk >> 5); i += NT) bitmap[i] = 0u;
+        __syncthreads();
+        const int j0 = lower_bound_i32(pid, npen, start);
+        for (int j = j0 + tid; j < npen && pid[j] < start + n; j += NT) {
+            const int e = pid[j] - (int)start;
+            atomicOr(&bitmap[e >> 5], 1u << (e & 31));
+        }
+        __syncthreads();
+    }
+
+    uint32_t lmax = 0u;
+    if (VEC) {
+        constexpr int VN = VecTraits<T>::N;
+        constexpr int U = 8;
+        const int nvec = n / VN;
+        const char* base = (const char*)(row + start);
+        for (int v0 = tid; v0 < nvec; v0 += NT * U) {
+            uint4 r[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + u * NT;
+                if (v < nvec) r[u] = ld_stream16(base + (size_t)v * 16);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int v = v0 + u * NT;
+                if (v < nvec) {
+                    float x[VN];
+                    unpack(r[u], x, T());
+                    uint32_t kk[VN];
+                    uint32_t excl = 0u;
+                    if (npen > 0) excl = (bitmap[(v * VN) >> 5] >> ((v * VN) & 31)) & ((1u << VN) - 1u);
+#pragma unroll
+                    for (int e = 0; e < VN; ++e) {
+                        kk[e] = ((excl >> e) & 1u) ? 0u : f2key(x[e]);
+                        lmax = max(lmax, kk[e]);
+                    }
+                    uint4* dst = (uint4*)(keys + v * VN);
+                    dst[0] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
+                    if constexpr (VN == 8) dst[1] = make_uint4(kk[4], kk[5], kk[6], kk[7]);
+                }
+            }
+        }
+        for (int i = nvec * VN + tid; i < n; i += NT) {
+            const bool ex = npen > 0 && ((bitmap[i >> 5] >> (i & 31)) & 1u);
+            const uint32_t k = ex ? 0u : f2key(ld_elem(row, start + i));
+            keys[i] = k;
+            lmax = max(lmax, k);
+        }
+    } else {
+        for (int i = tid; i < n; i += NT) {
+            const bool ex = npen > 0 && ((bitmap[i >> 5] >> (i & 31)) & 1u);
+            const uint32_t k = ex ? 0u : f2key(ld_elem(row, start + i));
+            keys[i] = k;
+            lmax = max(lmax, k);
+        }
+    }
+    const uint32_t kmax = block_max_u32(lmax, sh + 32);
+
+    SelectOut so = block_select(SmemKeySrc{keys}, n, K, kmax, bits_for((uint32_t)(n - 1)), hist, sh);
+    uint2* out = p.cand + ((int64_t)b * p.nchunks + c) * K;
+    if (tid == 0) sh[8] = 0u;
+    __syncthreads();
+    {
+        const int rounds = (n + NT - 1) / NT;
+        const uint32_t gbase = (uint32_t)(start + p.vocab_offset);
+        for (int j = 0; j < rounds; ++j) {
+            const int i = j * NT + tid;
+            uint32_t k = 0u;
+            bool s = false;
+            if (i < n) {
+                k = keys[i];
+                s = selected(k, (uint32_t)i, so);
+            }
+            const unsigned m = __ballot_sync(FULL, s);
+            if (m) {
+                uint32_t base = 0u;
+                if ((tid & 31) == 0) base = atomicAdd(&sh[8], (uint32_t)__popc(m));
+                base = __shfl_sync(FULL, base, 0);
+                if (s) {
+                    const uint32_t slot = base + __popc(m & lanemask_lt());
+                    if (slot < (uint32_t)K) out[slot] = make_uint2(k, gbase + (uint32_t)i);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t emitted = sh[8];
+    if (emitted > (uint32_t)K && tid == 0) atomicExch(p.err, kErrSelect);
+    for (int s = (int)emitted + tid; s < K; s += NT) out[s] = make_uint2(0u, 0xFFFFFFFFu);
+    if (tid == 0) p.chunk_info[(int64_t)b * p.nchunks + c] = make_uint2(so.kth_key, (uint32_t)so.tie_cut);
+
+    // Completion: the last CTA of the row runs stage 2.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(&p.row_counter[b], 1u);
+        sh[9] = prev == (uint32_t)(p.nchunks - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (sh[9] == 0u) return;
+    __threadfence();
+
+    // ---- stage 2: merge chunk candidates and penalised history entries ----
+    uint32_t* sk = (uint32_t*)region;
+    uint32_t* si = sk + K;
+    uint32_t* ckey = si + K;
+    const int nc = p.nchunks * K;
+    const int n2 = nc + npen;
+    uint32_t* cidx = ckey + n2;
+    const uint2* cb = p.cand + (int64_t)b * p.nchunks * K;
+    uint32_t lm = 0u, mi = 0u;
+    for (int i = tid; i < nc; i += NT) {
+        const uint2 e = __ldcg(cb + i);
+        ckey[i] = e.x;
+        cidx[i] = e.y;
+        lm = max(lm, e.x);
+        if (e.x) mi = max(mi, e.y);
+    }
+    for (int j = tid; j < npen; j += NT) {
+        const uint32_t k = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
+        ckey[nc + j] = k;
+        cidx[nc + j] = (uint32_t)(pid[j] + p.vocab_offset);
+        lm = max(lm, k);
+        mi = max(mi, cidx[nc + j]);
+    }
+    // Boundary-tie evidence from chunks that cut elements equal to their k-th key.
+    uint32_t ck_tie_keys = 0u;
+    const uint32_t gmax = block_max_u32(lm, sh + 32);
+    const uint32_t imax = block_max_u32(mi, sh + 32);
+    SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, bits_for(imax), hist, sh);
+    for (int i = tid; i < p.nchunks; i += NT) {
+        const uint2 ci = __ldcg(p.chunk_info + (int64_t)b * p.nchunks + i);
+        if (ci.y && ci.x == s2.kth_key) ck_tie_keys = 1u;
+    }
+    ck_tie_keys = block_max_u32(ck_tie_keys, sh + 32);
+    if (tid == 0) sh[8] = 0u;
+    __syncthreads();
+    {
+        const int rounds = (n2 + NT - 1) / NT;
+        for (int j = 0; j < rounds; ++j) {
+            const int i = j * NT + tid;
+            uint32_t k = 0u, t = 0u;
+            bool s = false;
+            if (i < n2) {
+                k = ckey[i];
+                t = cidx[i];
+                s = selected(k, t, s2);
+            }
+            const unsigned m = __ballot_sync(FULL, s);
+            if (m) {
+                uint32_t base = 0u;
+                if ((tid & 31) == 0) base = atomicAdd(&sh[8], (uint32_t)__popc(m));
+                base = __shfl_sync(FULL, base, 0);
+                if (s) {
+                    const uint32_t slot = base + __popc(m & lanemask_lt());
+                    if (slot < (uint32_t)K) {
+                        sk[slot] = k;
+                        si[slot] = t;
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int nsel = (int)min(sh[8], (uint32_t)K);
+    const uint32_t btie = (s2.tie_cut || ck_tie_keys) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
+    if (tid == 0) p.row_counter[b] = 0u;  // ready for the next launch
+
+    if (p.local_emit) {
+        // Vocab-sharded: publish the local top-K and tie evidence for the all-gather.
+        uint2* eo = p.emit_out + (int64_t)b * (K + 1);
+        for (int s = tid; s < K; s += NT) eo[s] = s < nsel ? make_uint2(sk[s], si[s]) : make_uint2(0u, 0xFFFFFFFFu);
+        if (tid == 0) eo[K] = make_uint2(s2.kth_key, (s2.tie_cut || ck_tie_keys) ? 1u : 0u);
+        return;
+    }
+    if (p.path == kGreedy) {
+        // Greedy (Sampler.pas:305-322): the canonical top-1 is the first maximum.
+        if (tid == 0) {
+            p.tokens[b] = (int32_t)si[0];
+            if (p.flags) p.flags[b] = VDXS_FLAG_GREEDY;
+        }
+        for (int s = tid; s < p.out_k; s += NT) {
+            if (p.out_idx) p.out_idx[(int64_t)b * p.out_k + s] = s == 0 ? (int32_t)si[0] : -1;
+            if (p.out_prob) p.out_prob[(int64_t)b * p.out_k + s] = 0.0f;
+        }
+        return;
+    }
+    unsigned char* work = (unsigned char*)(ckey);
+    work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
+    uint32_t f2;
+    const bool faithful = stage2_canonical(p, b, sk, si, nsel, gmax, btie, work, sh + 32, &f2);
+    if (faithful) faithful_row<T>(p, b, f2, region, sh + 32);
+}
+
+// ---------------------------------------------------------------------------------
+// Vocab-sharded merge and draw: candidates [ranks][B][K+1] from the all-gather.
+// ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT) merge_draw_kernel(KParams p, const uint2* recv, int ranks) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    const int tid = threadIdx.x, b = blockIdx.x, K = p.K;
+    uint32_t* sk = (uint32_t*)region;
+    uint32_t* si = sk + K;
+    uint32_t* ckey = si + K;
+    const int n2 = ranks * K;
+    uint32_t* cidx = ckey + n2;
+    uint32_t lm = 0u, mi = 0u;
+    for (int i = tid; i < n2; i += NT) {
+        const int r = i / K, s = i - r * K;
+        const uint2 e = recv[((int64_t)r * p.B + b) * (K + 1) + s];
+        ckey[i] = e.x;
+        cidx[i] = e.y;
+        lm = max(lm, e.x);
+        if (e.x) mi = max(mi, e.y);
+    }
+    const uint32_t gmax = block_max_u32(lm, sh + 32);
+    const uint32_t imax = block_max_u32(mi, sh + 32);
+    SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, bits_for(imax), hist, sh);
+    uint32_t rt = 0u;
+    for (int r = tid; r < ranks; r += NT) {
+        const uint2 info = recv[((int64_t)r * p.B + b) * (K + 1) + K];
+        if (info.y && info.x == s2.kth_key) rt = 1u;
+    }
+    rt = block_max_u32(rt, sh + 32);
+    if (tid == 0) sh[8] = 0u;
+    __syncthreads();
+    const int rounds = (n2 + NT - 1) / NT;
+    for (int j = 0; j < rounds; ++j) {
+        const int i = j * NT + tid;
+        uint32_t k = 0u, t = 0u;
+        bool s = false;
+        if (i < n2) {
+            k = ckey[i];
+            t = cidx[i];
+            s = selected(k, t, s2);
+        }
+        const unsigned m = __ballot_sync(FULL, s);
+        if (m) {
+            uint32_t base = 0u;
+            if ((tid & 31) == 0) base = atomicAdd(&sh[8], (uint32_t)__popc(m));
+            base = __shfl_sync(FULL, base, 0);
+            if (s) {
+                const uint32_t slot = base + __popc(m & lanemask_lt());
+                if (slot < (uint32_t)K) {
+                    sk[slot] = k;
+                    si[slot] = t;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int nsel = (int)min(sh[8], (uint32_t)K);
+    if (p.path == kGreedy) {
+        if (tid == 0) {
+            p.tokens[b] = (int32_t)si[0];
+            if (p.flags) p.flags[b] = VDXS_FLAG_GREEDY;
+        }
+        return;
+    }
+    const uint32_t btie = (s2.tie_cut || rt) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
+    unsigned char* work = (unsigned char*)(ckey);
+    work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
+    uint32_t f2;
+    stage2_canonical(p, b, sk, si, nsel, gmax, btie, work, sh + 32, &f2);
+}
+
+// ---------------------------------------------------------------------------------
+// Full-softmax path (Sampler.pas:461-527).
+// ---------------------------------------------------------------------------------
+struct PenLookup {
+    const uint32_t* bitmap;
+    const int32_t* ids;
+    const float* vals;
+    int n;
+    __device__ __forceinline__ float apply(int i, int64_t gi, float x) const {
+        if (n > 0 && ((bitmap[i >> 5] >> (i & 31)) & 1u)) {
+            const int j = lower_bound_i32(ids, n, gi);
+            return vals[j];
+        }
+        return x;
+    }
+};
+
+__device__ void build_chunk_bitmap(uint32_t* bitmap, int chunk, const int32_t* pid, int npen,
+                                   int64_t start, int n) {
+    for (int i = threadIdx.x; i < (chunk >> 5); i += NT) bitmap[i] = 0u;
+    __syncthreads();
+    const int j0 = lower_bound_i32(pid, npen, start);
+    for (int j = j0 + threadIdx.x; j < npen && pid[j] < start + n; j += NT) {
+        const int e = pid[j] - (int)start;
+        atomicOr(&bitmap[e >> 5], 1u << (e & 31));
+    }
+    __syncthreads();
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT) full_max_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* sh = (uint32_t*)smem_raw;
+    uint32_t* bitmap = sh + kShWords;
+    const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int64_t start = (int64_t)c * p.chunk;
+    const int n = (int)min((int64_t)p.chunk, (int64_t)p.V - start);
+    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    PenLookup pl{bitmap, p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr,
+                 p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr, npen};
+    if (npen > 0) build_chunk_bitmap(bitmap, p.chunk, pl.ids, npen, start, n);
+    uint32_t lm = 0u;
+    for (int i = tid; i < n; i += NT) {
+        const float x = pl.apply(i, start + i, ld_elem(row, start + i));
+        lm = max(lm, f2key(__fmul_rn(x, p.inv_temp)));
+    }
+    lm = block_max_u32(lm, sh);
+    if (tid == 0) p.fmax[(int64_t)b * p.nchunks + c] = lm;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(NT) full_sum_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* sh = (uint32_t*)smem_raw;
+    uint32_t* bitmap = sh + kShWords;
+    __shared__ double s_dsh[NWARPS];
+    __shared__ double s_d[8];
+    __shared__ int s_i[8];
+    const int c = blockIdx.x, b = blockIdx.y, tid = threadIdx.x;
+    const int64_t start = (int64_t)c * p.chunk;
+    const int n = (int)min((int64_t)p.chunk, (int64_t)p.V - start);
+    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    PenLookup pl{bitmap, p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr,
+                 p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr, npen};
+    if (npen > 0) build_chunk_bitmap(bitmap, p.chunk, pl.ids, npen, start, n);
+    uint32_t gm = 0u;
+    for (int i = tid; i < p.nchunks; i += NT) gm = max(gm, p.fmax[(int64_t)b * p.nchunks + i]);
+    gm = block_max_u32(gm, sh);
+    const float M = key2f(gm);
+    const double Md = (double)M;
+    const float best = (float)exp(Md - Md);  // the maximum element's probability
+    const bool use_min = p.min_p > 0.0f;
+    const float thr = __fmul_rn(best, p.min_p);
+    double s = 0.0;
+    uint32_t nz = 0u, emin = 0xFFFFFFFFu, pmax = 0u;
+    for (int i = tid; i < n; i += NT) {
+        const float x = pl.apply(i, start + i, ld_elem(row, start + i));
+        float e = (float)exp((double)__fmul_rn(x, p.inv_temp) - Md);
+        if (use_min && e < thr) e = 0.0f;
+        s += (double)e;
+        if (e > 0.0f) {
+            ++nz;
+            int ex = ilogbf(e);
+            ex = ex < -126 ? -126 : ex;
+            emin = min(emin, (uint32_t)(ex + 1024));
+            pmax = max(pmax, f2key(e));
+        }
+    }
+    double tot;
+    block_excl_scan_d(s, s_dsh, &tot);
+    nz = block_sum_u32(nz, sh);
+    emin = block_min_u32(emin, sh);
+    pmax = block_max_u32(pmax, sh);
+    if (tid == 0) {
+        p.fsum[(int64_t)b * p.nchunks + c] = tot;
+        p.fstat[(int64_t)b * p.nchunks + c] = make_uint2(nz, emin);
+        p.fmax[(int64_t)p.B * p.nchunks + (int64_t)b * p.nchunks + c] = pmax;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(&p.row_counter[b], 1u);
+        sh[9] = prev == (uint32_t)(p.nchunks - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (sh[9] == 0u) return;
+    __threadfence();
+    // Last CTA of the row: locate the chunk holding the draw, then the element.
+    if (tid == 0) {
+        double S = 0.0;
+        uint32_t nzt = 0u, em = 0xFFFFFFFFu, pm = 0u;
+        for (int i = 0; i < p.nchunks; ++i) {
+            S += __ldcg(p.fsum + (int64_t)b * p.nchunks + i);
+            const uint2 st = __ldcg(p.fstat + (int64_t)b * p.nchunks + i);
+            nzt += st.x;
+            em = min(em, st.y);
+            pm = max(pm, __ldcg(p.fmax + (int64_t)p.B * p.nchunks + (int64_t)b * p.nchunks + i));
+        }
+        const float u = p.uniform ? p.uniform[b] : 0.0f;
+        const double t = (double)u * S;
+        double acc = 0.0;
+        int cs = -1;
+        for (int i = 0; i < p.nchunks; ++i) {
+            const double cs_sum = __ldcg(p.fsum + (int64_t)b * p.nchunks + i);
+            if (acc + cs_sum > t) {
+                cs = i;
+                break;
+            }
+            acc += cs_sum;
+        }
+        bool exact = true;
+        if (nzt > 0u) {
+            const int E = ilogb((double)nzt * (double)key2f(pm));
+            exact = (int)em - 1024 >= E - 29;
+        }
+        s_i[0] = cs;
+        s_i[1] = exact ? 1 : 0;
+        s_d[0] = t;
+        s_d[1] = S;
+        s_d[2] = acc;
+    }
+    __syncthreads();
+    const int cs = s_i[0];
+    const double t = s_d[0], S = s_d[1];
+    uint32_t f = VDXS_FLAG_FULL | (s_i[1] ? 0u : VDXS_FLAG_INEXACT_SUM);
+    int tok = p.V - 1;
+    double before = 0.0, after = 0.0;
+    bool fallback = cs < 0;
+    if (!fallback) {
+        // Re-read the chunk with contiguous per-thread runs and scan in index order.
+        const int64_t cstart = (int64_t)cs * p.chunk;
+        const int cn = (int)min((int64_t)p.chunk, (int64_t)p.V - cstart);
+        if (npen > 0) build_chunk_bitmap(bitmap, p.chunk, pl.ids, npen, cstart, cn);
+        const int R = (p.chunk + NT - 1) / NT;
+        const int r0 = tid * R, r1 = min(r0 + R, cn);
+        double ls = 0.0;
+        for (int i = r0; i < r1; ++i) {
+            const float x = pl.apply(i, cstart + i, ld_elem(row, cstart + i));
+            float e = (float)exp((double)__fmul_rn(x, p.inv_temp) - Md);
+            if (use_min && e < thr) e = 0.0f;
+            ls += (double)e;
+        }
+        double tot2;
+        double off = block_excl_scan_d(ls, s_dsh, &tot2) + s_d[2];
+        uint32_t jj = 0xFFFFFFFFu;
+        double cum = off, bef = 0.0;
+        for (int i = r0; i < r1; ++i) {
+            const float x = pl.apply(i, cstart + i, ld_elem(row, cstart + i));
+            float e = (float)exp((double)__fmul_rn(x, p.inv_temp) - Md);
+            if (use_min && e < thr) e = 0.0f;
+            bef = cum;
+            cum += (double)e;
+            if (cum > t) {
+                jj = (uint32_t)i;
+                break;
+            }
+        }
+        const uint32_t jmin = block_min_u32(jj, sh);
+        if (jj == jmin && jj != 0xFFFFFFFFu) {
+            s_d[4] = bef;
+            s_d[5] = cum;
+            s_i[2] = (int)jj;
+        }
+        __syncthreads();
+        if (jmin == 0xFFFFFFFFu) {
+            fallback = true;
+        } else {
+            tok = (int)(cstart + s_i[2]);
+            before = s_d[4];
+            after = s_d[5];
+        }
+    }
+    if (tid == 0) {
+        if (fallback) f |= VDXS_FLAG_FALLBACK;
+        const double eps = 1e-6 * S;
+        if (fallback || (t - before) <= eps || (after - t) <= eps) f |= VDXS_FLAG_NEAR_BOUNDARY;
+        p.tokens[b] = tok;
+        if (p.flags) p.flags[b] = f;
+        p.row_counter[b] = 0u;
+    }
+    for (int s = tid; s < p.out_k; s += NT) {
+        if (p.out_idx) p.out_idx[(int64_t)b * p.out_k + s] = -1;
+        if (p.out_prob) p.out_prob[(int64_t)b * p.out_k + s] = 0.0f;
+    }
+}
+
+// ---------------------------------------------------------------------------------
+// Host side: plans, workspace, launches.
+// ---------------------------------------------------------------------------------
+static size_t align16(size_t x) { return (x + 15) & ~(size_t)15; }
+
+static int pow2_at_least(int n, int lo) {
+    int p = lo;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+static size_t stage2_bytes(int K, int n2) {
+    const int P2 = pow2_at_least(K, 32);
+    const size_t math = (size_t)24 * P2 + 8 + 16;
+    const size_t cands = (size_t)8 * n2;
+    return (size_t)8 * K + std::max(math, cands) + 16;
+}
+
+static size_t faithful_bytes(int K) {
+    const int P2 = pow2_at_least(K, 32);
+    return (size_t)8 * K + (size_t)6 * kFaithfulTile + 16 + (size_t)16 * P2 + 16;
+}
+
+cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std::string* err) {
+    const int K = a.K;
+    const int64_t V = a.V;
+    const int pen_stride = a.penalty_on ? (int)std::min<int64_t>(a.hist_stride, kMaxHistory) : 0;
+    int chunk = 16384;
+    // Aim for several CTAs per SM across the grid; small batches use smaller chunks.
+    const int64_t target = 148 * 4;
+    while (chunk > 2048 && (int64_t)a.B * ((V + chunk - 1) / chunk) < target) chunk >>= 1;
+    const int min_chunk = std::max(2048, pow2_at_least(4 * K, 32));
+    if (chunk < min_chunk) chunk = min_chunk;
+    if (V <= chunk) chunk = (int)((V + 31) / 32 * 32);
+    for (;;) {
+        const int nchunks = (int)((V + chunk - 1) / chunk);
+        const int n2 = nchunks * K + pen_stride;
+        const size_t s1 = (size_t)4 * chunk + (size_t)4 * (chunk / 32 + 1);
+        size_t need = std::max(s1, stage2_bytes(K, n2));
+        if (a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit)
+            need = std::max(need, faithful_bytes(K));
+        need += kHeadBytes;
+        if ((int64_t)need <= smem_optin) {
+            plan->chunk = chunk;
+            plan->nchunks = nchunks;
+            plan->smem = align16(need);
+            return cudaSuccess;
+        }
+        // Stage 2 too large: fewer, bigger chunks (until stage 1 itself is too large).
+        if (s1 + kHeadBytes > (size_t)smem_optin || nchunks == 1) break;
+        chunk <<= 1;
+    }
+    if (err) *err = "top_k too large for the shared-memory plan (top_k=" + std::to_string(K) + ")";
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t plan_full(const SampleArgs& a, LaunchPlan* plan, std::string*) {
+    int chunk = 16384;
+    const int64_t V = a.V;
+    while (chunk > 2048 && (int64_t)a.B * ((V + chunk - 1) / chunk) < 148 * 4) chunk >>= 1;
+    if (V <= chunk) chunk = (int)((V + 31) / 32 * 32);
+    plan->chunk = chunk;
+    plan->nchunks = (int)((V + chunk - 1) / chunk);
+    plan->smem = align16((size_t)4 * kShWords + (size_t)4 * (chunk / 32 + 1));
+    return cudaSuccess;
+}
+
+template <typename P>
+static cudaError_t grow(P** ptr, size_t* cap, size_t want, bool zero, cudaStream_t stream) {
+    if (*cap >= want && *ptr) return cudaSuccess;
+    if (*ptr) {
+        cudaError_t e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+        cudaFree(*ptr);
+        *ptr = nullptr;
+        *cap = 0;
+    }
+    size_t bytes = std::max<size_t>(want, 1) * sizeof(P);
+    cudaError_t e = cudaMalloc((void**)ptr, bytes);
+    if (e != cudaSuccess) {
+        *ptr = nullptr;
+        return e;
+    }
+    if (zero) {
+        e = cudaMemsetAsync(*ptr, 0, bytes, stream);
+        if (e != cudaSuccess) return e;
+    }
+    *cap = std::max<size_t>(want, 1);
+    return cudaSuccess;
+}
+
+cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPlan& plan, int ranks,
+                             cudaStream_t stream, std::string* err) {
+    cudaError_t e;
+    const size_t B = (size_t)a.B;
+    const size_t nch = (size_t)plan.nchunks;
+    if (!ws.err) {
+        if ((e = cudaMalloc((void**)&ws.err, sizeof(int32_t))) != cudaSuccess) return e;
+        if ((e = cudaMemsetAsync(ws.err, 0, sizeof(int32_t), stream)) != cudaSuccess) return e;
+    }
+    // Completion counters start at zero and every launch leaves them at zero.
+    if ((e = grow(&ws.row_counter, &ws.row_counter_cap, B, true, stream)) != cudaSuccess) return e;
+    if (a.path != kFull) {
+        if ((e = grow(&ws.cand, &ws.cand_cap, B * nch * (size_t)a.K, false, stream)) != cudaSuccess) return e;
+        if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, B * nch, false, stream)) != cudaSuccess) return e;
+    } else {
+        // fmax: [B*nch] max keys + [B*nch] probability max keys; fsum: [B*nch] sums + [B*nch] stats.
+        size_t cap_a = ws.full_cap, cap_b = ws.full_cap;
+        if ((e = grow(&ws.fmax, &cap_a, 2 * B * nch, false, stream)) != cudaSuccess) return e;
+        if ((e = grow(&ws.fsum, &cap_b, 2 * B * nch, false, stream)) != cudaSuccess) return e;
+        ws.full_cap = std::min(cap_a, cap_b);
+    }
+    if (a.penalty_on) {
+        const size_t ps = (size_t)std::min<int64_t>(a.hist_stride, kMaxHistory);
+        size_t cap_a = ws.pen_cap, cap_b = ws.pen_cap;
+        if ((e = grow(&ws.pen_ids, &cap_a, B * ps, false, stream)) != cudaSuccess) return e;
+        if ((e = grow(&ws.pen_vals, &cap_b, B * ps, false, stream)) != cudaSuccess) return e;
+        ws.pen_cap = std::min(cap_a, cap_b);
+        if ((e = grow(&ws.pen_cnt, &ws.pen_rows_cap, B, false, stream)) != cudaSuccess) return e;
+    }
+    if (a.local_emit) {
+        if ((e = grow(&ws.shard_send, &ws.shard_send_cap, B * (size_t)(a.K + 1), false, stream)) != cudaSuccess)
+            return e;
+        if ((e = grow(&ws.shard_recv, &ws.shard_recv_cap, (size_t)ranks * B * (size_t)(a.K + 1), false,
+                      stream)) != cudaSuccess)
+            return e;
+    }
+    (void)err;
+    return cudaSuccess;
+}
+
+void free_workspace(Workspace& ws) {
+    cudaFree(ws.cand);
+    cudaFree(ws.chunk_info);
+    cudaFree(ws.row_counter);
+    cudaFree(ws.pen_ids);
+    cudaFree(ws.pen_vals);
+    cudaFree(ws.pen_cnt);
+    cudaFree(ws.fmax);
+    cudaFree(ws.fsum);
+    cudaFree(ws.shard_send);
+    cudaFree(ws.shard_recv);
+    cudaFree(ws.err);
+    cudaFree(ws.d_logits);
+    cudaFree(ws.d_hist);
+    cudaFree(ws.d_hcnt);
+    cudaFree(ws.d_unif);
+    cudaFree(ws.d_tok);
+    if (ws.h_tok_pinned) cudaFreeHost(ws.h_tok_pinned);
+    ws = Workspace();
+}
+
+static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws) {
+    KParams p{};
+    p.logits = a.logits;
+    p.stride = a.stride;
+    p.V = a.V;
+    p.B = a.B;
+    p.chunk = plan.chunk;
+    p.nchunks = plan.nchunks;
+    p.K = a.K;
+    p.path = a.path;
+    if (a.penalty_on) {
+        p.pen_ids = ws.pen_ids;
+        p.pen_vals = ws.pen_vals;
+        p.pen_cnt = ws.pen_cnt;
+        p.pen_stride = (int)std::min<int64_t>(a.hist_stride, kMaxHistory);
+    }
+    p.cand = ws.cand;
+    p.chunk_info = ws.chunk_info;
+    p.row_counter = ws.row_counter;
+    p.err = ws.err;
+    p.fmax = ws.fmax;
+    p.fsum = ws.fsum;
+    p.fstat = (uint2*)(ws.fsum ? ws.fsum + (size_t)a.B * plan.nchunks : nullptr);
+    p.uniform = a.uniform;
+    p.tokens = a.tokens;
+    p.flags = a.flags;
+    p.out_idx = a.out_idx;
+    p.out_prob = a.out_prob;
+    p.out_k = a.out_k;
+    p.inv_temp = a.inv_temp;
+    p.min_p = a.min_p;
+    p.top_p = a.top_p;
+    p.tie_mode = a.tie_mode;
+    p.vocab_offset = a.vocab_offset;
+    p.local_emit = a.local_emit ? 1 : 0;
+    p.emit_out = ws.shard_send;
+    return p;
+}
+
+template <typename T>
+static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err) {
+    cudaError_t e;
+    KParams p = make_params(a, plan, ws);
+    if (a.penalty_on) {
+        const int ps = p.pen_stride;
+        const int P2 = pow2_at_least(std::max(ps, 1), 1);
+        const size_t sm = (size_t)4 * P2;
+        e = cudaFuncSetAttribute(penalty_prep_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (e != cudaSuccess) return e;
+        penalty_prep_kernel<T><<<a.B, NT, sm, a.stream>>>((const T*)a.logits, a.stride, a.V, a.vocab_offset, a.hist,
+                                                           a.hist_stride, a.hist_count, a.penalty, ws.pen_ids,
+                                                           ws.pen_vals, ws.pen_cnt, ps);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    }
+    (void)err;
+    const dim3 grid(plan.nchunks, a.B);
+    if (a.path == kFull) {
+        e = cudaFuncSetAttribute(full_max_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(full_sum_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
+        if (e != cudaSuccess) return e;
+        full_max_kernel<T><<<grid, NT, plan.smem, a.stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        full_sum_kernel<T><<<grid, NT, plan.smem, a.stream>>>(p);
+        return cudaGetLastError();
+    }
+    const size_t esz = sizeof(T);
+    const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0) &&
+                     (((size_t)plan.chunk * esz) % 16 == 0);
+    if (vec) {
+        e = cudaFuncSetAttribute(topk_fused_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)plan.smem);
+        if (e != cudaSuccess) return e;
+        topk_fused_kernel<T, true><<<grid, NT, plan.smem, a.stream>>>(p);
+    } else {
+        e = cudaFuncSetAttribute(topk_fused_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)plan.smem);
+        if (e != cudaSuccess) return e;
+        topk_fused_kernel<T, false><<<grid, NT, plan.smem, a.stream>>>(p);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err) {
+    if (a.dtype == VDXS_DTYPE_BF16) return launch_typed<uint16_t>(a, plan, ws, err);
+    return launch_typed<float>(a, plan, ws, err);
+}
+
+cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std::string* err) {
+    LaunchPlan plan{};
+    plan.nchunks = 1;
+    KParams p = make_params(a, plan, ws);
+    p.local_emit = 0;
+    p.tie_mode = VDXS_TIES_CANONICAL;
+    const int n2 = ranks * a.K;
+    const size_t sm = align16(kHeadBytes + stage2_bytes(a.K, n2));
+    cudaError_t e = cudaFuncSetAttribute(merge_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) {
+        if (err) *err = "merge kernel shared memory request rejected";
+        return e;
+    }
+    merge_draw_kernel<<<a.B, NT, sm, a.stream>>>(p, ws.shard_recv, ranks);
+    return cudaGetLastError();
+}
+
+}  // namespace vdxs

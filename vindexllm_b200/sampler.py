@@ -1,0 +1,249 @@
+"""Host-side mirror of VindexLLM's sampler interface over the C ABI.
+
+``TVdxSampler`` keeps the reference's method names and meaning (src/VindexLLM.Sampler.pas:
+DefaultConfig :100-109, SetConfig :132-150, GetConfig :152-155, Process :265-528,
+AddToHistory :530-539, ResetHistory :541-549) for a batch of rows, each with its own
+PRNG and history ring. ``SamplerContext.sample`` is the stateless batched call
+(vdxs_sample_ex). torch only supplies device memory and streams; all sampling runs in
+libvdxsampler.so, and a missing library raises instead of falling back.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import abi
+from ._lib import load, check, VdxsError
+from .abi import VdxsConfig, default_config
+
+__all__ = ["SamplerContext", "TVdxSampler", "ShardComm", "VdxsError", "default_config"]
+
+
+def _stream_ptr(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return C.c_void_p(int(stream.cuda_stream))
+
+
+def _dtype_code(t) -> int:
+    import torch
+    if t.dtype == torch.float32:
+        return abi.DTYPE_F32
+    if t.dtype == torch.bfloat16:
+        return abi.DTYPE_BF16
+    raise TypeError(f"logits must be float32 or bfloat16, got {t.dtype}")
+
+
+def _dptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+class SamplerContext:
+    """One vdxs_context: a device plus its lazily grown workspace."""
+
+    def __init__(self, device: int = 0, tie_mode: int = abi.TIES_FAITHFUL):
+        self.lib = load()
+        h = C.c_void_p()
+        check(self.lib.vdxs_create(device, C.byref(h)))
+        self._h = h
+        self.device = device
+        self.set_tie_mode(tie_mode)
+
+    @property
+    def handle(self):
+        return self._h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.vdxs_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_tie_mode(self, mode: int):
+        check(self.lib.vdxs_set_tie_mode(self._h, mode), self._h)
+
+    def sample(self, cfg: VdxsConfig, logits, uniforms=None, history=None, history_count=None,
+               vocab: int | None = None, out_k: int = 0, want_flags: bool = False, stream=None,
+               tokens=None):
+        """Stateless batched sampling on device tensors. Returns tokens, or
+        (tokens, flags, idx, prob) when diagnostics are requested."""
+        import torch
+        assert logits.is_cuda and logits.dim() == 2 and logits.stride(1) == 1
+        B, _ = logits.shape
+        V = logits.shape[1] if vocab is None else vocab
+        dev = logits.device
+        if tokens is None:
+            tokens = torch.empty(B, dtype=torch.int32, device=dev)
+        flags = torch.empty(B, dtype=torch.int32, device=dev) if (want_flags or out_k) else None
+        oi = torch.empty(B, out_k, dtype=torch.int32, device=dev) if out_k else None
+        op = torch.empty(B, out_k, dtype=torch.float32, device=dev) if out_k else None
+        hs = history.shape[1] if history is not None else 1
+        rc = self.lib.vdxs_sample_ex(self._h, C.byref(cfg), _dptr(logits), _dtype_code(logits), B, V,
+                                     logits.stride(0), _dptr(history), hs, _dptr(history_count),
+                                     _dptr(uniforms), _dptr(tokens), _dptr(flags), _dptr(oi), _dptr(op),
+                                     out_k, _stream_ptr(stream))
+        check(rc, self._h)
+        if flags is None:
+            return tokens
+        return tokens, flags, oi, op
+
+    def sample_host(self, cfg: VdxsConfig, logits: np.ndarray, uniforms=None, history=None,
+                    history_count=None, vocab: int | None = None, stream=None, out=None):
+        """Host-buffer call (vdxs_sample_host): numpy (or pinned torch CPU) inputs, host tokens."""
+        lg = logits
+        if hasattr(lg, "numpy"):
+            lg = lg.numpy()
+        if lg.dtype == np.float32:
+            dt = abi.DTYPE_F32
+        elif lg.dtype in (np.uint16, np.int16):
+            dt = abi.DTYPE_BF16
+        else:
+            raise TypeError("host logits must be float32 or bf16 bits (uint16)")
+        B, S = lg.shape
+        V = S if vocab is None else vocab
+        out = np.empty(B, np.int32) if out is None else out
+
+        def p(a):
+            if a is None:
+                return None
+            if hasattr(a, "numpy"):
+                a = a.numpy()
+            return C.c_void_p(a.ctypes.data)
+        hs = history.shape[1] if history is not None else 1
+        rc = self.lib.vdxs_sample_host(self._h, C.byref(cfg), p(lg), dt, B, V, S, p(history), hs,
+                                       p(history_count), p(uniforms), C.c_void_p(out.ctypes.data),
+                                       _stream_ptr(stream) if stream is not None else None)
+        check(rc, self._h)
+        return out
+
+
+class TVdxSampler:
+    """TVdxSampler (Sampler.pas:37-91) for ``batch`` independent rows."""
+
+    DefaultConfig = staticmethod(default_config)
+
+    def __init__(self, ctx: SamplerContext, batch: int = 1):
+        self.ctx = ctx
+        self.lib = ctx.lib
+        self.batch = batch
+        h = C.c_void_p()
+        check(self.lib.vdxs_sampler_create(ctx.handle, batch, C.byref(h)), ctx.handle)
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.vdxs_sampler_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def SetConfig(self, cfg: VdxsConfig):
+        check(self.lib.vdxs_sampler_set_config(self._h, C.byref(cfg)), self.ctx.handle)
+
+    def GetConfig(self) -> VdxsConfig:
+        c = VdxsConfig()
+        check(self.lib.vdxs_sampler_get_config(self._h, C.byref(c)), self.ctx.handle)
+        return c
+
+    def AddToHistory(self, token: int, row: int = 0):
+        check(self.lib.vdxs_sampler_add_to_history(self._h, row, int(token)), self.ctx.handle)
+
+    def AddToHistoryBatch(self, tokens):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(self.lib.vdxs_sampler_add_to_history_batch(self._h, C.c_void_p(t.ctypes.data)), self.ctx.handle)
+
+    def ResetHistory(self, row: int = -1):
+        check(self.lib.vdxs_sampler_reset_history(self._h, row), self.ctx.handle)
+
+    def Process(self, logits, vocab: int | None = None, stream=None):
+        """Process for every row. ``logits``: a CUDA tensor [batch, stride] (fp32/bf16), or a
+        host float32 array [batch, stride] (the reference's PSingle calling shape).
+        Returns an int32 numpy array of token ids (a Python int when batch == 1)."""
+        out = np.empty(self.batch, np.int32)
+        if isinstance(logits, np.ndarray):
+            assert logits.dtype == np.float32 and logits.ndim in (1, 2)
+            lg = np.ascontiguousarray(logits.reshape(self.batch, -1))
+            V = lg.shape[1] if vocab is None else vocab
+            check(self.lib.vdxs_sampler_process_host(self._h, C.c_void_p(lg.ctypes.data), V, lg.shape[1],
+                                                     C.c_void_p(out.ctypes.data)), self.ctx.handle)
+        else:
+            lg = logits.reshape(self.batch, -1) if logits.dim() == 1 else logits
+            V = lg.shape[1] if vocab is None else vocab
+            check(self.lib.vdxs_sampler_process(self._h, _dptr(lg), _dtype_code(lg), V, lg.stride(0),
+                                                C.c_void_p(out.ctypes.data), _stream_ptr(stream)),
+                  self.ctx.handle)
+        return int(out[0]) if self.batch == 1 else out
+
+    def NextFloat(self, row: int = 0) -> float:
+        f = C.c_float()
+        check(self.lib.vdxs_sampler_next_float(self._h, row, C.byref(f)), self.ctx.handle)
+        return f.value
+
+    def GetPrngState(self, row: int = 0):
+        st = (C.c_uint64 * 4)()
+        check(self.lib.vdxs_sampler_get_prng_state(self._h, row, st), self.ctx.handle)
+        return list(st)
+
+    def SetPrngState(self, state, row: int = 0):
+        check(self.lib.vdxs_sampler_set_prng_state(self._h, row, (C.c_uint64 * 4)(*state)), self.ctx.handle)
+
+    def GetHistory(self, row: int = 0):
+        cap = max(1, self.GetConfig().repeat_window)
+        buf = (C.c_int32 * cap)()
+        cnt, pos = C.c_int32(), C.c_int32()
+        check(self.lib.vdxs_sampler_get_history(self._h, row, buf, cap, C.byref(cnt), C.byref(pos)),
+              self.ctx.handle)
+        return list(buf[: cnt.value]), cnt.value, pos.value
+
+
+class ShardComm:
+    """An NCCL communicator owned by the library (vdxs_comm)."""
+
+    def __init__(self, ctx: SamplerContext, nranks: int, rank: int, unique_id: bytes):
+        self.ctx = ctx
+        self.lib = ctx.lib
+        assert len(unique_id) == 128
+        buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
+        h = C.c_void_p()
+        check(self.lib.vdxs_comm_create(ctx.handle, nranks, rank, buf, C.byref(h)), ctx.handle)
+        self._h = h
+        self.nranks = nranks
+        self.rank = rank
+
+    @staticmethod
+    def unique_id() -> bytes:
+        lib = load()
+        buf = (C.c_uint8 * 128)()
+        check(lib.vdxs_comm_unique_id(buf))
+        return bytes(buf)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.vdxs_comm_destroy(self._h)
+            self._h = None
+
+    def sample(self, cfg: VdxsConfig, logits_shard, vocab_offset: int, vocab_total: int, uniforms=None,
+               history=None, history_count=None, want_flags: bool = False, stream=None, tokens=None):
+        import torch
+        B, V = logits_shard.shape
+        if tokens is None:
+            tokens = torch.empty(B, dtype=torch.int32, device=logits_shard.device)
+        flags = torch.empty(B, dtype=torch.int32, device=logits_shard.device) if want_flags else None
+        hs = history.shape[1] if history is not None else 1
+        rc = self.lib.vdxs_sample_sharded(self.ctx.handle, self._h, C.byref(cfg), _dptr(logits_shard),
+                                          _dtype_code(logits_shard), B, V, logits_shard.stride(0),
+                                          vocab_offset, vocab_total, _dptr(history), hs, _dptr(history_count),
+                                          _dptr(uniforms), _dptr(tokens), _dptr(flags), _stream_ptr(stream))
+        check(rc, self.ctx.handle)
+        return (tokens, flags) if want_flags else tokens
