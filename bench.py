@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--profile", action="store_true", help="only warmup + timed steps (for ncu launch lists)")
+    ap.add_argument("--batch", type=int, default=None, help="override the config's batch (profiling only)")
+    ap.add_argument("--no-flush", action="store_true", help="skip the L2 flush between steps (profiling only)")
     return ap.parse_args()
 
 
@@ -156,18 +158,20 @@ def run_ours(args, rank, world, local):
     spec = synth.CONFIGS[name]
     if world > 1 and name not in ("c4", "c1", "c2"):
         raise SystemExit("sharded benchmark runs c4 (or c1/c2)")
+    if args.batch:
+        spec = dict(spec, batch=args.batch)
     B, V = spec["batch"], synth.VOCAB
     cfg = synth.sampler_config(name)
     mode = abi.TIES_FAITHFUL if args.tie_mode == "faithful" else abi.TIES_CANONICAL
     ctx = SamplerContext(local, tie_mode=mode if world == 1 else abi.TIES_CANONICAL)
     shard = V // world
     off = rank * shard
-    x_full = synth.make_logits(name, step=0, device=str(dev))
+    x_full = synth.make_logits(name, step=0, batch=B, device=str(dev))
     x = x_full[:, off:off + shard].contiguous() if world > 1 else x_full
     if world > 1:
         del x_full
     esz = x.element_size()
-    hist, hcnt = synth.make_history(name, step=0, device=str(dev))
+    hist, hcnt = synth.make_history(name, step=0, batch=B, device=str(dev))
     nsteps = args.warmup + args.steps
     u_all = torch.as_tensor(synth.make_uniforms(name, nsteps, batch=B), device=dev)
     tok = torch.empty(B, dtype=torch.int32, device=dev)
@@ -183,7 +187,7 @@ def run_ours(args, rank, world, local):
         else:
             ctx.sample(cfg, x, u_all[i], hist, hcnt, tokens=tok)
 
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.empty(16 if args.no_flush else 256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     for i in range(args.warmup):
         step(i)

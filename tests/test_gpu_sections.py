@@ -12,6 +12,13 @@ pytestmark = pytest.mark.gpu
 V = 10
 
 
+@pytest.fixture(autouse=True)
+def faithful_mode(gpu_ctx):
+    """TVdxSampler semantics: the context must be in FAITHFUL mode (the default)."""
+    from vindexllm_b200 import abi
+    gpu_ctx.set_tie_mode(abi.TIES_FAITHFUL)
+
+
 def dev(a):
     import torch
     return torch.as_tensor(np.asarray(a, np.float32), device="cuda")[None, :]

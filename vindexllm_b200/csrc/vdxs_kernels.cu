@@ -496,8 +496,8 @@ __global__ void __launch_bounds__(NT) penalty_prep_kernel(const T* logits, int64
 // `work` must hold 24 * 1024 + 8 bytes.
 // ---------------------------------------------------------------------------------
 __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, const uint32_t* si,
-                                 int nsel, uint32_t kmax, uint32_t flags_in, unsigned char* work,
-                                 uint32_t* shu, uint32_t* flags_out) {
+                                 int nsel, uint32_t kmax, uint32_t kth_key, uint32_t flags_in,
+                                 unsigned char* work, uint32_t* shu, uint32_t* flags_out) {
     __shared__ double s_dsh[NWARPS];
     __shared__ double s_d[4];
     __shared__ int s_i[4];
@@ -513,6 +513,9 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
     const double Md = (double)M, it = (double)p.inv_temp;
     for (int s = tid; s < P2; s += NT) q[s] = s < nsel ? (float)exp(((double)key2f(sk[s]) - Md) * it) : 0.0f;
     __syncthreads();
+    // Probability of the boundary value (the k-th largest); when more elements share it
+    // than fit, the reference's survivor among them depends on its slot history.
+    float qb = kth_key ? (float)exp(((double)key2f(kth_key) - Md) * it) : -1.0f;
     if (p.min_p > 0.0f) {
         uint32_t mk = 0u;
         for (int s = tid; s < nsel; s += NT) mk = max(mk, f2key(q[s]));
@@ -520,6 +523,7 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
         const float thr = __fmul_rn(key2f(mk), p.min_p);
         for (int s = tid; s < nsel; s += NT)
             if (q[s] < thr) q[s] = 0.0f;
+        if (qb >= 0.0f && qb < thr) qb = 0.0f;
         __syncthreads();
     }
     for (int s = tid; s < P2; s += NT)
@@ -628,8 +632,10 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
         if (fallback || (t - before) <= eps || (after - t) <= eps) f |= VDXS_FLAG_NEAR_BOUNDARY;
     }
     *flags_out = f;
+    const bool boundary_draw = (f & VDXS_FLAG_BOUNDARY_TIE) && q[j] == qb;
     const bool need_faithful = p.tie_mode == VDXS_TIES_FAITHFUL && p.K > 1 &&
-                               (f & (VDXS_FLAG_DRAW_TIE_RUN | VDXS_FLAG_INEXACT_SUM | VDXS_FLAG_SLOT_ORDER));
+                               (boundary_draw ||
+                                (f & (VDXS_FLAG_DRAW_TIE_RUN | VDXS_FLAG_INEXACT_SUM | VDXS_FLAG_SLOT_ORDER)));
     if (!need_faithful) {
         if (tid == 0) {
             p.tokens[b] = qid[j];
@@ -1007,16 +1013,9 @@ __global__ void __launch_bounds__(NT) topk_fused_kernel(KParams p) {
         lm = max(lm, k);
         mi = max(mi, cidx[nc + j]);
     }
-    // Boundary-tie evidence from chunks that cut elements equal to their k-th key.
-    uint32_t ck_tie_keys = 0u;
     const uint32_t gmax = block_max_u32(lm, sh + 32);
     const uint32_t imax = block_max_u32(mi, sh + 32);
     SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, bits_for(imax), hist, sh);
-    for (int i = tid; i < p.nchunks; i += NT) {
-        const uint2 ci = __ldcg(p.chunk_info + (int64_t)b * p.nchunks + i);
-        if (ci.y && ci.x == s2.kth_key) ck_tie_keys = 1u;
-    }
-    ck_tie_keys = block_max_u32(ck_tie_keys, sh + 32);
     if (tid == 0) sh[8] = 0u;
     __syncthreads();
     {
@@ -1047,14 +1046,25 @@ __global__ void __launch_bounds__(NT) topk_fused_kernel(KParams p) {
     }
     __syncthreads();
     const int nsel = (int)min(sh[8], (uint32_t)K);
-    const uint32_t btie = (s2.tie_cut || ck_tie_keys) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
+    // The boundary value is the smallest selected key. A boundary tie exists when the
+    // merge cut elements of that value, or a chunk cut elements of that value.
+    uint32_t kb = 0xFFFFFFFFu;
+    for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
+    kb = block_min_u32(kb, sh + 32);
+    uint32_t ck_tie = 0u;
+    for (int i = tid; i < p.nchunks; i += NT) {
+        const uint2 ci = __ldcg(p.chunk_info + (int64_t)b * p.nchunks + i);
+        if (ci.y && ci.x == kb) ck_tie = 1u;
+    }
+    ck_tie = block_max_u32(ck_tie, sh + 32);
+    const uint32_t btie = (s2.tie_cut || ck_tie) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
     if (tid == 0) p.row_counter[b] = 0u;  // ready for the next launch
 
     if (p.local_emit) {
         // Vocab-sharded: publish the local top-K and tie evidence for the all-gather.
         uint2* eo = p.emit_out + (int64_t)b * (K + 1);
         for (int s = tid; s < K; s += NT) eo[s] = s < nsel ? make_uint2(sk[s], si[s]) : make_uint2(0u, 0xFFFFFFFFu);
-        if (tid == 0) eo[K] = make_uint2(s2.kth_key, (s2.tie_cut || ck_tie_keys) ? 1u : 0u);
+        if (tid == 0) eo[K] = make_uint2(kb, btie ? 1u : 0u);
         return;
     }
     if (p.path == kGreedy) {
@@ -1072,7 +1082,7 @@ __global__ void __launch_bounds__(NT) topk_fused_kernel(KParams p) {
     unsigned char* work = (unsigned char*)(ckey);
     work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
     uint32_t f2;
-    const bool faithful = stage2_canonical(p, b, sk, si, nsel, gmax, btie, work, sh + 32, &f2);
+    const bool faithful = stage2_canonical(p, b, sk, si, nsel, gmax, kb, btie, work, sh + 32, &f2);
     if (faithful) faithful_row<T>(p, b, f2, region, sh + 32);
 }
 
@@ -1102,12 +1112,6 @@ __global__ void __launch_bounds__(NT) merge_draw_kernel(KParams p, const uint2* 
     const uint32_t gmax = block_max_u32(lm, sh + 32);
     const uint32_t imax = block_max_u32(mi, sh + 32);
     SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, bits_for(imax), hist, sh);
-    uint32_t rt = 0u;
-    for (int r = tid; r < ranks; r += NT) {
-        const uint2 info = recv[((int64_t)r * p.B + b) * (K + 1) + K];
-        if (info.y && info.x == s2.kth_key) rt = 1u;
-    }
-    rt = block_max_u32(rt, sh + 32);
     if (tid == 0) sh[8] = 0u;
     __syncthreads();
     const int rounds = (n2 + NT - 1) / NT;
@@ -1143,11 +1147,20 @@ __global__ void __launch_bounds__(NT) merge_draw_kernel(KParams p, const uint2* 
         }
         return;
     }
+    uint32_t kb = 0xFFFFFFFFu;
+    for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
+    kb = block_min_u32(kb, sh + 32);
+    uint32_t rt = 0u;
+    for (int r = tid; r < ranks; r += NT) {
+        const uint2 info = recv[((int64_t)r * p.B + b) * (K + 1) + K];
+        if (info.y && info.x == kb) rt = 1u;
+    }
+    rt = block_max_u32(rt, sh + 32);
     const uint32_t btie = (s2.tie_cut || rt) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
     unsigned char* work = (unsigned char*)(ckey);
     work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
     uint32_t f2;
-    stage2_canonical(p, b, sk, si, nsel, gmax, btie, work, sh + 32, &f2);
+    stage2_canonical(p, b, sk, si, nsel, gmax, kb, btie, work, sh + 32, &f2);
 }
 
 // ---------------------------------------------------------------------------------
