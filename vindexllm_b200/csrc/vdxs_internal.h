@@ -9,10 +9,10 @@
 
 namespace vdxs {
 
-constexpr int kThreads = 512;        // threads per CTA in every sampling kernel
+constexpr int kThreads = 256;        // threads per CTA in every sampling kernel
 constexpr int kMaxTopK = 1024;       // largest top_k served by the top-k path
 constexpr int kMaxHistory = 8192;    // largest history stride served by the penalty prep
-constexpr int kFaithfulTile = 8192;  // elements per tile of the min-buffer emulation
+constexpr int kFaithfulTile = 4096;  // elements per tile of the min-buffer emulation
 
 enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
 
@@ -82,8 +82,11 @@ struct SampleArgs {
 };
 
 struct LaunchPlan {
-    int chunk = 0;
-    int nchunks = 0;
+    int chunk = 0;    // elements per chunk (one register tile of the CTA)
+    int nchunks = 0;  // chunks per row (full-softmax path: CTAs per row)
+    int span = 1;     // chunks walked by one CTA of the top-k path
+    int nspans = 0;   // CTAs per row of the top-k path
+    int elems = 32;   // keys per thread per chunk
     size_t smem = 0;
 };
 

@@ -4,10 +4,10 @@
 // [B, V] device-resident logits.
 //
 //   penalty_prep_kernel   Sampler.pas:285-303  history ids -> sorted unique (id, f^n(x))
-//   topk_fused_kernel     Sampler.pas:305-459  one CTA per (row, chunk): stream the chunk
-//                         once from HBM with 128-bit loads, keep it in shared memory as
-//                         order-preserving keys, radix-select the chunk top-K; the last
-//                         CTA of a row merges the chunk candidates plus the penalised
+//   topk_span_kernel      Sampler.pas:305-459  one CTA per (row, span of chunks): stream
+//                         each chunk once from HBM with 128-bit loads into registers as
+//                         order-preserving keys, keep a running top-K of the span; the last
+//                         CTA of a row merges the span candidates plus the penalised
 //                         history entries, then applies exp / min-p / sort / top-p / draw.
 //                         Rows whose token depends on the reference's min-buffer slot
 //                         order are re-resolved in the same CTA by an exact emulation of
@@ -40,15 +40,38 @@ constexpr int kHistWords = 512;
 constexpr int kShWords = 64;
 constexpr size_t kHeadBytes = (kHistWords + kShWords) * 4;  // hist + scalars at smem start
 
-enum ErrCode : int32_t { kErrNone = 0, kErrSelect = 1, kErrFaithful = 2 };
+enum ErrCode : int32_t { kErrNone = 0, kErrSelect = 1, kErrFaithful = 2, kErrTimeout = 3 };
+
+// Phase timing for development builds (-DVDXS_TIMING): thread 0 of each CTA adds the
+// cycles of each phase to a per-phase total. Compiled out of the library otherwise.
+#ifdef VDXS_TIMING
+__device__ unsigned long long g_phase_cycles[32];
+__device__ unsigned long long g_phase_count[32];
+#define VDXS_T0(v) long long v = clock64()
+#define VDXS_T1(id, v)                                                          \
+    do {                                                                        \
+        if (threadIdx.x == 0) {                                                 \
+            atomicAdd(&g_phase_cycles[id], (unsigned long long)(clock64() - v)); \
+            atomicAdd(&g_phase_count[id], 1ull);                                \
+        }                                                                       \
+    } while (0)
+#else
+#define VDXS_T0(v) \
+    do {           \
+    } while (0)
+#define VDXS_T1(id, v) \
+    do {               \
+    } while (0)
+#endif
 
 struct KParams {
     const void* logits;
     int64_t stride;
     int V;
     int B;
-    int chunk;
-    int nchunks;
+    int chunk;    // elements per chunk (top-k path: NT * keys per thread)
+    int nchunks;  // CTAs per row (top-k path: spans; full path: chunks)
+    int span;     // chunks per span (top-k path)
     int K;
     int path;
     // penalty list (sorted unique local ids and their penalised values); null when off
@@ -149,6 +172,55 @@ __device__ __forceinline__ unsigned lanemask_lt() {
     unsigned m;
     asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
     return m;
+}
+
+// ---- 1-D TMA bulk copies (global -> shared) completed on an mbarrier ---------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) into this
+// CTA's shared memory; completion is counted on `bar`.
+__device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_inval(uint64_t* bar) {
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0u;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Waits for phase `parity` of `bar`, giving up after about 2 s (returns false).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (;;) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > 2000000000ull) return false;
+    }
 }
 
 // ---------------------------------------------------------------------------------
@@ -550,14 +622,24 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
         exact = (int)emin - 1024 >= E - 29;
     }
     const float u = p.uniform ? p.uniform[b] : 0.0f;
-    // Each thread owns two consecutive walk positions (P2 <= 1024 = 2 * NT).
-    const int i0 = 2 * tid;
+    // Each thread owns EPT consecutive walk positions (P2 <= 1024 = EPT * NT).
+    constexpr int EPT = 1024 / NT;
+    const int i0 = EPT * tid;
     if (exact) {
-        double a0 = i0 < P2 ? (double)q[i0] : 0.0, a1 = i0 + 1 < P2 ? (double)q[i0 + 1] : 0.0;
+        double a[EPT];
+        double part = 0.0;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            a[e] = i0 + e < P2 ? (double)q[i0 + e] : 0.0;
+            part += a[e];
+        }
         double tot;
-        double off = block_excl_scan_d(a0 + a1, s_dsh, &tot);
-        if (i0 < P2) pre[i0] = off;
-        if (i0 + 1 < P2) pre[i0 + 1] = off + a0;
+        double off = block_excl_scan_d(part, s_dsh, &tot);
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) {
+            if (i0 + e < P2) pre[i0 + e] = off;
+            off += a[e];
+        }
         if (tid == 0) pre[P2] = tot;
         __syncthreads();
         double lsum = tot;
@@ -565,14 +647,14 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
         if (p.top_p < 1.0f) {
             const double target = (double)p.top_p * tot;
             uint32_t mm = (uint32_t)nsel;
-            for (int i = i0; i < i0 + 2 && i < nsel; ++i)
+            for (int i = i0; i < i0 + EPT && i < nsel; ++i)
                 if (!(pre[i] < target && q[i] > 0.0f)) mm = min(mm, (uint32_t)i);
             m = (int)block_min_u32(mm, shu);
             lsum = pre[m];
         }
         const double t = (double)u * lsum;
         uint32_t jj = 0xFFFFFFFFu;
-        for (int i = i0; i < i0 + 2 && i < m; ++i)
+        for (int i = i0; i < i0 + EPT && i < m; ++i)
             if (pre[i] + (double)q[i] > t) jj = min(jj, (uint32_t)i);
         jj = block_min_u32(jj, shu);
         if (tid == 0) {
@@ -862,192 +944,146 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
 }
 
 // ---------------------------------------------------------------------------------
-// Stage 1 + stage 2 (top-k and greedy paths).
-// Shared memory: [hist 512 | scalars 64] then
-//   stage 1: keys[chunk] | bitmap[chunk/32]
-//   stage 2: sk[K] | si[K] | ckey[n2] | cidx[n2]   (math work aliases ckey)
-//   faithful: its own layout from the same base.
+// Stage 1 (top-k and greedy paths): one CTA walks a span of consecutive chunks of a
+// row. Each chunk (NT*E elements) is streamed once from HBM with 128-bit loads into
+// registers as order-preserving keys. The CTA keeps a running top-K of its span in
+// shared memory; after the first chunk every element costs one register compare
+// against the running K-th key (later elements lose ties, so the compare is strict).
+// The first chunk's threshold is a lower bound on its K-th key taken from a log-bin
+// histogram of each thread's top-M keys, so only about K candidates reach the exact
+// select. Candidate overflow falls back to an exact select over the whole chunk.
 // ---------------------------------------------------------------------------------
-template <typename T, bool VEC>
-__global__ void __launch_bounds__(NT) topk_fused_kernel(KParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint32_t* hist = (uint32_t*)smem_raw;
-    uint32_t* sh = hist + kHistWords;
-    unsigned char* region = smem_raw + kHeadBytes;
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+// Keys of one chunk from its shared-memory stage (first n_tma elements) and, for a
+// ragged tail, from global memory. Element (j, e) of thread t is chunk position
+// (t + j*NT)*VN + e. Excluded (history) and out-of-range elements get key 0.
+template <typename T, int E>
+__device__ __forceinline__ void load_stage_keys(const T* stage, int n_tma, const T* row, int64_t start, int n,
+                                                const uint32_t* bitmap, bool excl, uint32_t (&keys)[E]) {
+    constexpr int VN = 16 / sizeof(T);
+    constexpr int NV = E / VN;
+    static_assert(E % VN == 0, "keys per thread must be a multiple of the vector width");
     const int tid = threadIdx.x;
-    const int c = blockIdx.x, b = blockIdx.y;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+        const int pos = (tid + j * NT) * VN;
+        float x[VN];
+        if (pos + VN <= n_tma) {
+            unpack(*reinterpret_cast<const uint4*>(stage + pos), x, T());
+        } else {
+#pragma unroll
+            for (int e = 0; e < VN; ++e) {
+                const int i = pos + e;
+                x[e] = i < n ? (i < n_tma ? to_f(stage[i]) : ld_elem(row, start + i)) : 0.0f;
+            }
+        }
+        const uint32_t ex = excl ? (bitmap[pos >> 5] >> (pos & 31)) : 0u;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) keys[j * VN + e] = (pos + e < n && !((ex >> e) & 1u)) ? f2key(x[e]) : 0u;
+    }
+}
+
+// Keys of one chunk straight from global memory (rows that are not 16-byte aligned).
+template <typename T, int E>
+__device__ __forceinline__ void load_global_keys(const T* row, int64_t start, int n, const uint32_t* bitmap,
+                                                 bool excl, uint32_t (&keys)[E]) {
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+        const int pos = tid + j * NT;
+        const bool ex = excl && ((bitmap[pos >> 5] >> (pos & 31)) & 1u);
+        keys[j] = (pos < n && !ex) ? f2key(ld_elem(row, start + pos)) : 0u;
+    }
+}
+
+// Chunk position of register key e of this thread.
+template <typename T, int E, bool VEC>
+__device__ __forceinline__ int key_pos(int e) {
+    constexpr int VN = VEC ? (int)(16 / sizeof(T)) : 1;
+    return (threadIdx.x + (e / VN) * NT) * VN + (e % VN);
+}
+
+// Writes every selected element of src to (ok, oi), returns the count (uniform).
+template <class Src, class IdxF>
+__device__ int block_emit(const Src& src, int n, const SelectOut& s, uint32_t* ok, uint32_t* oi, int cap,
+                          uint32_t* counter, IdxF idx_of) {
+    const int tid = threadIdx.x;
+    if (tid == 0) *counter = 0u;
+    __syncthreads();
+    const int rounds = (n + NT - 1) / NT;
+    for (int j = 0; j < rounds; ++j) {
+        const int i = j * NT + tid;
+        uint32_t k = 0u;
+        bool sel = false;
+        if (i < n) {
+            k = src.key(i);
+            sel = selected(k, src.tb(i), s);
+        }
+        const unsigned m = __ballot_sync(FULL, sel);
+        if (m) {
+            uint32_t base = 0u;
+            if ((tid & 31) == 0) base = atomicAdd(counter, (uint32_t)__popc(m));
+            base = __shfl_sync(FULL, base, 0);
+            if (sel) {
+                const uint32_t slot = base + __popc(m & lanemask_lt());
+                if (slot < (uint32_t)cap) {
+                    ok[slot] = k;
+                    oi[slot] = idx_of(i);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const uint32_t c = *counter;
+    __syncthreads();
+    return (int)min(c, (uint32_t)cap);
+}
+
+struct IdentIdx {
+    const uint32_t* t;
+    __device__ __forceinline__ uint32_t operator()(int i) const { return t[i]; }
+};
+struct OffsetIdx {
+    uint32_t base;
+    __device__ __forceinline__ uint32_t operator()(int i) const { return base + (uint32_t)i; }
+};
+
+// Stage 2 for one row, run by the last CTA of the row: merge the span candidates and
+// the penalised history entries, then greedy / draw (or publish for the all-gather).
+template <typename T>
+__device__ void finish_row(const KParams& p, int b, unsigned char* region, uint32_t* hist, uint32_t* sh) {
+    const int tid = threadIdx.x;
     const int K = p.K;
-    const int64_t start = (int64_t)c * p.chunk;
-    const int n = (int)min((int64_t)p.chunk, (int64_t)p.V - start);
-    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
-    uint32_t* keys = (uint32_t*)region;
-    uint32_t* bitmap = keys + p.chunk;
     const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
     const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-
-    // History entries are excluded here and re-enter stage 2 with penalised values.
-    if (npen > 0) {
-        for (int i = tid; i < (p.chunk >> 5); i += NT) bitmap[i] = 0u;
-        __syncthreads();
-        const int j0 = lower_bound_i32(pid, npen, start);
-        for (int j = j0 + tid; j < npen && pid[j] < start + n; j += NT) {
-            const int e = pid[j] - (int)start;
-            atomicOr(&bitmap[e >> 5], 1u << (e & 31));
-        }
-        __syncthreads();
-    }
-
-    uint32_t lmax = 0u;
-    if (VEC) {
-        constexpr int VN = VecTraits<T>::N;
-        constexpr int U = 8;
-        const int nvec = n / VN;
-        const char* base = (const char*)(row + start);
-        for (int v0 = tid; v0 < nvec; v0 += NT * U) {
-            uint4 r[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int v = v0 + u * NT;
-                if (v < nvec) r[u] = ld_stream16(base + (size_t)v * 16);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const int v = v0 + u * NT;
-                if (v < nvec) {
-                    float x[VN];
-                    unpack(r[u], x, T());
-                    uint32_t kk[VN];
-                    uint32_t excl = 0u;
-                    if (npen > 0) excl = (bitmap[(v * VN) >> 5] >> ((v * VN) & 31)) & ((1u << VN) - 1u);
-#pragma unroll
-                    for (int e = 0; e < VN; ++e) {
-                        kk[e] = ((excl >> e) & 1u) ? 0u : f2key(x[e]);
-                        lmax = max(lmax, kk[e]);
-                    }
-                    uint4* dst = (uint4*)(keys + v * VN);
-                    dst[0] = make_uint4(kk[0], kk[1], kk[2], kk[3]);
-                    if constexpr (VN == 8) dst[1] = make_uint4(kk[4], kk[5], kk[6], kk[7]);
-                }
-            }
-        }
-        for (int i = nvec * VN + tid; i < n; i += NT) {
-            const bool ex = npen > 0 && ((bitmap[i >> 5] >> (i & 31)) & 1u);
-            const uint32_t k = ex ? 0u : f2key(ld_elem(row, start + i));
-            keys[i] = k;
-            lmax = max(lmax, k);
-        }
-    } else {
-        for (int i = tid; i < n; i += NT) {
-            const bool ex = npen > 0 && ((bitmap[i >> 5] >> (i & 31)) & 1u);
-            const uint32_t k = ex ? 0u : f2key(ld_elem(row, start + i));
-            keys[i] = k;
-            lmax = max(lmax, k);
-        }
-    }
-    const uint32_t kmax = block_max_u32(lmax, sh + 32);
-
-    SelectOut so = block_select(SmemKeySrc{keys}, n, K, kmax, bits_for((uint32_t)(n - 1)), hist, sh);
-    uint2* out = p.cand + ((int64_t)b * p.nchunks + c) * K;
-    if (tid == 0) sh[8] = 0u;
-    __syncthreads();
-    {
-        const int rounds = (n + NT - 1) / NT;
-        const uint32_t gbase = (uint32_t)(start + p.vocab_offset);
-        for (int j = 0; j < rounds; ++j) {
-            const int i = j * NT + tid;
-            uint32_t k = 0u;
-            bool s = false;
-            if (i < n) {
-                k = keys[i];
-                s = selected(k, (uint32_t)i, so);
-            }
-            const unsigned m = __ballot_sync(FULL, s);
-            if (m) {
-                uint32_t base = 0u;
-                if ((tid & 31) == 0) base = atomicAdd(&sh[8], (uint32_t)__popc(m));
-                base = __shfl_sync(FULL, base, 0);
-                if (s) {
-                    const uint32_t slot = base + __popc(m & lanemask_lt());
-                    if (slot < (uint32_t)K) out[slot] = make_uint2(k, gbase + (uint32_t)i);
-                }
-            }
-        }
-    }
-    __syncthreads();
-    const uint32_t emitted = sh[8];
-    if (emitted > (uint32_t)K && tid == 0) atomicExch(p.err, kErrSelect);
-    for (int s = (int)emitted + tid; s < K; s += NT) out[s] = make_uint2(0u, 0xFFFFFFFFu);
-    if (tid == 0) p.chunk_info[(int64_t)b * p.nchunks + c] = make_uint2(so.kth_key, (uint32_t)so.tie_cut);
-
-    // Completion: the last CTA of the row runs stage 2.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&p.row_counter[b], 1u);
-        sh[9] = prev == (uint32_t)(p.nchunks - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (sh[9] == 0u) return;
-    __threadfence();
-
-    // ---- stage 2: merge chunk candidates and penalised history entries ----
     uint32_t* sk = (uint32_t*)region;
     uint32_t* si = sk + K;
     uint32_t* ckey = si + K;
-    const int nc = p.nchunks * K;
+    const int nc = p.nchunks * K;  // nchunks = spans per row on this path
     const int n2 = nc + npen;
     uint32_t* cidx = ckey + n2;
-    const uint2* cb = p.cand + (int64_t)b * p.nchunks * K;
-    uint32_t lm = 0u, mi = 0u;
+    const uint2* cb = p.cand + (int64_t)b * nc;
+    uint32_t lm = 0u;
     for (int i = tid; i < nc; i += NT) {
         const uint2 e = __ldcg(cb + i);
         ckey[i] = e.x;
         cidx[i] = e.y;
         lm = max(lm, e.x);
-        if (e.x) mi = max(mi, e.y);
     }
     for (int j = tid; j < npen; j += NT) {
         const uint32_t k = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
         ckey[nc + j] = k;
         cidx[nc + j] = (uint32_t)(pid[j] + p.vocab_offset);
         lm = max(lm, k);
-        mi = max(mi, cidx[nc + j]);
     }
     const uint32_t gmax = block_max_u32(lm, sh + 32);
-    const uint32_t imax = block_max_u32(mi, sh + 32);
-    SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, bits_for(imax), hist, sh);
-    if (tid == 0) sh[8] = 0u;
-    __syncthreads();
-    {
-        const int rounds = (n2 + NT - 1) / NT;
-        for (int j = 0; j < rounds; ++j) {
-            const int i = j * NT + tid;
-            uint32_t k = 0u, t = 0u;
-            bool s = false;
-            if (i < n2) {
-                k = ckey[i];
-                t = cidx[i];
-                s = selected(k, t, s2);
-            }
-            const unsigned m = __ballot_sync(FULL, s);
-            if (m) {
-                uint32_t base = 0u;
-                if ((tid & 31) == 0) base = atomicAdd(&sh[8], (uint32_t)__popc(m));
-                base = __shfl_sync(FULL, base, 0);
-                if (s) {
-                    const uint32_t slot = base + __popc(m & lanemask_lt());
-                    if (slot < (uint32_t)K) {
-                        sk[slot] = k;
-                        si[slot] = t;
-                    }
-                }
-            }
-        }
-    }
-    __syncthreads();
-    const int nsel = (int)min(sh[8], (uint32_t)K);
+    const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
+    const SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
+    const int nsel = block_emit(SmemPairSrc{ckey, cidx}, n2, s2, sk, si, K, &sh[8], IdentIdx{cidx});
     // The boundary value is the smallest selected key. A boundary tie exists when the
-    // merge cut elements of that value, or a chunk cut elements of that value.
+    // merge cut elements of that value, or a span cut elements of that value.
     uint32_t kb = 0xFFFFFFFFu;
     for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
     kb = block_min_u32(kb, sh + 32);
@@ -1082,8 +1118,247 @@ __global__ void __launch_bounds__(NT) topk_fused_kernel(KParams p) {
     unsigned char* work = (unsigned char*)(ckey);
     work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
     uint32_t f2;
+    VDXS_T0(t_s2);
     const bool faithful = stage2_canonical(p, b, sk, si, nsel, gmax, kb, btie, work, sh + 32, &f2);
-    if (faithful) faithful_row<T>(p, b, f2, region, sh + 32);
+    VDXS_T1(6, t_s2);
+    if (faithful) {
+        VDXS_T0(t_ff);
+        faithful_row<T>(p, b, f2, region, sh + 32);
+        VDXS_T1(7, t_ff);
+    }
+}
+
+template <typename T>
+__host__ __device__ constexpr int stage_count() { return sizeof(T) == 4 ? 4 : 6; }
+
+template <typename T, int E, int M, bool TMA>
+__global__ void __launch_bounds__(NT) topk_span_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    const int tid = threadIdx.x;
+    const int sp = blockIdx.x, b = blockIdx.y;
+    const int K = p.K;
+    constexpr int CH = NT * E;
+    constexpr int CAP = CH / 2;
+    constexpr int NST = stage_count<T>();
+    T* stages = (T*)region;                                                  // [NST][CH]
+    uint64_t* bars = (uint64_t*)(region + (size_t)NST * CH * sizeof(T));    // [NST]
+    uint32_t* lk = (uint32_t*)(bars + NST);  // running top-K of the span
+    uint32_t* li = lk + K;
+    uint32_t* bk = li + K;                   // select output
+    uint32_t* bi = bk + K;
+    uint32_t* ak = bi + K;                   // [K + CAP] list + candidates, aliased by fk[CH]
+    uint32_t* ai = ak + K + CAP;
+    uint32_t* fk = ak;
+    uint32_t* bitmap = ai + K + CAP;         // [CH / 32]
+    int* scan_sh = (int*)(sh + 48);
+
+    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+    const int c0 = sp * p.span, c1 = min(c0 + p.span, (p.V + CH - 1) / CH);
+    const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
+    int L = 0;              // entries in the running list
+    uint32_t tau = 0u;      // its smallest key once L == K
+    uint32_t lmaxk = 0u;    // its largest key
+    uint32_t max_cut = 0u;  // largest key at which elements equal to it were dropped
+    VDXS_T0(t_all);
+
+    // One elected thread streams chunk c into stage (c - c0) % NST.
+    auto issue = [&](int c) {
+        const int stg = (c - c0) % NST;
+        const int64_t st0 = (int64_t)c * CH;
+        const int nn = (int)min((int64_t)CH, (int64_t)p.V - st0);
+        const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
+        if (bytes) {
+            mbar_arrive_expect_tx(&bars[stg], bytes);
+            tma_load_1d(stages + (size_t)stg * CH, row + st0, bytes, &bars[stg]);
+        } else {
+            mbar_arrive(&bars[stg]);
+        }
+    };
+    if constexpr (TMA) {
+        if (tid == 0) {
+            for (int s = 0; s < NST; ++s) mbar_init(&bars[s], 1);
+            fence_mbar_init();
+        }
+        __syncthreads();
+        if (tid == 0)
+            for (int c = c0; c < c1 && c < c0 + NST; ++c) issue(c);
+    }
+
+    for (int c = c0; c < c1; ++c) {
+        const int64_t start = (int64_t)c * CH;
+        const int n = (int)min((int64_t)CH, (int64_t)p.V - start);
+        VDXS_T0(t_w);
+        if (npen > 0) {
+            for (int i = tid; i < CH / 32; i += NT) bitmap[i] = 0u;
+            __syncthreads();
+            const int j0 = lower_bound_i32(pid, npen, start);
+            for (int j = j0 + tid; j < npen && pid[j] < start + n; j += NT) {
+                const int e = pid[j] - (int)start;
+                atomicOr(&bitmap[e >> 5], 1u << (e & 31));
+            }
+            __syncthreads();
+        }
+        uint32_t keys[E];
+        if constexpr (TMA) {
+            const int it = c - c0, stg = it % NST;
+            if (!mbar_wait_bounded(&bars[stg], (uint32_t)((it / NST) & 1))) atomicExch(p.err, kErrTimeout);
+            const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
+            load_stage_keys<T, E>(stages + (size_t)stg * CH, n_tma, row, start, n, bitmap, npen > 0, keys);
+            __syncthreads();  // every thread has its keys: the stage can be refilled
+            if (tid == 0 && c + NST < c1) issue(c + NST);
+        } else {
+            load_global_keys<T, E>(row, start, n, bitmap, npen > 0, keys);
+        }
+        VDXS_T1(1, t_w);
+        VDXS_T0(t_e);
+
+        uint32_t thr = 1u;
+        const bool strict = L == K;
+        if (strict) {
+            thr = tau;
+        } else {
+            // Lower bound on this chunk's K-th key from each thread's top-M keys.
+            uint32_t top[M];
+#pragma unroll
+            for (int m = 0; m < M; ++m) top[m] = 0u;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                uint32_t k = keys[e];
+#pragma unroll
+                for (int m = 0; m < M; ++m) {
+                    const uint32_t hi = max(top[m], k);
+                    k = min(top[m], k);
+                    top[m] = hi;
+                }
+            }
+            const uint32_t kmx = block_max_u32(top[0], sh + 32);
+            if (kmx == 0u) continue;  // nothing valid in this chunk (uniform)
+            for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
+            __syncthreads();
+#pragma unroll
+            for (int m = 0; m < M; ++m)
+                if (top[m]) atomicAdd(&hist[logbin(kmx - top[m])], 1u);
+            __syncthreads();
+            if (tid < 32) warp_find(hist, kHistBins, (uint32_t)K, sh);
+            __syncthreads();
+            if (sh[0] != 0xFFFFFFFFu) {
+                uint32_t lo;
+                int bits;
+                logbin_range((int)sh[0], &lo, &bits);
+                const uint32_t dmax = min(lo + ((1u << bits) - 1u), kmx - 1u);
+                thr = kmx - dmax;
+            }
+            __syncthreads();
+        }
+        VDXS_T1(2, t_e);
+        VDXS_T0(t_f);
+        int cnt = 0;
+        bool eqd = false;
+        uint32_t cmax = 0u;
+#pragma unroll
+        for (int e = 0; e < E; ++e) {
+            const uint32_t k = keys[e];
+            const bool pass = k != 0u && (strict ? k > thr : k >= thr);
+            cnt += pass ? 1 : 0;
+            cmax = pass ? max(cmax, k) : cmax;
+            eqd |= strict && k == thr;
+        }
+        if (strict && __syncthreads_or(eqd)) max_cut = max(max_cut, thr);
+        int total;
+        int off = block_excl_scan(cnt, scan_sh, &total);
+        VDXS_T1(3, t_f);
+        if (total == 0) continue;
+        VDXS_T0(t_m);
+        const uint32_t gbase = (uint32_t)(p.vocab_offset + start);
+        int m_new;
+        if (L + total <= K + CAP) {
+            for (int s = tid; s < L; s += NT) {
+                ak[s] = lk[s];
+                ai[s] = li[s];
+            }
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                const uint32_t k = keys[e];
+                if (k != 0u && (strict ? k > thr : k >= thr)) {
+                    ak[L + off] = k;
+                    ai[L + off] = gbase + (uint32_t)key_pos<T, E, TMA>(e);
+                    ++off;
+                }
+            }
+            const uint32_t kall = max(block_max_u32(cmax, sh + 32), lmaxk);
+            const SelectOut so = block_select(SmemPairSrc{ak, ai}, L + total, K, kall, tbb, hist, sh);
+            if (so.tie_cut) max_cut = max(max_cut, so.kth_key);
+            m_new = block_emit(SmemPairSrc{ak, ai}, L + total, so, bk, bi, K, &sh[8], IdentIdx{ai});
+        } else {
+            // Candidate overflow: exact select over the whole chunk, then merge.
+            uint32_t km = 0u;
+#pragma unroll
+            for (int e = 0; e < E; ++e) {
+                fk[key_pos<T, E, TMA>(e)] = keys[e];
+                km = max(km, keys[e]);
+            }
+            km = block_max_u32(km, sh + 32);
+            const SelectOut sc = block_select(SmemKeySrc{fk}, CH, K, km, bits_for((uint32_t)(CH - 1)), hist, sh);
+            if (sc.tie_cut) max_cut = max(max_cut, sc.kth_key);
+            const int mc = block_emit(SmemKeySrc{fk}, CH, sc, bk, bi, K, &sh[8], OffsetIdx{gbase});
+            for (int s = tid; s < L; s += NT) {
+                ak[s] = lk[s];
+                ai[s] = li[s];
+            }
+            for (int s = tid; s < mc; s += NT) {
+                ak[L + s] = bk[s];
+                ai[L + s] = bi[s];
+            }
+            __syncthreads();
+            const uint32_t kall = max(km, lmaxk);
+            const SelectOut so = block_select(SmemPairSrc{ak, ai}, L + mc, K, kall, tbb, hist, sh);
+            if (so.tie_cut) max_cut = max(max_cut, so.kth_key);
+            m_new = block_emit(SmemPairSrc{ak, ai}, L + mc, so, bk, bi, K, &sh[8], IdentIdx{ai});
+        }
+        uint32_t mn = 0xFFFFFFFFu, mx = 0u;
+        for (int s = tid; s < m_new; s += NT) {
+            lk[s] = bk[s];
+            li[s] = bi[s];
+            mn = min(mn, bk[s]);
+            mx = max(mx, bk[s]);
+        }
+        L = m_new;
+        mn = block_min_u32(mn, sh + 32);
+        lmaxk = block_max_u32(mx, sh + 32);
+        tau = L == K ? mn : 0u;
+        VDXS_T1(4, t_m);
+    }
+    if constexpr (TMA) {
+        __syncthreads();
+        if (tid == 0)
+            for (int s = 0; s < NST; ++s) mbar_inval(&bars[s]);
+    }
+
+    // Publish the span's list (padded) and its boundary-tie evidence.
+    uint2* out = p.cand + ((int64_t)b * p.nchunks + sp) * K;
+    for (int s = tid; s < K; s += NT) out[s] = s < L ? make_uint2(lk[s], li[s]) : make_uint2(0u, 0xFFFFFFFFu);
+    if (tid == 0)
+        p.chunk_info[(int64_t)b * p.nchunks + sp] = make_uint2(tau, (L == K && max_cut == tau) ? 1u : 0u);
+
+    VDXS_T1(0, t_all);
+    // Completion: the last CTA of the row runs stage 2.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t prev = atomicAdd(&p.row_counter[b], 1u);
+        sh[9] = prev == (uint32_t)(p.nchunks - 1) ? 1u : 0u;
+    }
+    __syncthreads();
+    if (sh[9] == 0u) return;
+    __threadfence();
+    VDXS_T0(t_fin);
+    finish_row<T>(p, b, region, hist, sh);
+    VDXS_T1(5, t_fin);
 }
 
 // ---------------------------------------------------------------------------------
@@ -1398,30 +1673,35 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     const int K = a.K;
     const int64_t V = a.V;
     const int pen_stride = a.penalty_on ? (int)std::min<int64_t>(a.hist_stride, kMaxHistory) : 0;
-    int chunk = 16384;
-    // Aim for several CTAs per SM across the grid; small batches use smaller chunks.
-    const int64_t target = 148 * 4;
-    while (chunk > 2048 && (int64_t)a.B * ((V + chunk - 1) / chunk) < target) chunk >>= 1;
-    const int min_chunk = std::max(2048, pow2_at_least(4 * K, 32));
-    if (chunk < min_chunk) chunk = min_chunk;
-    if (V <= chunk) chunk = (int)((V + 31) / 32 * 32);
+    const size_t esz = a.dtype == VDXS_DTYPE_BF16 ? 2 : 4;
+    const int nst = esz == 4 ? stage_count<float>() : stage_count<uint16_t>();
+    // Enough CTAs for several waves at two resident CTAs per SM; otherwise long spans,
+    // so that each CTA filters most elements against an established K-th key.
+    const int64_t target = 148 * 8;
+    const int E = 16;
+    const int CH = NT * E;
+    const int nch = (int)((V + CH - 1) / CH);
+    int span = 1;
+    while (span < nch && (int64_t)a.B * ((nch + 2 * span - 1) / (2 * span)) >= target) span <<= 1;
     for (;;) {
-        const int nchunks = (int)((V + chunk - 1) / chunk);
-        const int n2 = nchunks * K + pen_stride;
-        const size_t s1 = (size_t)4 * chunk + (size_t)4 * (chunk / 32 + 1);
-        size_t need = std::max(s1, stage2_bytes(K, n2));
+        const int nspans = (nch + span - 1) / span;
+        const size_t s1 = (size_t)nst * CH * esz + 8 * (size_t)nst + (size_t)16 * K + (size_t)8 * (K + CH / 2) +
+                          (size_t)CH / 8;
+        size_t need = std::max(s1, stage2_bytes(K, nspans * K + pen_stride));
         if (a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit)
             need = std::max(need, faithful_bytes(K));
         need += kHeadBytes;
         if ((int64_t)need <= smem_optin) {
-            plan->chunk = chunk;
-            plan->nchunks = nchunks;
+            plan->chunk = CH;
+            plan->elems = E;
+            plan->span = span;
+            plan->nspans = nspans;
+            plan->nchunks = nspans;
             plan->smem = align16(need);
             return cudaSuccess;
         }
-        // Stage 2 too large: fewer, bigger chunks (until stage 1 itself is too large).
-        if (s1 + kHeadBytes > (size_t)smem_optin || nchunks == 1) break;
-        chunk <<= 1;
+        if (span >= nch) break;
+        span <<= 1;
     }
     if (err) *err = "top_k too large for the shared-memory plan (top_k=" + std::to_string(K) + ")";
     return cudaErrorInvalidValue;
@@ -1531,6 +1811,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.B = a.B;
     p.chunk = plan.chunk;
     p.nchunks = plan.nchunks;
+    p.span = plan.span;
     p.K = a.K;
     p.path = a.path;
     if (a.penalty_on) {
@@ -1590,19 +1871,14 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         return cudaGetLastError();
     }
     const size_t esz = sizeof(T);
-    const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0) &&
-                     (((size_t)plan.chunk * esz) % 16 == 0);
-    if (vec) {
-        e = cudaFuncSetAttribute(topk_fused_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)plan.smem);
-        if (e != cudaSuccess) return e;
-        topk_fused_kernel<T, true><<<grid, NT, plan.smem, a.stream>>>(p);
-    } else {
-        e = cudaFuncSetAttribute(topk_fused_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)plan.smem);
-        if (e != cudaSuccess) return e;
-        topk_fused_kernel<T, false><<<grid, NT, plan.smem, a.stream>>>(p);
-    }
+    const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0);
+    const int M = a.K <= NT ? 1 : 4;
+    void (*kern)(KParams) = nullptr;
+    if (M == 1) kern = vec ? topk_span_kernel<T, 16, 1, true> : topk_span_kernel<T, 16, 1, false>;
+    else kern = vec ? topk_span_kernel<T, 16, 4, true> : topk_span_kernel<T, 16, 4, false>;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, NT, plan.smem, a.stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -1629,3 +1905,18 @@ cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std
 }
 
 }  // namespace vdxs
+
+#ifdef VDXS_TIMING
+extern "C" __attribute__((visibility("default"))) int vdxs_debug_phase_times(unsigned long long* cycles,
+                                                                                unsigned long long* counts,
+                                                                                int reset) {
+    cudaMemcpyFromSymbol(cycles, vdxs::g_phase_cycles, sizeof(unsigned long long) * 32);
+    cudaMemcpyFromSymbol(counts, vdxs::g_phase_count, sizeof(unsigned long long) * 32);
+    if (reset) {
+        unsigned long long z[32] = {0};
+        cudaMemcpyToSymbol(vdxs::g_phase_cycles, z, sizeof(z));
+        cudaMemcpyToSymbol(vdxs::g_phase_count, z, sizeof(z));
+    }
+    return 0;
+}
+#endif
