@@ -162,6 +162,30 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg,
                                   const float* h_uniform, int32_t* h_out_tokens,
                                   void* stream);
 
+/* Allocation-free variant of vdxs_sample for callers that cannot allocate device
+ * memory while sampling: for example a host that reserves all of its GPU memory when
+ * the model loads and treats any later allocation as an error, or a decode loop that
+ * must not take the implicit device-wide synchronisation of cudaMalloc/cudaFree.
+ * No counterpart in the reference (its sampler runs on the host and allocates its
+ * workspace lazily, Sampler.pas:250-263).
+ *
+ * Runs on the calling thread's current CUDA device and takes no context: its
+ * workspace is a fixed 4 MiB device array built into the library, which every GPU
+ * that loads the library holds until the process exits. Calls whose workspace would
+ * exceed it return VDXS_E_UNSUPPORTED (batch 512 at vocab 262144 with top_k 64 fits;
+ * batch 1024 with top_k 1024 does not). The call never allocates: no cudaMalloc,
+ * cudaFree or allocating library routine. Its first call on a device resolves the
+ * array's device address (once per device, with that device current); make that
+ * first call before any stream capture. All calls share the one array and it keeps
+ * the last call's contents, so calls that overlap on the GPU (other streams, other
+ * host threads) race: serialise them. `tie_mode` is VDXS_TIES_FAITHFUL or
+ * VDXS_TIES_CANONICAL; the other arguments are those of vdxs_sample. */
+VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, const void* d_logits,
+                                     int32_t dtype, int32_t batch, int32_t vocab,
+                                     int64_t row_stride, const int32_t* d_history,
+                                     int64_t history_stride, const int32_t* d_history_count,
+                                     const float* d_uniform, int32_t* d_out_tokens, void* stream);
+
 /* ------------------------------------------------------------------------------
  * Stateful mirror of TVdxSampler: one sampler state (config, xoshiro256** PRNG,
  * repeat-history ring) per batch row, kept on the host exactly as the reference

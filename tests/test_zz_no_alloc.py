@@ -1,0 +1,65 @@
+"""vdxs_sample_noalloc: the allocation-free entry point, for callers that cannot allocate
+device memory while sampling (a host that reserves all GPU memory at model load and
+forbids later allocations, or a decode loop that cannot take cudaMalloc's device-wide
+synchronisation). It must return the same tokens as vdxs_sample, call after call, while
+sharing one fixed device array. This file is collected last on purpose."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from vindexllm_b200 import _lib, abi, synth
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(lib, cfg, mode, x, u, h, c):
+    import torch
+    tok = torch.full((x.shape[0],), -7, dtype=torch.int32, device=x.device)
+    hs = h.shape[1] if h is not None else 1
+    rc = lib.vdxs_sample_noalloc(C.byref(cfg), mode, C.c_void_p(x.data_ptr()),
+                                 abi.DTYPE_BF16 if x.dtype == torch.bfloat16 else abi.DTYPE_F32,
+                                 x.shape[0], x.shape[1], x.stride(0),
+                                 None if h is None else C.c_void_p(h.data_ptr()), hs,
+                                 None if c is None else C.c_void_p(c.data_ptr()), C.c_void_p(u.data_ptr()),
+                                 C.c_void_p(tok.data_ptr()), C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == abi.OK, lib.vdxs_last_error(None)
+    torch.cuda.synchronize()
+    return tok.cpu().numpy()
+
+
+@pytest.mark.parametrize("name,batch", [("c4", None), ("c1", None), ("c2", 64), ("c0", None)])
+def test_noalloc_matches_context_entry(name, batch):
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from vindexllm_b200.sampler import SamplerContext
+    lib = _lib.load()
+    cfg = synth.sampler_config(name)
+    ctx = SamplerContext(0)
+    for mode in (abi.TIES_FAITHFUL, abi.TIES_CANONICAL):
+        ctx.set_tie_mode(mode)
+        for step in range(2):  # two calls in a row share and reuse the fixed array
+            x = synth.make_logits(name, step=step, batch=batch)
+            h, c = synth.make_history(name, step=step, batch=batch)
+            u = torch.as_tensor(synth.make_uniforms(name, step + 1, batch=x.shape[0])[step], device="cuda")
+            want = ctx.sample(cfg, x, u, h, c).cpu().numpy()
+            got = _noalloc(lib, cfg, mode, x, u, h, c)
+            assert (got == want).all(), f"{name} step {step} mode {mode}"
+    ctx.close()
+
+
+def test_noalloc_rejects_oversized_requests():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    lib = _lib.load()
+    cfg = synth.sampler_config("c3")  # batch 1024, top_k 1024: workspace beyond the fixed array
+    x = torch.zeros((1024, 262144), dtype=torch.float32, device="cuda")
+    u = torch.zeros(1024, dtype=torch.float32, device="cuda")
+    tok = torch.empty(1024, dtype=torch.int32, device="cuda")
+    rc = lib.vdxs_sample_noalloc(C.byref(cfg), abi.TIES_FAITHFUL, C.c_void_p(x.data_ptr()), abi.DTYPE_F32,
+                                 1024, 262144, 262144, None, 1, None, C.c_void_p(u.data_ptr()),
+                                 C.c_void_p(tok.data_ptr()), None)
+    assert rc == abi.E_UNSUPPORTED
+    assert b"allocation-free" in lib.vdxs_last_error(None)

@@ -341,6 +341,66 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg, con
     return VDXS_OK;
 }
 
+VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, const void* d_logits,
+                                     int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,
+                                     const int32_t* d_history, int64_t history_stride,
+                                     const int32_t* d_history_count, const float* d_uniform,
+                                     int32_t* d_out_tokens, void* stream) {
+    // Argument checks need a context only for their error text: use the thread's.
+    if (!cfg) return fail(nullptr, VDXS_E_INVALID_ARG, "config is NULL");
+    if (!d_logits || !d_out_tokens) return fail(nullptr, VDXS_E_INVALID_ARG, "NULL logits or token pointer");
+    if (dtype != VDXS_DTYPE_F32 && dtype != VDXS_DTYPE_BF16)
+        return fail(nullptr, VDXS_E_INVALID_ARG, "dtype %d is neither VDXS_DTYPE_F32 nor VDXS_DTYPE_BF16", dtype);
+    if (batch < 1 || batch > 65535) return fail(nullptr, VDXS_E_INVALID_ARG, "batch %d out of range [1,65535]", batch);
+    if (vocab < 1 || row_stride < vocab)
+        return fail(nullptr, VDXS_E_INVALID_ARG, "vocab %d / row_stride %lld invalid", vocab, (long long)row_stride);
+    if (d_history && (!d_history_count || history_stride < 1 || history_stride > kMaxHistory))
+        return fail(nullptr, VDXS_E_INVALID_ARG, "history needs counts and 1 <= history_stride <= %d", kMaxHistory);
+    if (tie_mode != VDXS_TIES_FAITHFUL && tie_mode != VDXS_TIES_CANONICAL)
+        return fail(nullptr, VDXS_E_INVALID_ARG, "unknown tie mode %d", tie_mode);
+    SampleArgs a;
+    int32_t rc = resolve_config(nullptr, cfg, vocab, &a);
+    if (rc != VDXS_OK) return rc;
+    if (a.path != kGreedy && !d_uniform)
+        return fail(nullptr, VDXS_E_INVALID_ARG, "uniform pointer is NULL but temperature != 0");
+    a.logits = d_logits;
+    a.dtype = dtype;
+    a.B = batch;
+    a.V = vocab;
+    a.stride = row_stride;
+    a.penalty_on = cfg->repeat_penalty != 1.0f && d_history != nullptr && d_history_count != nullptr;
+    a.hist = d_history;
+    a.hist_stride = history_stride;
+    a.hist_count = d_history_count;
+    a.uniform = d_uniform;
+    a.tokens = d_out_tokens;
+    a.tie_mode = tie_mode;
+    a.vocab_total = vocab;
+    a.stream = (cudaStream_t)stream;
+    void* scratch = nullptr;
+    int optin = 0;
+    cudaError_t e = noalloc_scratch(&scratch, &optin);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "scratch address lookup");
+    LaunchPlan plan;
+    std::string msg;
+    e = a.path == kFull ? plan_full(a, &plan, &msg) : plan_topk(a, optin, &plan, &msg);
+    if (e != cudaSuccess) return fail(nullptr, VDXS_E_UNSUPPORTED, "%s", msg.c_str());
+    Workspace ws;
+    const size_t need = carve_workspace(ws, (unsigned char*)scratch, kNoAllocScratchBytes, a, plan);
+    if (need > kNoAllocScratchBytes)
+        return fail(nullptr, VDXS_E_UNSUPPORTED,
+                    "this call needs %zu bytes of workspace; the allocation-free entry point has %zu "
+                    "(use vdxs_sample with a context)",
+                    need, kNoAllocScratchBytes);
+    // The array keeps the previous call's contents: reset what must start at zero.
+    if ((e = cudaMemsetAsync(ws.err, 0, sizeof(int32_t), a.stream)) != cudaSuccess ||
+        (e = cudaMemsetAsync(ws.row_counter, 0, sizeof(uint32_t) * batch, a.stream)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "scratch reset");
+    if ((e = launch_sample(a, plan, ws, &msg)) != cudaSuccess) return cuda_fail(nullptr, e, "kernel launch");
+    ok(nullptr);
+    return VDXS_OK;
+}
+
 }  // extern "C"
 
 // =====================================================================================

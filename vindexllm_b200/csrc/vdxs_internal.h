@@ -101,4 +101,13 @@ cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace
 cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std::string* err);
 void free_workspace(Workspace& ws);
 
+// Fixed device scratch used by vdxs_sample_noalloc (no allocation on any call).
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+// Device address of the scratch on the current device (resolved once per device) and
+// that device's opt-in shared-memory limit.
+cudaError_t noalloc_scratch(void** ptr, int* smem_optin);
+// Lays out the workspace of one call inside [base, base + cap) without allocating.
+// Returns the bytes the call needs; the pointers are set only when it fits.
+size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const SampleArgs& a, const LaunchPlan& plan);
+
 }  // namespace vdxs

@@ -28,6 +28,7 @@
 #include <climits>
 #include <cstdint>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 namespace vdxs {
@@ -1780,6 +1781,69 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
     }
     (void)err;
     return cudaSuccess;
+}
+
+// Scratch of vdxs_sample_noalloc: one fixed array per device, held until the process
+// exits. Host code must not use the symbol as a pointer; noalloc_scratch() resolves its
+// device address with cudaGetSymbolAddress once per device, with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+cudaError_t noalloc_scratch(void** ptr, int* smem_optin) {
+    static std::mutex mu;
+    static void* addr[64] = {nullptr};
+    static int optin[64] = {0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return e;
+        int o = 0;
+        e = cudaDeviceGetAttribute(&o, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (e != cudaSuccess) return e;
+        addr[dev] = p;
+        optin[dev] = o;
+    }
+    *ptr = addr[dev];
+    *smem_optin = optin[dev];
+    return cudaSuccess;
+}
+
+size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const SampleArgs& a, const LaunchPlan& plan) {
+    const size_t B = (size_t)a.B, nch = (size_t)plan.nchunks;
+    size_t off = 0;
+    Workspace w;
+    auto take = [&](size_t bytes) -> unsigned char* {
+        unsigned char* p = base + off;
+        off += (bytes + 255) & ~(size_t)255;
+        return p;
+    };
+    w.err = (int32_t*)take(sizeof(int32_t));
+    w.row_counter = (uint32_t*)take(B * sizeof(uint32_t));
+    w.row_counter_cap = B;
+    if (a.path != kFull) {
+        w.cand = (uint2*)take(B * nch * (size_t)a.K * sizeof(uint2));
+        w.cand_cap = B * nch * (size_t)a.K;
+        w.chunk_info = (uint2*)take(B * nch * sizeof(uint2));
+        w.chunk_info_cap = B * nch;
+    } else {
+        w.fmax = (uint32_t*)take(2 * B * nch * sizeof(uint32_t));
+        w.fsum = (double*)take(2 * B * nch * sizeof(double));
+        w.full_cap = 2 * B * nch;
+    }
+    if (a.penalty_on) {
+        const size_t ps = (size_t)std::min<int64_t>(a.hist_stride, kMaxHistory);
+        w.pen_ids = (int32_t*)take(B * ps * sizeof(int32_t));
+        w.pen_vals = (float*)take(B * ps * sizeof(float));
+        w.pen_cnt = (int32_t*)take(B * sizeof(int32_t));
+        w.pen_cap = B * ps;
+        w.pen_rows_cap = B;
+    }
+    if (off <= cap) ws = w;
+    return off;
 }
 
 void free_workspace(Workspace& ws) {
