@@ -13,6 +13,7 @@ constexpr int kThreads = 256;        // threads per CTA in every sampling kernel
 constexpr int kMaxTopK = 1024;       // largest top_k served by the top-k path
 constexpr int kMaxHistory = 8192;    // largest history stride served by the penalty prep
 constexpr int kFaithfulTile = 4096;  // elements per tile of the min-buffer emulation
+constexpr int kTauStride = 32;       // words between rows of the stream path's row bounds (one L2 line)
 
 enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
 
@@ -25,6 +26,8 @@ struct Workspace {
     size_t chunk_info_cap = 0;
     uint32_t* row_counter = nullptr;  // [rows] completion counters, self-resetting
     size_t row_counter_cap = 0;
+    uint32_t* row_tau = nullptr;      // [rows * kTauStride] stream path K-th key bounds, self-resetting
+    size_t row_tau_cap = 0;
     int32_t* pen_ids = nullptr;     // [rows * pen_stride] sorted unique history ids
     float* pen_vals = nullptr;      // [rows * pen_stride] penalised values
     int32_t* pen_cnt = nullptr;     // [rows]
@@ -87,7 +90,10 @@ struct LaunchPlan {
     int span = 1;     // chunks walked by one CTA of the top-k path
     int nspans = 0;   // CTAs per row of the top-k path
     int elems = 32;   // keys per thread per chunk
+    bool stream = false;  // top-k path: persistent stream kernel + finish kernel
+    int grid = 0;         // stream kernel grid (CTAs)
     size_t smem = 0;
+    size_t smem2 = 0;     // finish kernel shared memory
 };
 
 // Host-side launchers (vdxs_kernels.cu). Return cudaSuccess or the launch error;

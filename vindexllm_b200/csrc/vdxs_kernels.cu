@@ -84,6 +84,7 @@ struct KParams {
     uint2* cand;
     uint2* chunk_info;
     uint32_t* row_counter;
+    uint32_t* row_tau;  // stream path: per-row lower bound on the K-th key (reset by finish)
     int32_t* err;
     uint32_t* fmax;
     double* fsum;
@@ -207,6 +208,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0u;
+}
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -1132,6 +1138,727 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
 template <typename T>
 __host__ __device__ constexpr int stage_count() { return sizeof(T) == 4 ? 4 : 6; }
 
+// ---------------------------------------------------------------------------------
+// Warp-level select (one warp, warp-private histogram; __syncwarp only). Same result
+// as block_select: the K-th best element of src[0..n) in (key desc, tb asc) order.
+// ---------------------------------------------------------------------------------
+struct WarpFind {
+    int g;
+    uint32_t before, total, cnt_g;
+};
+// First bin g of hist[0..NB) whose inclusive prefix reaches `need` (one warp).
+template <int NB>
+__device__ __forceinline__ WarpFind warp_find_reg(const uint32_t* hist, uint32_t need) {
+    constexpr int SEG = (NB + 31) / 32;
+    const int l = threadIdx.x & 31;
+    uint32_t v[SEG];
+    uint32_t s = 0;
+#pragma unroll
+    for (int j = 0; j < SEG; ++j) {
+        const int bI = l * SEG + j;
+        v[j] = bI < NB ? hist[bI] : 0u;
+        s += v[j];
+    }
+    uint32_t incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(FULL, incl, o);
+        if (l >= o) incl += y;
+    }
+    WarpFind f;
+    f.total = __shfl_sync(FULL, incl, 31);
+    const unsigned m = __ballot_sync(FULL, incl >= need);
+    if (m == 0u) {
+        f.g = -1;
+        f.before = f.total;
+        f.cnt_g = 0;
+        return f;
+    }
+    const int L = __ffs(m) - 1;
+    // Resolve inside lane L's segment from registers.
+    uint32_t c = incl - s;
+    int gj = SEG - 1;
+    uint32_t cg = 0;
+    bool found = false;
+#pragma unroll
+    for (int j = 0; j < SEG; ++j) {
+        if (!found && c + v[j] >= need) {
+            gj = j;
+            cg = v[j];
+            found = true;
+        } else if (!found) {
+            c += v[j];
+        }
+    }
+    f.g = __shfl_sync(FULL, l * SEG + gj, L);
+    f.before = __shfl_sync(FULL, c, L);
+    f.cnt_g = __shfl_sync(FULL, cg, L);
+    return f;
+}
+
+template <class Src>
+__device__ SelectOut warp_select(const Src& src, int n, int K, uint32_t kmax, int tb_bits, uint32_t* wh) {
+    const int lane = threadIdx.x & 31;
+    SelectOut r;
+    r.tie_cut = 0;
+    for (int i = lane; i < kHistBins; i += 32) wh[i] = 0u;
+    __syncwarp();
+    for (int i = lane; i < n; i += 32) {
+        const uint32_t k = src.key(i);
+        if (k) atomicAdd(&wh[logbin(kmax - k)], 1u);
+    }
+    __syncwarp();
+    WarpFind f = warp_find_reg<kHistBins>(wh, (uint32_t)K);
+    r.n_valid = f.total;
+    if (f.total <= (uint32_t)K) {
+        r.kth_key = 0u;
+        r.kth_tb = 0xFFFFFFFFu;
+        __syncwarp();
+        return r;
+    }
+    uint32_t need = (uint32_t)K - f.before;
+    uint32_t dlo;
+    int bits;
+    logbin_range(f.g, &dlo, &bits);
+    const uint32_t width = 1u << bits;
+    __syncwarp();
+    if (f.cnt_g <= 32u) {
+        // Few elements in the boundary bin: gather them one per lane and rank them
+        // exactly in the composite order (key desc, tb asc).
+        uint32_t mk = 0u, mt = 0xFFFFFFFFu;
+        int got = 0;
+        for (int base = 0; base < n; base += 32) {
+            const int i = base + lane;
+            uint32_t k = 0u, t = 0u;
+            bool in = false;
+            if (i < n) {
+                k = src.key(i);
+                in = k != 0u && ((kmax - k) - dlo) < width;
+                if (in) t = src.tb(i);
+            }
+            const unsigned m = __ballot_sync(FULL, in);
+            const int pos = got + __popc(m & lanemask_lt());
+            // Lane `pos` receives this element.
+            for (unsigned mm = m; mm; mm &= mm - 1) {
+                const int src_l = __ffs(mm) - 1;
+                const int dst = got + __popc(m & ((1u << src_l) - 1u));
+                const uint32_t kk = __shfl_sync(FULL, k, src_l);
+                const uint32_t tt = __shfl_sync(FULL, t, src_l);
+                if (lane == dst) {
+                    mk = kk;
+                    mt = tt;
+                }
+            }
+            (void)pos;
+            got += __popc(m);
+        }
+        // rank = number of gathered elements that beat mine
+        int rank = 0;
+        for (int j = 0; j < got; ++j) {
+            const uint32_t kj = __shfl_sync(FULL, mk, j);
+            const uint32_t tj = __shfl_sync(FULL, mt, j);
+            rank += (kj > mk || (kj == mk && tj < mt)) ? 1 : 0;
+        }
+        const unsigned hit = __ballot_sync(FULL, lane < got && rank == (int)need - 1);
+        const int hl = __ffs(hit) - 1;
+        r.kth_key = __shfl_sync(FULL, mk, hl);
+        r.kth_tb = __shfl_sync(FULL, mt, hl);
+        // Tie cut: some gathered element with the same key ranks below the K-th.
+        const bool cut = lane < got && mk == r.kth_key && rank > (int)need - 1;
+        r.tie_cut = __any_sync(FULL, cut) ? 1 : 0;
+        if (!r.tie_cut) r.kth_tb = 0xFFFFFFFFu;  // every element equal to kth_key is taken
+        return r;
+    }
+    uint32_t n_eq = f.cnt_g;
+    while (bits > 0) {
+        const int w = bits < 8 ? bits : 8;
+        const int shift = bits - w;
+        const uint32_t wd = 1u << bits;
+        for (int i = lane; i < 256; i += 32) wh[i] = 0u;
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) {
+            const uint32_t k = src.key(i);
+            if (k) {
+                const uint32_t dd = (kmax - k) - dlo;
+                if (dd < wd) atomicAdd(&wh[dd >> shift], 1u);
+            }
+        }
+        __syncwarp();
+        f = warp_find_reg<256>(wh, need);
+        __syncwarp();
+        n_eq = f.cnt_g;
+        dlo += (uint32_t)f.g << shift;
+        need -= f.before;
+        bits = shift;
+    }
+    r.kth_key = kmax - dlo;
+    if (need == n_eq) {
+        r.kth_tb = 0xFFFFFFFFu;
+        return r;
+    }
+    r.tie_cut = 1;
+    uint32_t tlo = 0u;
+    int tbits = tb_bits;
+    while (tbits > 0) {
+        const int w = tbits < 8 ? tbits : 8;
+        const int shift = tbits - w;
+        const uint32_t hi_mask = tbits >= 32 ? 0u : (0xFFFFFFFFu << tbits);
+        for (int i = lane; i < 256; i += 32) wh[i] = 0u;
+        __syncwarp();
+        for (int i = lane; i < n; i += 32) {
+            if (src.key(i) == r.kth_key) {
+                const uint32_t t = src.tb(i);
+                if (((t ^ tlo) & hi_mask) == 0u) atomicAdd(&wh[(t >> shift) & ((1u << w) - 1u)], 1u);
+            }
+        }
+        __syncwarp();
+        f = warp_find_reg<256>(wh, need);
+        __syncwarp();
+        tlo |= (uint32_t)f.g << shift;
+        need -= f.before;
+        tbits = shift;
+    }
+    r.kth_tb = tlo;
+    return r;
+}
+
+// ---------------------------------------------------------------------------------
+// Warp sorting networks on 64-bit composites (key << 32 | ~index): larger = better,
+// so ties go to the lower index; 0 = empty. A warp array of N = 32*R elements keeps
+// element i = r*32 + lane in register r of lane `lane`.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t shfl_xor64(uint64_t v, int m) {
+    const uint32_t lo = __shfl_xor_sync(FULL, (uint32_t)v, m);
+    const uint32_t hi = __shfl_xor_sync(FULL, (uint32_t)(v >> 32), m);
+    return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ uint64_t shfl64(uint64_t v, int src) {
+    const uint32_t lo = __shfl_sync(FULL, (uint32_t)v, src);
+    const uint32_t hi = __shfl_sync(FULL, (uint32_t)(v >> 32), src);
+    return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ uint64_t comp_key(uint32_t key, uint32_t idx) {
+    return ((uint64_t)key << 32) | (uint64_t)(~idx);
+}
+
+// One compare-exchange stage (distance J) of a descending bitonic network whose
+// sub-sequences of length KB alternate direction (KB = 0: every block descending).
+// KB and J are compile-time so that every register index is static.
+template <int R, int KB, int J>
+__device__ __forceinline__ void bitonic_stage(uint64_t (&a)[R]) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (J >= 32) {
+        constexpr int RJ = J >> 5;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            if ((r ^ RJ) > r) {
+                const int i = r * 32 + lane;
+                const bool desc = KB == 0 || (i & KB) == 0;
+                const uint64_t x = a[r], y = a[r ^ RJ];
+                const bool sw = desc ? (x < y) : (x > y);
+                a[r] = sw ? y : x;
+                a[r ^ RJ] = sw ? x : y;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int i = r * 32 + lane;
+            const uint64_t y = shfl_xor64(a[r], J);
+            const bool desc = KB == 0 || (i & KB) == 0;
+            const bool lower = (lane & J) == 0;
+            a[r] = (lower == desc) ? max(a[r], y) : min(a[r], y);
+        }
+    }
+}
+template <int R, int KB, int J>
+__device__ __forceinline__ void bitonic_stages(uint64_t (&a)[R]) {
+    if constexpr (J > 0) {
+        bitonic_stage<R, KB, J>(a);
+        bitonic_stages<R, KB, J / 2>(a);
+    }
+}
+template <int R, int KK>
+__device__ __forceinline__ void bitonic_levels(uint64_t (&a)[R]) {
+    if constexpr (KK <= 32 * R) {
+        bitonic_stages<R, (KK == 32 * R ? 0 : KK), KK / 2>(a);
+        bitonic_levels<R, KK * 2>(a);
+    }
+}
+
+// Sorts the warp array descending.
+template <int R>
+__device__ __forceinline__ void warp_sort_desc(uint64_t (&a)[R]) {
+    bitonic_levels<R, 2>(a);
+}
+
+// a, b sorted descending -> a = the 32*R largest of a and b, sorted descending.
+// Returns the largest element dropped (key part only), for tie bookkeeping.
+template <int R>
+__device__ __forceinline__ uint64_t warp_merge_desc(uint64_t (&a)[R], const uint64_t (&b)[R]) {
+    const int lane = threadIdx.x & 31;
+    uint64_t dropped = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const uint64_t br = shfl64(b[R - 1 - r], 31 - lane);
+        dropped = max(dropped, min(a[r], br));
+        a[r] = max(a[r], br);
+    }
+    bitonic_stages<R, 0, 16 * R>(a);
+    uint32_t hi = __reduce_max_sync(FULL, (uint32_t)(dropped >> 32));
+    return (uint64_t)hi << 32;
+}
+
+// Element i of a warp array (broadcast to all lanes).
+template <int R>
+__device__ __forceinline__ uint64_t warp_elem(const uint64_t (&a)[R], int i) {
+    uint64_t v = 0;
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+        if (r == (i >> 5)) v = a[r];
+    return shfl64(v, i & 31);
+}
+
+#ifdef VDXS_TIMING
+// Development self-test of the sorting networks: sorts/merges n_tests arrays.
+template <int R>
+__global__ void warp_network_selftest(const uint64_t* in, uint64_t* out_sorted, uint64_t* out_merged, int n_tests) {
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (t >= n_tests) return;
+    uint64_t a[R], b[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        a[r] = in[(size_t)t * 64 * R + r * 32 + lane];
+        b[r] = in[(size_t)t * 64 * R + 32 * R + r * 32 + lane];
+    }
+    warp_sort_desc<R>(a);
+    warp_sort_desc<R>(b);
+#pragma unroll
+    for (int r = 0; r < R; ++r) out_sorted[(size_t)t * 32 * R + r * 32 + lane] = a[r];
+    warp_merge_desc<R>(a, b);
+#pragma unroll
+    for (int r = 0; r < R; ++r) out_merged[(size_t)t * 32 * R + r * 32 + lane] = a[r];
+}
+#endif
+
+// Moves the selected entries of (k, t)[0..n) to the front, in order; returns the count.
+__device__ __forceinline__ int warp_compact_selected(uint32_t* k, uint32_t* t, int n, const SelectOut& s) {
+    const int lane = threadIdx.x & 31;
+    int out = 0;
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        uint32_t kk = 0u, tt = 0u;
+        bool sel = false;
+        if (i < n) {
+            kk = k[i];
+            tt = t[i];
+            sel = selected(kk, tt, s);
+        }
+        const unsigned m = __ballot_sync(FULL, sel);
+        __syncwarp();
+        if (sel) {
+            const int pos = out + __popc(m & lanemask_lt());
+            k[pos] = kk;
+            t[pos] = tt;
+        }
+        out += __popc(m);
+        __syncwarp();
+    }
+    return out;
+}
+
+__device__ __forceinline__ uint32_t warp_min_u32(uint32_t v) { return __reduce_min_sync(FULL, v); }
+__device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) { return __reduce_max_sync(FULL, v); }
+
+// ---------------------------------------------------------------------------------
+// Stream stage 1 for top_k <= kWarpMaxK (persistent; one CTA per SM).
+// Work item = (row, span of span_elems elements). Warp w of the CTA streams the
+// contiguous sub-range [w*SW, (w+1)*SW) of the span (SW = span_elems / 8) through its
+// own ring of TMA slices (kSlice elements each), so warps never wait on one another
+// and each ring keeps loading the next items while the warp computes. Each warp keeps
+// a running top-K of its own stream: its first slice sets a threshold by binary search
+// over the lanes' top-M keys (a lower bound on that slice's K-th key); later slices are
+// filtered strictly against the warp's K-th key (its stream is in index order), the
+// survivors are buffered and merged with a warp-level select when the buffer fills.
+// At the end of an item warp 0 merges the 8 warp lists and publishes the span's top-K.
+// ---------------------------------------------------------------------------------
+constexpr int kWarpMaxK = 128;
+constexpr int kSlice = 512;     // elements per ring slot (16 per lane)
+constexpr int kWarpBuf = 576;   // candidate room per warp beyond its list
+template <typename T>
+__host__ __device__ constexpr int ring_slots() { return sizeof(T) == 4 ? 8 : 16; }
+// Per-warp shared-memory area in 32-bit words, rounded to 128 bytes so that every
+// warp's ring slots stay 16-byte aligned (TMA destinations, 128-bit loads).
+__host__ __device__ constexpr int warp_area_words(int K, int slots, int esz) {
+    return ((slots * kSlice * esz) / 4 + 2 * slots + 2 * (K + kWarpBuf) + kHistBins + kSlice / 32 + 31) & ~31;
+}
+
+struct VirtListSrc {  // the 8 warp lists as one index space: i -> (warp i / K, entry i % K)
+    const uint32_t* base;
+    int stride_words;
+    int K;
+    int cap;
+    const int* cnt;
+    __device__ __forceinline__ uint32_t key(int i) const {
+        const int w = i / K, j = i - w * K;
+        return j < cnt[w] ? base[(size_t)w * stride_words + j] : 0u;
+    }
+    __device__ __forceinline__ uint32_t tb(int i) const {
+        const int w = i / K, j = i - w * K;
+        return base[(size_t)w * stride_words + cap + j];
+    }
+};
+
+template <int M>
+__device__ __forceinline__ uint32_t warp_kth_lower_bound(const uint32_t (&keys)[16], int K) {
+    uint32_t top[M];
+#pragma unroll
+    for (int m = 0; m < M; ++m) top[m] = 0u;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        uint32_t k = keys[e];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+            const uint32_t hi = max(top[m], k);
+            k = min(top[m], k);
+            top[m] = hi;
+        }
+    }
+    int c1 = 0;
+#pragma unroll
+    for (int m = 0; m < M; ++m) c1 += top[m] != 0u;
+    if ((int)__reduce_add_sync(FULL, (uint32_t)c1) < K) return 0u;
+    // Largest t with at least K of the lanes' top-M keys >= t.
+    uint32_t lo = 1u, hi = __reduce_max_sync(FULL, top[0]);
+    while (lo < hi) {
+        const uint32_t mid = lo + ((hi - lo + 1u) >> 1);
+        int c = 0;
+#pragma unroll
+        for (int m = 0; m < M; ++m) c += top[m] >= mid;
+        if ((int)__reduce_add_sync(FULL, (uint32_t)c) >= K) lo = mid;
+        else hi = mid - 1u;
+    }
+    return lo;
+}
+
+// Per-warp area (32-bit words) of topk_net_kernel, rounded to 128 bytes.
+template <typename T>
+__host__ __device__ constexpr int net_ring_slots() { return sizeof(T) == 4 ? 4 : 8; }
+__host__ __device__ constexpr int net_area_words(int R, int slots, int esz) {
+    return ((slots * kSlice * esz) / 4 + 2 * slots + 64 * R + kSlice / 32 + 31) & ~31;
+}
+
+// Stream stage 1 on register-resident sorted lists (top_k <= 32*R, R <= 4).
+// Persistent CTAs (two per SM), 8 warps each. Work item = (row, span); warp w streams
+// the contiguous sub-range [w*SW, (w+1)*SW) of the span through its own ring of TMA
+// slices. Each warp keeps the 32*R best (key, index) composites of its stream sorted
+// in registers; candidates that beat the warp's K-th key are batched in shared memory
+// and merged with a bitonic network once the batch holds 32*R entries. The first
+// slice of an item is filtered against a lower bound on its K-th key (binary search
+// over the lanes' top-M keys). At the end of an item warp 0 merges the 8 lists.
+// Merges a warp's candidate batch (bcount entries of buf) into its sorted list, then
+// refreshes its K-th key `tau` and the largest dropped key `max_cut`.
+template <int R>
+__device__ __forceinline__ void net_merge_batch(uint64_t (&lst)[R], const uint64_t* buf, int& bcount, int K,
+                                                uint32_t& tau, uint32_t& max_cut) {
+    const int lane = threadIdx.x & 31;
+    VDXS_T0(t_mg);
+    uint64_t bv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int i = r * 32 + lane;
+        bv[r] = i < bcount ? buf[i] : 0ull;
+    }
+    warp_sort_desc<R>(bv);
+    const uint64_t dropped = warp_merge_desc<R>(lst, bv);
+    max_cut = max(max_cut, (uint32_t)(dropped >> 32));
+    bcount = 0;
+    const uint64_t kth = warp_elem<R>(lst, K - 1);
+    tau = max(tau, (uint32_t)(kth >> 32));
+    __syncwarp();
+    VDXS_T1(11, t_mg);
+}
+
+template <int M>
+__device__ __forceinline__ uint32_t warp_kth_lower_bound_f(const float (&x)[16], int K) {
+    uint32_t keys[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) keys[e] = x[e] == x[e] ? f2key(x[e]) : 0u;  // NaN marks an empty slot
+    return warp_kth_lower_bound<M>(keys, K);
+}
+
+template <typename T, bool TMA, int R, int M>
+__global__ void __launch_bounds__(NT, 2) topk_net_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* sh = (uint32_t*)smem_raw + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    constexpr int RS = net_ring_slots<T>();
+    constexpr int VN = TMA ? (int)(16 / sizeof(T)) : 1;
+    constexpr int NB = 32 * R;  // list and batch length
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K;
+    const int WW = net_area_words(R, RS, (int)sizeof(T));
+    uint32_t* wa = (uint32_t*)region + (size_t)warp * WW;
+    T* ring = (T*)wa;
+    uint64_t* full = (uint64_t*)(wa + (RS * kSlice * (int)sizeof(T)) / 4);
+    uint64_t* buf = full + RS;
+    uint32_t* wbm = (uint32_t*)(buf + NB);
+    uint64_t* lists = (uint64_t*)((uint32_t*)region + (size_t)NWARPS * WW);  // [8][NB]
+    uint32_t* s_cut = sh + 24;
+    // CTA threshold: the largest of the warps' K-th keys for the current item. Every
+    // warp list holds K elements at or above its K-th key, so the item's K-th key is at
+    // least this; warps filter against it non-strictly.
+    volatile uint32_t* s_tau = sh + 20;
+    const int nsp = p.nchunks;
+    const int SPAN = p.chunk;
+    const int SW = SPAN / NWARPS;
+    const int items = p.B * nsp;
+    const float NANF = __uint_as_float(0x7FC00000u);
+    if (tid == 0) sh[20] = 0u;
+    __syncthreads();
+
+    // Producer cursor (lane 0): the warp's slices of its items, in consumption order.
+    int pi = blockIdx.x - (int)gridDim.x, pq = 0, pns = 0;
+    int64_t pleft = 0;
+    const T* psrc = nullptr;
+    uint32_t pn = 0;
+    auto next_item = [&]() {
+        for (;;) {
+            pi += gridDim.x;
+            if (pi >= items) return;
+            const int bb = pi / nsp, sp0 = pi - bb * nsp;
+            const int64_t a = (int64_t)sp0 * SPAN + (int64_t)warp * SW;
+            const int64_t e = min(a + SW, (int64_t)p.V);
+            if (e > a) {
+                pleft = e - a;
+                pns = (int)((pleft + kSlice - 1) / kSlice);
+                psrc = (const T*)p.logits + (int64_t)bb * p.stride + a;
+                pq = 0;
+                return;
+            }
+        }
+    };
+    auto issue = [&]() {
+        if (pq >= pns) next_item();
+        if (pi >= items) return;
+        const int nn = (int)min((int64_t)kSlice, pleft - (int64_t)pq * kSlice);
+        const int slot = (int)(pn % RS);
+        const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
+        if (bytes) {
+            mbar_arrive_expect_tx(&full[slot], bytes);
+            tma_load_1d(ring + (size_t)slot * kSlice, psrc + (int64_t)pq * kSlice, bytes, &full[slot]);
+        } else {
+            mbar_arrive(&full[slot]);
+        }
+        ++pn;
+        ++pq;
+    };
+    if constexpr (TMA) {
+        if (lane == 0) {
+            for (int s = 0; s < RS; ++s) mbar_init(&full[s], 1);
+            fence_mbar_init();
+            for (int s = 0; s < RS; ++s) issue();
+        }
+        __syncwarp();
+    }
+
+    uint32_t cn = 0;
+    bool timed_out = false;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int b = item / nsp, spn = item - b * nsp;
+        const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+        const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+        const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+        const int64_t a0 = (int64_t)spn * SPAN + (int64_t)warp * SW;
+        const int64_t a1 = min(a0 + SW, (int64_t)p.V);
+        const int ns = a1 > a0 ? (int)((a1 - a0 + kSlice - 1) / kSlice) : 0;
+        uint64_t lst[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) lst[r] = 0ull;
+        int bcount = 0, pj = 0;
+        uint32_t tau = 0u, max_cut = 0u;
+        float tauf = -INFINITY;  // candidates satisfy x >= tauf
+        if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
+        VDXS_T0(t_item);
+
+        uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
+        uint32_t rtau_next = ld_relaxed_u32(rtp);
+        for (int q = 0; q < ns; ++q) {
+            const int64_t start = a0 + (int64_t)q * kSlice;
+            const int n = (int)min((int64_t)kSlice, a1 - start);
+            // The row bound is fetched one slice ahead so its L2 latency is hidden.
+            const uint32_t rtau = rtau_next;
+            rtau_next = ld_relaxed_u32(rtp);
+            float x[16];
+            if constexpr (TMA) {
+                const int slot = (int)(cn % RS);
+                if (!mbar_wait_bounded(&full[slot], (cn / RS) & 1u)) timed_out = true;
+                const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
+                const T* sl = ring + (size_t)slot * kSlice;
+#pragma unroll
+                for (int j = 0; j < 16 / VN; ++j) {
+                    const int pos = (j * 32 + lane) * VN;
+                    if (pos + VN <= n_tma) {
+                        unpack(*reinterpret_cast<const uint4*>(sl + pos), &x[j * VN], T());
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < VN; ++e) {
+                            const int i = pos + e;
+                            x[j * VN + e] = i < n ? (i < n_tma ? to_f(sl[i]) : ld_elem(row, start + i)) : NANF;
+                        }
+                    }
+                }
+                __syncwarp();
+                ++cn;
+                if (lane == 0) issue();  // refill the slot just read
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int pos = e * 32 + lane;
+                    x[e] = pos < n ? ld_elem(row, start + pos) : NANF;
+                }
+            }
+            if (npen > 0) {
+                // Penalised history ids are excluded here (they re-enter in stage 2).
+                if (lane < kSlice / 32) wbm[lane] = 0u;
+                __syncwarp();
+                for (;;) {
+                    const int j = pj + lane;
+                    const bool in = j < npen && pid[j] < start + n;
+                    if (in) {
+                        const int d = (int)(pid[j] - start);
+                        atomicOr(&wbm[d >> 5], 1u << (d & 31));
+                    }
+                    const unsigned m = __ballot_sync(FULL, in);
+                    pj += __popc(m);
+                    if (m != FULL) break;
+                }
+                __syncwarp();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                    if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
+                }
+            }
+            if (q == 0) {
+                // Lower bound on this slice's K-th key from the lanes' top-M keys.
+                tau = warp_kth_lower_bound_f<M>(x, K);
+                tauf = tau ? key2f(tau) : -INFINITY;
+                if (lane == 0 && tau) {
+                    atomicMax((uint32_t*)s_tau, tau);
+                    atomicMax(rtp, tau);
+                }
+            }
+            // Threshold: the warp's own K-th key, the CTA's and the row's (all lower bounds).
+            const uint32_t tg = max(*s_tau, rtau);
+            float thr = tg > tau ? key2f(tg) : tauf;
+            float lmax = x[0];
+#pragma unroll
+            for (int e = 1; e < 16; ++e) lmax = fmaxf(lmax, x[e]);  // NaN slots are ignored
+            if (!__any_sync(FULL, lmax >= thr)) continue;
+            const uint32_t gb = (uint32_t)(p.vocab_offset + start);
+            // Append the passing elements to the batch; when the batch would overflow,
+            // stop, merge (one copy of the network), tighten the threshold and resume.
+            // The filter is non-strict, so elements equal to a threshold always reach a
+            // merge, which orders them by (key, index) and records what it drops.
+            int e0 = 0;
+            for (;;) {
+                int stop = 16;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                    const bool pass = e >= e0 && x[e] >= thr;
+                    const unsigned m = __ballot_sync(FULL, pass);
+                    if (m == 0u) continue;
+                    if (bcount + __popc(m) > NB) {
+                        stop = e;
+                        break;
+                    }
+                    if (pass) buf[bcount + __popc(m & lanemask_lt())] = comp_key(f2key(x[e]), gb + (uint32_t)pos);
+                    bcount += __popc(m);
+                }
+                if (stop == 16) break;
+                __syncwarp();
+                net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
+                const uint32_t kk = (uint32_t)(warp_elem<R>(lst, K - 1) >> 32);
+                if (kk) {
+                    thr = fmaxf(thr, key2f(kk));
+                    tauf = fmaxf(tauf, key2f(kk));
+                    if (lane == 0) {
+                        atomicMax((uint32_t*)s_tau, kk);
+                        atomicMax(rtp, kk);
+                    }
+                }
+                e0 = stop;
+            }
+            __syncwarp();
+        }
+        if (bcount > 0) {
+            net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
+            const uint64_t kth = warp_elem<R>(lst, K - 1);
+            if (kth && lane == 0) atomicMax(rtp, (uint32_t)(kth >> 32));
+        }
+        VDXS_T1(10, t_item);
+        // Entries past the K-th are cut when the list is published.
+        if (K < NB) max_cut = max(max_cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
+#pragma unroll
+        for (int r = 0; r < R; ++r) lists[(size_t)warp * NB + r * 32 + lane] = lst[r];
+        if (lane == 0) s_cut[warp] = max_cut;
+        __syncthreads();
+        VDXS_T0(t_cm);
+        if (warp == 0) {
+            uint32_t cut = s_cut[0];
+#pragma unroll 1
+            for (int w = 1; w < NWARPS; ++w) {
+                uint64_t bv[R];
+#pragma unroll
+                for (int r = 0; r < R; ++r) bv[r] = lists[(size_t)w * NB + r * 32 + lane];
+                cut = max(cut, s_cut[w]);
+                const uint64_t dropped = warp_merge_desc<R>(lst, bv);
+                cut = max(cut, (uint32_t)(dropped >> 32));
+            }
+            if (K < NB) cut = max(cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
+            const uint64_t kth = warp_elem<R>(lst, K - 1);
+            const uint32_t kk = (uint32_t)(kth >> 32);
+            uint2* out = p.cand + ((int64_t)b * nsp + spn) * K;
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+                const int i = r * 32 + lane;
+                if (i < K) {
+                    const uint64_t v = lst[r];
+                    out[i] = v ? make_uint2((uint32_t)(v >> 32), ~(uint32_t)v) : make_uint2(0u, 0xFFFFFFFFu);
+                }
+            }
+            if (lane == 0) {
+                p.chunk_info[(int64_t)b * nsp + spn] = make_uint2(kk, (kk != 0u && cut == kk) ? 1u : 0u);
+                *s_tau = 0u;  // next item
+            }
+        }
+        __syncthreads();
+        VDXS_T1(13, t_cm);
+    }
+    if (__any_sync(FULL, timed_out) && lane == 0) atomicExch(p.err, kErrTimeout);
+    if constexpr (TMA) {
+        __syncwarp();
+        if (lane == 0)
+            for (int s = 0; s < RS; ++s) mbar_inval(&full[s]);
+    }
+}
+
+// Stage 2 as its own kernel (one CTA per row) after topk_stream_kernel.
+template <typename T>
+__global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    VDXS_T0(t_fin);
+    finish_row<T>(p, blockIdx.x, region, hist, sh);
+    if (threadIdx.x == 0 && p.row_tau) p.row_tau[(size_t)blockIdx.x * kTauStride] = 0u;  // ready for the next launch
+    VDXS_T1(5, t_fin);
+}
+
 template <typename T, int E, int M, bool TMA>
 __global__ void __launch_bounds__(NT) topk_span_kernel(KParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -1675,6 +2402,38 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     const int64_t V = a.V;
     const int pen_stride = a.penalty_on ? (int)std::min<int64_t>(a.hist_stride, kMaxHistory) : 0;
     const size_t esz = a.dtype == VDXS_DTYPE_BF16 ? 2 : 4;
+    const bool faithful = a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit;
+    if (K <= kWarpMaxK) {
+        // Stream path: persistent stage 1 (two CTAs per SM) + one finish CTA per row.
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        constexpr int unit = NWARPS * kSlice;  // 4096
+        const int64_t units = (V + unit - 1) / unit;
+        const int64_t want = std::max<int64_t>(1, ((int64_t)sms * 8 + a.B - 1) / a.B);
+        int nsp = (int)std::min<int64_t>(units, want);
+        const int64_t span = (units + nsp - 1) / nsp * unit;
+        nsp = (int)((V + span - 1) / span);
+        const int R = K <= 32 ? 1 : (K <= 64 ? 2 : 4);
+        const int rs = esz == 4 ? net_ring_slots<float>() : net_ring_slots<uint16_t>();
+        const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(R, rs, (int)esz) + (size_t)NWARPS * 32 * R * 8;
+        size_t s2 = std::max(stage2_bytes(K, nsp * K + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
+        s2 += kHeadBytes;
+        if ((int64_t)s1 > smem_optin || (int64_t)s2 > smem_optin) {
+            if (err) *err = "shared-memory plan exceeds the device limit";
+            return cudaErrorInvalidValue;
+        }
+        plan->chunk = (int)span;
+        plan->nchunks = nsp;
+        plan->nspans = nsp;
+        plan->span = 1;
+        plan->elems = R;
+        plan->stream = true;
+        plan->grid = (int)std::min<int64_t>((int64_t)a.B * nsp, (int64_t)sms * 2);
+        plan->smem = align16(s1);
+        plan->smem2 = align16(s2);
+        return cudaSuccess;
+    }
     const int nst = esz == 4 ? stage_count<float>() : stage_count<uint16_t>();
     // Enough CTAs for several waves at two resident CTAs per SM; otherwise long spans,
     // so that each CTA filters most elements against an established K-th key.
@@ -1689,8 +2448,7 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         const size_t s1 = (size_t)nst * CH * esz + 8 * (size_t)nst + (size_t)16 * K + (size_t)8 * (K + CH / 2) +
                           (size_t)CH / 8;
         size_t need = std::max(s1, stage2_bytes(K, nspans * K + pen_stride));
-        if (a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit)
-            need = std::max(need, faithful_bytes(K));
+        if (faithful) need = std::max(need, faithful_bytes(K));
         need += kHeadBytes;
         if ((int64_t)need <= smem_optin) {
             plan->chunk = CH;
@@ -1698,6 +2456,7 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
             plan->span = span;
             plan->nspans = nspans;
             plan->nchunks = nspans;
+            plan->stream = false;
             plan->smem = align16(need);
             return cudaSuccess;
         }
@@ -1752,8 +2511,9 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
         if ((e = cudaMalloc((void**)&ws.err, sizeof(int32_t))) != cudaSuccess) return e;
         if ((e = cudaMemsetAsync(ws.err, 0, sizeof(int32_t), stream)) != cudaSuccess) return e;
     }
-    // Completion counters start at zero and every launch leaves them at zero.
+    // Completion counters and row thresholds start at zero and every launch leaves them at zero.
     if ((e = grow(&ws.row_counter, &ws.row_counter_cap, B, true, stream)) != cudaSuccess) return e;
+    if ((e = grow(&ws.row_tau, &ws.row_tau_cap, B * kTauStride, true, stream)) != cudaSuccess) return e;
     if (a.path != kFull) {
         if ((e = grow(&ws.cand, &ws.cand_cap, B * nch * (size_t)a.K, false, stream)) != cudaSuccess) return e;
         if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, B * nch, false, stream)) != cudaSuccess) return e;
@@ -1824,6 +2584,8 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
     w.err = (int32_t*)take(sizeof(int32_t));
     w.row_counter = (uint32_t*)take(B * sizeof(uint32_t));
     w.row_counter_cap = B;
+    w.row_tau = (uint32_t*)take(B * kTauStride * sizeof(uint32_t));
+    w.row_tau_cap = B * kTauStride;
     if (a.path != kFull) {
         w.cand = (uint2*)take(B * nch * (size_t)a.K * sizeof(uint2));
         w.cand_cap = B * nch * (size_t)a.K;
@@ -1850,6 +2612,7 @@ void free_workspace(Workspace& ws) {
     cudaFree(ws.cand);
     cudaFree(ws.chunk_info);
     cudaFree(ws.row_counter);
+    cudaFree(ws.row_tau);
     cudaFree(ws.pen_ids);
     cudaFree(ws.pen_vals);
     cudaFree(ws.pen_cnt);
@@ -1887,6 +2650,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.cand = ws.cand;
     p.chunk_info = ws.chunk_info;
     p.row_counter = ws.row_counter;
+    p.row_tau = ws.row_tau;
     p.err = ws.err;
     p.fmax = ws.fmax;
     p.fsum = ws.fsum;
@@ -1936,6 +2700,26 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
     }
     const size_t esz = sizeof(T);
     const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0);
+    if (plan.stream) {
+        void (*k1)(KParams) = nullptr;
+        const int R = plan.elems;
+        const int M = 2 * ((a.K + 31) / 32);
+#define VDXS_NET(R_, M_) k1 = vec ? topk_net_kernel<T, true, R_, M_> : topk_net_kernel<T, false, R_, M_>
+        if (R == 1) VDXS_NET(1, 2);
+        else if (R == 2) VDXS_NET(2, 4);
+        else VDXS_NET(4, 8);
+#undef VDXS_NET
+        (void)M;
+        if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem)) != cudaSuccess)
+            return e;
+        if ((e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)plan.smem2)) != cudaSuccess)
+            return e;
+        k1<<<plan.grid, NT, plan.smem, a.stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        finish_kernel<T><<<a.B, NT, plan.smem2, a.stream>>>(p);
+        return cudaGetLastError();
+    }
     const int M = a.K <= NT ? 1 : 4;
     void (*kern)(KParams) = nullptr;
     if (M == 1) kern = vec ? topk_span_kernel<T, 16, 1, true> : topk_span_kernel<T, 16, 1, false>;
@@ -1971,6 +2755,16 @@ cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std
 }  // namespace vdxs
 
 #ifdef VDXS_TIMING
+extern "C" __attribute__((visibility("default"))) int vdxs_debug_network_selftest(int R, const uint64_t* d_in,
+                                                                                     uint64_t* d_sorted,
+                                                                                     uint64_t* d_merged, int n) {
+    const int blocks = (n + 7) / 8;
+    if (R == 1) vdxs::warp_network_selftest<1><<<blocks, 256>>>(d_in, d_sorted, d_merged, n);
+    else if (R == 2) vdxs::warp_network_selftest<2><<<blocks, 256>>>(d_in, d_sorted, d_merged, n);
+    else if (R == 4) vdxs::warp_network_selftest<4><<<blocks, 256>>>(d_in, d_sorted, d_merged, n);
+    else return -1;
+    return cudaDeviceSynchronize() == cudaSuccess ? 0 : -2;
+}
 extern "C" __attribute__((visibility("default"))) int vdxs_debug_phase_times(unsigned long long* cycles,
                                                                                 unsigned long long* counts,
                                                                                 int reset) {
