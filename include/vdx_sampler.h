@@ -258,6 +258,29 @@ VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm,
                                      const float* d_uniform, int32_t* d_out_tokens,
                                      uint32_t* d_out_flags, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Status and diagnostics. None of these has a counterpart in the reference, whose
+ * Process runs on the host and cannot fail (Sampler.pas:265-528).
+ * ---------------------------------------------------------------------------- */
+
+/* Waits for `stream` and reads the context's device error word, which the kernels
+ * set instead of trapping when a bounded wait gives up (VDXS_E_TIMEOUT) or an
+ * internal selection check fails (VDXS_E_DEVICE_STATE). A non-zero word means the
+ * tokens of the calls since the last check may be wrong; the word and the kernels'
+ * self-resetting counters are cleared before returning, so the context stays usable.
+ * vdxs_sample_host and vdxs_sampler_process* perform this check themselves. */
+VDXS_API int32_t vdxs_device_status(vdxs_context* ctx, void* stream);
+
+/* Profiling hook: while set, every sampling call on `ctx` records `ev_begin`
+ * (a cudaEvent_t created on the context's device) on the call's stream immediately
+ * before its dominant pass over the logits and `ev_end` immediately after it, so
+ * the caller can time that kernel alone. Pass NULL, NULL to stop. */
+VDXS_API int32_t vdxs_set_stage_events(vdxs_context* ctx, void* ev_begin, void* ev_end);
+
+/* Number of kernels launched by the library for calls on `ctx` since it was
+ * created (NCCL's own kernels are not counted). */
+VDXS_API int32_t vdxs_get_launch_count(const vdxs_context* ctx, int64_t* out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,12 @@ def test_edge_cases(gpu_ctx, oracle_mod, mode):
     b = np.arange(V, dtype=np.float32)[None, :].repeat(2, 0) * 0.001
     cases.append(("increasing", b))
     cases.append(("decreasing", b[:, ::-1].copy()))
+    # Distinct values that all share one 12-bit key prefix (one threshold-histogram bin),
+    # in order and shuffled: every element passes the bin threshold, so the candidate
+    # buffer overflows into the exact per-warp lists.
+    d = (1.0 + np.arange(V, dtype=np.float64) * 2.0 ** -22).astype(np.float32)[None, :].repeat(2, 0)
+    cases.append(("one_bin_sorted", d))
+    cases.append(("one_bin_shuffled", np.random.default_rng(11).permuted(d, axis=1)))
     for name, x in cases:
         for cfg in [default_config(temperature=1.0, top_k=5), default_config(temperature=1.0, top_k=5, top_p=0.5),
                     default_config(temperature=0.0), default_config(temperature=2.0, top_k=100, top_p=0.9),

@@ -49,6 +49,9 @@ SIGNATURES = {
     "vdxs_comm_destroy": (i32, [vp]),
     "vdxs_sample_sharded": (i32, [vp, vp, P(VdxsConfig), vp, i32, i32, i32, i64, i64, i64, vp, i64, vp,
                                   vp, vp, vp, vp]),
+    "vdxs_device_status": (i32, [vp, vp]),
+    "vdxs_set_stage_events": (i32, [vp, vp, vp]),
+    "vdxs_get_launch_count": (i32, [vp, P(i64)]),
 }
 
 

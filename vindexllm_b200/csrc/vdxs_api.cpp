@@ -29,6 +29,9 @@ struct vdxs_context {
     int tie_mode = VDXS_TIES_FAITHFUL;
     Workspace ws;
     std::string last_error;
+    cudaEvent_t ev_begin = nullptr;  // profiling hook (vdxs_set_stage_events)
+    cudaEvent_t ev_end = nullptr;
+    int64_t launches = 0;            // kernels launched for this context
 };
 
 namespace {
@@ -143,6 +146,26 @@ cudaError_t grow_dev(P** ptr, size_t* cap, size_t want, cudaStream_t stream) {
     return cudaSuccess;
 }
 
+// Maps a non-zero device error word to a status; clears the word and the kernels'
+// self-resetting counters so the next call starts clean.
+int32_t device_word_status(vdxs_context* ctx, int32_t word, cudaStream_t stream) {
+    if (word == 0) return VDXS_OK;
+    reset_device_state(ctx->ws, stream);
+    cudaStreamSynchronize(stream);
+    if (word == 3)
+        return fail(ctx, VDXS_E_TIMEOUT, "a bounded device wait gave up (tensor-memory copy did not complete); "
+                                         "the tokens of the affected call are not valid");
+    return fail(ctx, VDXS_E_DEVICE_STATE, "device selection check failed (code %d); the tokens of the affected "
+                                          "call are not valid", word);
+}
+
+// Fills the diagnostics part of SampleArgs from the context.
+void attach_diagnostics(vdxs_context* ctx, SampleArgs* a) {
+    a->ev_begin = ctx->ev_begin;
+    a->ev_end = ctx->ev_end;
+    a->launches = &ctx->launches;
+}
+
 }  // namespace
 
 extern "C" {
@@ -243,6 +266,7 @@ VDXS_API int32_t vdxs_sample_ex(vdxs_context* ctx, const vdxs_config* cfg, const
     a.tie_mode = ctx->tie_mode;
     a.vocab_total = vocab;
     a.stream = (cudaStream_t)stream;
+    attach_diagnostics(ctx, &a);
 
     DeviceGuard g(ctx->device);
     LaunchPlan plan;
@@ -306,7 +330,7 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg, con
         if ((e = grow_dev(&ws.d_unif, &c1, (size_t)batch, st)) != cudaSuccess ||
             (e = grow_dev(&ws.d_tok, &c2, (size_t)batch, st)) != cudaSuccess ||
             (e = grow_dev(&ws.d_hcnt, &c3, (size_t)batch, st)) != cudaSuccess ||
-            (e = cudaMallocHost((void**)&ws.h_tok_pinned, sizeof(int32_t) * batch)) != cudaSuccess)
+            (e = cudaMallocHost((void**)&ws.h_tok_pinned, sizeof(int32_t) * (batch + 1))) != cudaSuccess)
             return cuda_fail(ctx, e, "staging allocation");
         ws.d_rows_cap = batch;
     }
@@ -333,9 +357,12 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg, con
                      cfg->temperature != 0.0f ? ws.d_unif : nullptr, ws.d_tok, stream);
     if (rc != VDXS_OK) return rc;
     if ((e = cudaMemcpyAsync(ws.h_tok_pinned, ws.d_tok, sizeof(int32_t) * batch, cudaMemcpyDeviceToHost, st)) !=
-        cudaSuccess)
+            cudaSuccess ||
+        (e = cudaMemcpyAsync(ws.h_tok_pinned + batch, ws.err, sizeof(int32_t), cudaMemcpyDeviceToHost, st)) !=
+            cudaSuccess)
         return cuda_fail(ctx, e, "token download");
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
+    if ((rc = device_word_status(ctx, ws.h_tok_pinned[batch], st)) != VDXS_OK) return rc;
     std::memcpy(h_out_tokens, ws.h_tok_pinned, sizeof(int32_t) * batch);
     ok(ctx);
     return VDXS_OK;
@@ -399,6 +426,40 @@ VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, c
         return cuda_fail(nullptr, e, "scratch reset");
     if ((e = launch_sample(a, plan, ws, &msg)) != cudaSuccess) return cuda_fail(nullptr, e, "kernel launch");
     ok(nullptr);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_device_status(vdxs_context* ctx, void* stream) {
+    if (!ctx) return fail(nullptr, VDXS_E_INVALID_ARG, "context is NULL");
+    DeviceGuard g(ctx->device);
+    cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "stream synchronize");
+    if (!ctx->ws.err) {
+        ok(ctx);
+        return VDXS_OK;
+    }
+    int32_t word = 0;
+    if ((e = cudaMemcpy(&word, ctx->ws.err, sizeof(int32_t), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(ctx, e, "error word download");
+    int32_t rc = device_word_status(ctx, word, st);
+    if (rc == VDXS_OK) ok(ctx);
+    return rc;
+}
+
+VDXS_API int32_t vdxs_set_stage_events(vdxs_context* ctx, void* ev_begin, void* ev_end) {
+    if (!ctx) return fail(nullptr, VDXS_E_INVALID_ARG, "context is NULL");
+    if ((ev_begin == nullptr) != (ev_end == nullptr))
+        return fail(ctx, VDXS_E_INVALID_ARG, "give both events or neither");
+    ctx->ev_begin = (cudaEvent_t)ev_begin;
+    ctx->ev_end = (cudaEvent_t)ev_end;
+    ok(ctx);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_get_launch_count(const vdxs_context* ctx, int64_t* out) {
+    if (!ctx || !out) return fail(nullptr, VDXS_E_INVALID_ARG, "NULL argument");
+    *out = ctx->launches;
     return VDXS_OK;
 }
 
@@ -531,9 +592,12 @@ int32_t sampler_run(vdxs_sampler* s, const void* d_logits, int32_t dtype, int32_
                      greedy ? nullptr : s->d_unif, s->d_tok, st);
     if (rc != VDXS_OK) return rc;
     if ((e = cudaMemcpyAsync(s->h_tok, s->d_tok, sizeof(int32_t) * s->batch, cudaMemcpyDeviceToHost, st)) !=
-        cudaSuccess)
+            cudaSuccess ||
+        (e = cudaMemcpyAsync(s->h_tok + s->batch, s->ctx->ws.err, sizeof(int32_t), cudaMemcpyDeviceToHost, st)) !=
+            cudaSuccess)
         return cuda_fail(s->ctx, e, "token download");
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(s->ctx, e, "stream synchronize");
+    if ((rc = device_word_status(s->ctx, s->h_tok[s->batch], st)) != VDXS_OK) return rc;
     std::memcpy(h_out, s->h_tok, sizeof(int32_t) * s->batch);
     ok(s->ctx);
     return VDXS_OK;
@@ -562,7 +626,7 @@ VDXS_API int32_t vdxs_sampler_create(vdxs_context* ctx, int32_t batch, vdxs_samp
         (e = cudaMalloc((void**)&s->d_unif, sizeof(float) * batch)) != cudaSuccess ||
         (e = cudaMalloc((void**)&s->d_tok, sizeof(int32_t) * batch)) != cudaSuccess ||
         (e = cudaMallocHost((void**)&s->h_unif, sizeof(float) * batch)) != cudaSuccess ||
-        (e = cudaMallocHost((void**)&s->h_tok, sizeof(int32_t) * batch)) != cudaSuccess ||
+        (e = cudaMallocHost((void**)&s->h_tok, sizeof(int32_t) * (batch + 1))) != cudaSuccess ||
         (e = cudaMallocHost((void**)&s->h_hcnt, sizeof(int32_t) * batch)) != cudaSuccess) {
         vdxs_sampler_destroy(s);
         return cuda_fail(ctx, e, "sampler allocation");
@@ -840,6 +904,7 @@ VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm, const v
     a.vocab_total = vocab_total;
     a.local_emit = true;
     a.stream = (cudaStream_t)stream;
+    attach_diagnostics(ctx, &a);
     DeviceGuard g(ctx->device);
     LaunchPlan plan;
     std::string msg;

@@ -20,7 +20,7 @@ enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
 // Device workspace owned by a context (TVdxSampler.EnsureWorkspace analogue,
 // Sampler.pas:250-263). Grown on demand; never shrunk until the context dies.
 struct Workspace {
-    uint2* cand = nullptr;          // [rows * nchunks * K] stage-1 (key, index) candidates
+    uint2* cand = nullptr;          // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
     size_t cand_cap = 0;            // elements
     uint2* chunk_info = nullptr;    // [rows * nchunks] (chunk k-th key, tie-cut flag)
     size_t chunk_info_cap = 0;
@@ -82,6 +82,10 @@ struct SampleArgs {
     int64_t vocab_total = 0;
     bool local_emit = false;         // emit local top-K candidates instead of drawing
     cudaStream_t stream = nullptr;
+    // diagnostics
+    cudaEvent_t ev_begin = nullptr;  // recorded just before the dominant pass
+    cudaEvent_t ev_end = nullptr;    // recorded just after it
+    int64_t* launches = nullptr;     // incremented per kernel launch
 };
 
 struct LaunchPlan {
@@ -92,6 +96,7 @@ struct LaunchPlan {
     int elems = 32;   // keys per thread per chunk
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
     int grid = 0;         // stream kernel grid (CTAs)
+    int cand_cap = 0;     // top-k path: candidates each stage-1 item may write
     size_t smem = 0;
     size_t smem2 = 0;     // finish kernel shared memory
 };
@@ -106,6 +111,8 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
 cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err);
 cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std::string* err);
 void free_workspace(Workspace& ws);
+// Clears the device error word and the self-resetting counters (after a failed launch).
+cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream);
 
 // Fixed device scratch used by vdxs_sample_noalloc (no allocation on any call).
 constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;

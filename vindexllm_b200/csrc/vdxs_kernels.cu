@@ -81,8 +81,9 @@ struct KParams {
     const int32_t* pen_cnt;
     int pen_stride;
     // workspace
-    uint2* cand;
-    uint2* chunk_info;
+    uint2* cand;        // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
+    int cand_cap;       // candidates each stage-1 item may write
+    uint2* chunk_info;  // [rows * nchunks] (candidate count, largest key dropped by an exact cut)
     uint32_t* row_counter;
     uint32_t* row_tau;  // stream path: per-row lower bound on the K-th key (reset by finish)
     int32_t* err;
@@ -1068,16 +1069,33 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     uint32_t* sk = (uint32_t*)region;
     uint32_t* si = sk + K;
     uint32_t* ckey = si + K;
-    const int nc = p.nchunks * K;  // nchunks = spans per row on this path
+    const int nsp = p.nchunks;  // stage-1 items (spans) of this row
+    const int cc = p.cand_cap;
+    uint32_t cnt = 0u;
+    for (int i = tid; i < nsp; i += NT) cnt += min(__ldcg(&p.chunk_info[(int64_t)b * nsp + i].x), (uint32_t)cc);
+    const int nc = (int)block_sum_u32(cnt, sh + 32);
     const int n2 = nc + npen;
     uint32_t* cidx = ckey + n2;
-    const uint2* cb = p.cand + (int64_t)b * nc;
     uint32_t lm = 0u;
-    for (int i = tid; i < nc; i += NT) {
-        const uint2 e = __ldcg(cb + i);
-        ckey[i] = e.x;
-        cidx[i] = e.y;
-        lm = max(lm, e.x);
+    {
+        // Gather the variable-length item lists; warp w takes items w, w+8, ...
+        const int lane = tid & 31;
+        if (tid == 0) sh[40] = 0u;
+        __syncthreads();
+        for (int it = tid >> 5; it < nsp; it += NWARPS) {
+            const int64_t ii = (int64_t)b * nsp + it;
+            const int c = (int)min(__ldcg(&p.chunk_info[ii].x), (uint32_t)cc);
+            uint32_t base = 0u;
+            if (lane == 0) base = atomicAdd(&sh[40], (uint32_t)c);
+            base = __shfl_sync(FULL, base, 0);
+            const uint2* src = p.cand + ii * cc;
+            for (int j = lane; j < c; j += 32) {
+                const uint2 e = __ldcg(src + j);
+                ckey[base + j] = e.x;
+                cidx[base + j] = e.y;
+                lm = max(lm, e.x);
+            }
+        }
     }
     for (int j = tid; j < npen; j += NT) {
         const uint32_t k = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
@@ -1097,7 +1115,7 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     uint32_t ck_tie = 0u;
     for (int i = tid; i < p.nchunks; i += NT) {
         const uint2 ci = __ldcg(p.chunk_info + (int64_t)b * p.nchunks + i);
-        if (ci.y && ci.x == kb) ck_tie = 1u;
+        if (ci.y != 0u && ci.y == kb) ck_tie = 1u;
     }
     ck_tie = block_max_u32(ck_tie, sh + 32);
     const uint32_t btie = (s2.tie_cut || ck_tie) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
@@ -1588,14 +1606,100 @@ __device__ __forceinline__ uint32_t warp_kth_lower_bound_f(const float (&x)[16],
     return warp_kth_lower_bound<M>(keys, K);
 }
 
-template <typename T, bool TMA, int R, int M>
-__global__ void __launch_bounds__(NT, 2) topk_net_kernel(KParams p) {
+// ---------------------------------------------------------------------------------
+// Threshold histogram of the stream kernel. Bins are the top 12 bits of the key (sign,
+// exponent and 3 mantissa bits); groups are the top 6 bits (64 bins each). Every count
+// is of distinct elements of one row, so any bin edge with at least K counted elements
+// at or above it is a lower bound on that row's K-th key.
+// ---------------------------------------------------------------------------------
+constexpr int kTBins = 4096;
+constexpr int kTGroups = 64;
+constexpr int kCandTotal = 2304;  // CTA candidate entries, the warp-list spill area included
+
+__host__ __device__ constexpr int hist_area_words() { return kTBins + kTGroups + 2 * kCandTotal; }
+
+__device__ __forceinline__ void lds_v2_volatile(const uint32_t* a, uint32_t& x, uint32_t& y) {
+    asm volatile("ld.volatile.shared.v2.u32 {%0, %1}, [%2];" : "=r"(x), "=r"(y) : "r"(smem_u32(a)));
+}
+
+// Inclusive suffix sum over lanes: lane l receives the sum of lanes l..31.
+__device__ __forceinline__ uint32_t warp_suffix_sum(uint32_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        const uint32_t o = __shfl_down_sync(FULL, v, d);
+        if (lane + d < 32) v += o;
+    }
+    return v;
+}
+
+// Largest bin lower edge (a key) with at least K counted elements at or above it, or 0.
+// Counts only grow, so reads that race with increments can only make the edge lower.
+__device__ __forceinline__ uint32_t hist_threshold(const uint32_t* H, const uint32_t* G, int K) {
+    const int lane = threadIdx.x & 31;
+    uint32_t g0, g1;
+    lds_v2_volatile(G + 2 * lane, g0, g1);
+    const uint32_t s = warp_suffix_sum(g0 + g1);  // count in groups >= 2*lane
+    const unsigned m0 = __ballot_sync(FULL, s >= (uint32_t)K);
+    if (m0 == 0u) return 0u;
+    const unsigned m1 = __ballot_sync(FULL, s - g0 >= (uint32_t)K);  // groups >= 2*lane+1
+    const int l0 = 31 - __clz((int)m0);
+    const int hi = (int)((m1 >> l0) & 1u);
+    const int grp = 2 * l0 + hi;
+    const uint32_t s_l0 = __shfl_sync(FULL, s, l0);
+    const uint32_t g0_l0 = __shfl_sync(FULL, g0, l0);
+    const uint32_t s_next = __shfl_sync(FULL, s, (l0 + 1) & 31);
+    const uint32_t above = hi ? (l0 < 31 ? s_next : 0u) : s_l0 - g0_l0;  // count in groups > grp
+    uint32_t h0, h1;
+    lds_v2_volatile(H + grp * 64 + 2 * lane, h0, h1);
+    const uint32_t t = warp_suffix_sum(h0 + h1) + above;
+    const unsigned n0 = __ballot_sync(FULL, t >= (uint32_t)K);
+    if (n0 == 0u) return (uint32_t)grp << 26;  // the group count qualified, its bins not yet
+    const unsigned n1 = __ballot_sync(FULL, t - h0 >= (uint32_t)K);
+    const int j0 = 31 - __clz((int)n0);
+    return (uint32_t)(grp * 64 + 2 * j0 + (int)((n1 >> j0) & 1u)) << 20;
+}
+
+// Float threshold for "key >= k". Bin edges below the key of -inf (0x007FFFFF) are
+// NaN bit patterns as floats; every non-NaN value is at or above them.
+__device__ __forceinline__ float key_threshold(uint32_t k) { return k > 0x007FFFFFu ? key2f(k) : -INFINITY; }
+
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Maximum of the 16 register values of a lane (NaN marks an empty slot and is ignored).
+__device__ __forceinline__ float max16(const float (&x)[16]) {
+    const float a = fmax3f(x[0], x[1], x[2]), b = fmax3f(x[3], x[4], x[5]), c = fmax3f(x[6], x[7], x[8]);
+    const float d = fmax3f(x[9], x[10], x[11]), e = fmax3f(x[12], x[13], x[14]);
+    return fmaxf(fmax3f(a, b, c), fmax3f(d, e, x[15]));
+}
+
+// Stream stage 1 for top_k <= 128. Persistent CTAs (two per SM), 8 warps each. Work
+// item = (row, span); warp w streams the contiguous sub-range [w*SW, (w+1)*SW) of the
+// span through its own ring of TMA bulk copies (plain loads when the rows are not
+// 16-byte aligned). Elements at or above the CTA threshold are appended to a shared
+// candidate buffer and counted in the threshold histogram; the threshold is then
+// raised to the histogram's K-th edge and published per row, so every CTA of the row
+// filters against the best bound found so far. The first slice of each warp is counted
+// whole, which starts the threshold near the K-th key of the CTA's first 4096 elements.
+// At the end of an item the candidates at or above the final threshold are written out
+// unsorted (the finish kernel selects); only when more remain than the output holds is
+// an exact top-K taken here. If the buffer fills (e.g. many equal keys), a warp keeps
+// the rest of its candidates in an exact register list (bitonic networks, composite
+// (key, index) order), which also records any key it drops for the tie flags.
+template <typename T, bool TMA, int R>
+__global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint32_t* sh = (uint32_t*)smem_raw + kHistWords;
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
     unsigned char* region = smem_raw + kHeadBytes;
     constexpr int RS = net_ring_slots<T>();
     constexpr int VN = TMA ? (int)(16 / sizeof(T)) : 1;
     constexpr int NB = 32 * R;  // list and batch length
+    constexpr int CAP = kCandTotal - NWARPS * NB;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K;
     const int WW = net_area_words(R, RS, (int)sizeof(T));
@@ -1604,18 +1708,26 @@ __global__ void __launch_bounds__(NT, 2) topk_net_kernel(KParams p) {
     uint64_t* full = (uint64_t*)(wa + (RS * kSlice * (int)sizeof(T)) / 4);
     uint64_t* buf = full + RS;
     uint32_t* wbm = (uint32_t*)(buf + NB);
-    uint64_t* lists = (uint64_t*)((uint32_t*)region + (size_t)NWARPS * WW);  // [8][NB]
-    uint32_t* s_cut = sh + 24;
-    // CTA threshold: the largest of the warps' K-th keys for the current item. Every
-    // warp list holds K elements at or above its K-th key, so the item's K-th key is at
-    // least this; warps filter against it non-strictly.
-    volatile uint32_t* s_tau = sh + 20;
+    uint32_t* H = (uint32_t*)region + (size_t)NWARPS * WW;
+    uint32_t* G = H + kTBins;
+    uint32_t* ckey = G + kTGroups;
+    uint32_t* cidx = ckey + kCandTotal;
+    volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current item
+    uint32_t* s_cnt = sh + 21;         // buffer slots reserved (may pass CAP on a spill)
+    uint32_t* s_ovf = sh + 22;         // some warp spilled to its list
+    uint32_t* s_out = sh + 23;         // output counter
+    uint32_t* s_cut = sh + 24;         // [NWARPS] largest key each warp list dropped
     const int nsp = p.nchunks;
     const int SPAN = p.chunk;
     const int SW = SPAN / NWARPS;
     const int items = p.B * nsp;
     const float NANF = __uint_as_float(0x7FC00000u);
-    if (tid == 0) sh[20] = 0u;
+    for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
+    if (tid == 0) {
+        sh[20] = 0u;
+        sh[21] = 0u;
+        sh[22] = 0u;
+    }
     __syncthreads();
 
     // Producer cursor (lane 0): the warp's slices of its items, in consumption order.
@@ -1678,12 +1790,12 @@ __global__ void __launch_bounds__(NT, 2) topk_net_kernel(KParams p) {
         for (int r = 0; r < R; ++r) lst[r] = 0ull;
         int bcount = 0, pj = 0;
         uint32_t tau = 0u, max_cut = 0u;
-        float tauf = -INFINITY;  // candidates satisfy x >= tauf
+        bool ovf = false;  // warp-uniform: candidates go to the exact list from now on
         if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
-        VDXS_T0(t_item);
-
         uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
         uint32_t rtau_next = ld_relaxed_u32(rtp);
+        VDXS_T0(t_item);
+
         for (int q = 0; q < ns; ++q) {
             const int64_t start = a0 + (int64_t)q * kSlice;
             const int n = (int)min((int64_t)kSlice, a1 - start);
@@ -1741,99 +1853,186 @@ __global__ void __launch_bounds__(NT, 2) topk_net_kernel(KParams p) {
                     if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
                 }
             }
-            if (q == 0) {
-                // Lower bound on this slice's K-th key from the lanes' top-M keys.
-                tau = warp_kth_lower_bound_f<M>(x, K);
-                tauf = tau ? key2f(tau) : -INFINITY;
-                if (lane == 0 && tau) {
-                    atomicMax((uint32_t*)s_tau, tau);
-                    atomicMax(rtp, tau);
-                }
-            }
-            // Threshold: the warp's own K-th key, the CTA's and the row's (all lower bounds).
-            const uint32_t tg = max(*s_tau, rtau);
-            float thr = tg > tau ? key2f(tg) : tauf;
-            float lmax = x[0];
-#pragma unroll
-            for (int e = 1; e < 16; ++e) lmax = fmaxf(lmax, x[e]);  // NaN slots are ignored
-            if (!__any_sync(FULL, lmax >= thr)) continue;
-            const uint32_t gb = (uint32_t)(p.vocab_offset + start);
-            // Append the passing elements to the batch; when the batch would overflow,
-            // stop, merge (one copy of the network), tighten the threshold and resume.
-            // The filter is non-strict, so elements equal to a threshold always reach a
-            // merge, which orders them by (key, index) and records what it drops.
-            int e0 = 0;
-            for (;;) {
-                int stop = 16;
+            const bool counted = q == 0;
+            if (counted) {
+                // Count the whole first slice, then take the threshold it supports.
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                    const bool pass = e >= e0 && x[e] >= thr;
+                    if (x[e] == x[e]) {
+                        const uint32_t k = f2key(x[e]);
+                        atomicAdd(&H[k >> 20], 1u);
+                        atomicAdd(&G[k >> 26], 1u);
+                    }
+                }
+                __syncwarp();
+                const uint32_t t = hist_threshold(H, G, K);
+                if (lane == 0 && t > *s_T) {
+                    atomicMax((uint32_t*)s_T, t);
+                    if (t > rtau) atomicMax(rtp, t);
+                }
+            }
+            // Threshold: the CTA's, the row's and (after a spill) the warp list's K-th key.
+            const uint32_t tg = max(max(*s_T, rtau), tau);
+            float thr = key_threshold(tg);
+            if (!__any_sync(FULL, max16(x) >= thr)) continue;
+            const uint32_t gb = (uint32_t)(p.vocab_offset + start);
+            int e0 = 0;
+            bool added = false;
+            if (!ovf) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const bool pass = x[e] >= thr;
                     const unsigned m = __ballot_sync(FULL, pass);
                     if (m == 0u) continue;
-                    if (bcount + __popc(m) > NB) {
-                        stop = e;
+                    const uint32_t c = (uint32_t)__popc(m);
+                    uint32_t base = 0u;
+                    if (lane == 0) base = atomicAdd(s_cnt, c);
+                    base = __shfl_sync(FULL, base, 0);
+                    if (base + c > (uint32_t)CAP) {
+                        // Buffer full: blank this warp's share of the reservation and spill.
+                        for (uint32_t i = base + lane; i < (uint32_t)CAP; i += 32) ckey[i] = 0u;
+                        ovf = true;
+                        e0 = e;
                         break;
                     }
-                    if (pass) buf[bcount + __popc(m & lanemask_lt())] = comp_key(f2key(x[e]), gb + (uint32_t)pos);
-                    bcount += __popc(m);
-                }
-                if (stop == 16) break;
-                __syncwarp();
-                net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
-                const uint32_t kk = (uint32_t)(warp_elem<R>(lst, K - 1) >> 32);
-                if (kk) {
-                    thr = fmaxf(thr, key2f(kk));
-                    tauf = fmaxf(tauf, key2f(kk));
-                    if (lane == 0) {
-                        atomicMax((uint32_t*)s_tau, kk);
-                        atomicMax(rtp, kk);
+                    if (pass) {
+                        const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                        const uint32_t k = f2key(x[e]);
+                        const uint32_t slot = base + __popc(m & lanemask_lt());
+                        ckey[slot] = k;
+                        cidx[slot] = gb + (uint32_t)pos;
+                        if (!counted) {
+                            atomicAdd(&H[k >> 20], 1u);
+                            atomicAdd(&G[k >> 26], 1u);
+                        }
                     }
+                    added = true;
                 }
-                e0 = stop;
+                if (ovf && lane == 0) atomicExch(s_ovf, 1u);
+            }
+            if (ovf) {
+                // Exact list: append from element e0 on; merge when the batch would
+                // overflow, then tighten the threshold and resume.
+                for (;;) {
+                    int stop = 16;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                        const bool pass = e >= e0 && x[e] >= thr;
+                        const unsigned m = __ballot_sync(FULL, pass);
+                        if (m == 0u) continue;
+                        if (bcount + __popc(m) > NB) {
+                            stop = e;
+                            break;
+                        }
+                        if (pass) buf[bcount + __popc(m & lanemask_lt())] = comp_key(f2key(x[e]), gb + (uint32_t)pos);
+                        bcount += __popc(m);
+                    }
+                    if (stop == 16) break;
+                    __syncwarp();
+                    net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
+                    const uint32_t kk = (uint32_t)(warp_elem<R>(lst, K - 1) >> 32);
+                    if (kk) {
+                        thr = fmaxf(thr, key_threshold(kk));
+                        if (lane == 0) {
+                            atomicMax((uint32_t*)s_T, kk);
+                            atomicMax(rtp, kk);
+                        }
+                    }
+                    e0 = stop;
+                }
+            }
+            if (added) {
+                __syncwarp();
+                const uint32_t t = hist_threshold(H, G, K);
+                if (lane == 0 && t > *s_T) {
+                    atomicMax((uint32_t*)s_T, t);
+                    if (t > rtau) atomicMax(rtp, t);
+                }
             }
             __syncwarp();
         }
-        if (bcount > 0) {
-            net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
-            const uint64_t kth = warp_elem<R>(lst, K - 1);
-            if (kth && lane == 0) atomicMax(rtp, (uint32_t)(kth >> 32));
+        if (ovf) {
+            if (bcount > 0) net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
+            // Entries past the K-th are cut when the list is published.
+            if (K < NB) max_cut = max(max_cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
         }
         VDXS_T1(10, t_item);
-        // Entries past the K-th are cut when the list is published.
-        if (K < NB) max_cut = max(max_cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
-#pragma unroll
-        for (int r = 0; r < R; ++r) lists[(size_t)warp * NB + r * 32 + lane] = lst[r];
-        if (lane == 0) s_cut[warp] = max_cut;
+        if (lane == 0) s_cut[warp] = ovf ? max_cut : 0u;
         __syncthreads();
         VDXS_T0(t_cm);
-        if (warp == 0) {
-            uint32_t cut = s_cut[0];
-#pragma unroll 1
-            for (int w = 1; w < NWARPS; ++w) {
-                uint64_t bv[R];
-#pragma unroll
-                for (int r = 0; r < R; ++r) bv[r] = lists[(size_t)w * NB + r * 32 + lane];
-                cut = max(cut, s_cut[w]);
-                const uint64_t dropped = warp_merge_desc<R>(lst, bv);
-                cut = max(cut, (uint32_t)(dropped >> 32));
-            }
-            if (K < NB) cut = max(cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
-            const uint64_t kth = warp_elem<R>(lst, K - 1);
-            const uint32_t kk = (uint32_t)(kth >> 32);
-            uint2* out = p.cand + ((int64_t)b * nsp + spn) * K;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                const int i = r * 32 + lane;
-                if (i < K) {
-                    const uint64_t v = lst[r];
-                    out[i] = v ? make_uint2((uint32_t)(v >> 32), ~(uint32_t)v) : make_uint2(0u, 0xFFFFFFFFu);
+        if (tid == 0) {
+            sh[19] = max((uint32_t)*s_T, ld_relaxed_u32(rtp));
+            *s_out = 0u;
+        }
+        __syncthreads();
+        // Every candidate at or above the final threshold leaves; anything below it is
+        // below the row's K-th key, so it cannot be selected or tie at the boundary.
+        const uint32_t tfin = sh[19];
+        const bool any_ovf = *s_ovf != 0u;
+        const int nbuf = (int)min(*s_cnt, (uint32_t)CAP);
+        uint2* out = p.cand + (size_t)item * p.cand_cap;
+        bool done = false;
+        if (!any_ovf) {
+            for (int i0 = 0; i0 < nbuf; i0 += NT) {
+                const int i = i0 + tid;
+                uint32_t k = 0u;
+                bool sel = false;
+                if (i < nbuf) {
+                    k = ckey[i];
+                    sel = k != 0u && k >= tfin;
+                }
+                const unsigned m = __ballot_sync(FULL, sel);
+                if (m) {
+                    uint32_t base = 0u;
+                    if (lane == 0) base = atomicAdd(s_out, (uint32_t)__popc(m));
+                    base = __shfl_sync(FULL, base, 0);
+                    const uint32_t slot = base + __popc(m & lanemask_lt());
+                    if (sel && slot < (uint32_t)p.cand_cap) out[slot] = make_uint2(k, cidx[i]);
                 }
             }
-            if (lane == 0) {
-                p.chunk_info[(int64_t)b * nsp + spn] = make_uint2(kk, (kk != 0u && cut == kk) ? 1u : 0u);
-                *s_tau = 0u;  // next item
+            __syncthreads();
+            const uint32_t total = *s_out;
+            if (total <= (uint32_t)p.cand_cap) {
+                if (tid == 0) p.chunk_info[item] = make_uint2(total, 0u);
+                done = true;
             }
+        }
+        if (!done) {
+            // Exact top-K of the buffer (and of the warp lists after a spill).
+            int nin = nbuf;
+            if (any_ovf) {
+#pragma unroll
+                for (int r = 0; r < R; ++r) {
+                    const int i = CAP + warp * NB + r * 32 + lane;
+                    const uint64_t v = lst[r];
+                    ckey[i] = v ? (uint32_t)(v >> 32) : 0u;
+                    cidx[i] = ~(uint32_t)v;
+                }
+                nin = CAP + NWARPS * NB;
+            }
+            __syncthreads();
+            uint32_t km = 0u;
+            for (int i = tid; i < nin; i += NT) km = max(km, ckey[i]);
+            km = block_max_u32(km, sh + 32);
+            const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
+            const SelectOut so = block_select(SmemPairSrc{ckey, cidx}, nin, K, km, tbb, hist, sh);
+            uint32_t* ok = H;
+            uint32_t* oi = H + K;
+            const int m_out = block_emit(SmemPairSrc{ckey, cidx}, nin, so, ok, oi, K, &sh[8], IdentIdx{cidx});
+            for (int j = tid; j < m_out; j += NT) out[j] = make_uint2(ok[j], oi[j]);
+            if (tid == 0) {
+                uint32_t cut = so.tie_cut ? so.kth_key : 0u;
+                for (int w = 0; w < NWARPS; ++w) cut = max(cut, s_cut[w]);
+                p.chunk_info[item] = make_uint2((uint32_t)m_out, cut);
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
+        if (tid == 0) {
+            sh[20] = 0u;
+            sh[21] = 0u;
+            sh[22] = 0u;
         }
         __syncthreads();
         VDXS_T1(13, t_cm);
@@ -2068,10 +2267,9 @@ __global__ void __launch_bounds__(NT) topk_span_kernel(KParams p) {
     }
 
     // Publish the span's list (padded) and its boundary-tie evidence.
-    uint2* out = p.cand + ((int64_t)b * p.nchunks + sp) * K;
-    for (int s = tid; s < K; s += NT) out[s] = s < L ? make_uint2(lk[s], li[s]) : make_uint2(0u, 0xFFFFFFFFu);
-    if (tid == 0)
-        p.chunk_info[(int64_t)b * p.nchunks + sp] = make_uint2(tau, (L == K && max_cut == tau) ? 1u : 0u);
+    uint2* out = p.cand + ((int64_t)b * p.nchunks + sp) * p.cand_cap;
+    for (int s = tid; s < L; s += NT) out[s] = make_uint2(lk[s], li[s]);
+    if (tid == 0) p.chunk_info[(int64_t)b * p.nchunks + sp] = make_uint2((uint32_t)L, max_cut);
 
     VDXS_T1(0, t_all);
     // Completion: the last CTA of the row runs stage 2.
@@ -2416,20 +2614,28 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         nsp = (int)((V + span - 1) / span);
         const int R = K <= 32 ? 1 : (K <= 64 ? 2 : 4);
         const int rs = esz == 4 ? net_ring_slots<float>() : net_ring_slots<uint16_t>();
-        const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(R, rs, (int)esz) + (size_t)NWARPS * 32 * R * 8;
-        size_t s2 = std::max(stage2_bytes(K, nsp * K + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
+        const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(R, rs, (int)esz) + (size_t)4 * hist_area_words();
+        // Each item writes its candidates at or above the final threshold (usually its
+        // share of the row's top-K plus the boundary bin); more than this takes an exact
+        // top-K in the item.
+        const int cc = (int)std::max<int64_t>(K, std::min<int64_t>(4 * K, 8192 / nsp));
+        size_t s2 = std::max(stage2_bytes(K, nsp * cc + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
         s2 += kHeadBytes;
         if ((int64_t)s1 > smem_optin || (int64_t)s2 > smem_optin) {
             if (err) *err = "shared-memory plan exceeds the device limit";
             return cudaErrorInvalidValue;
         }
+        int per_sm = 0;
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        const int ctas_per_sm = per_sm >= 2 * (int)(align16(s1) + 1024) ? 2 : 1;
         plan->chunk = (int)span;
         plan->nchunks = nsp;
         plan->nspans = nsp;
         plan->span = 1;
         plan->elems = R;
         plan->stream = true;
-        plan->grid = (int)std::min<int64_t>((int64_t)a.B * nsp, (int64_t)sms * 2);
+        plan->cand_cap = cc;
+        plan->grid = (int)std::min<int64_t>((int64_t)a.B * nsp, (int64_t)sms * ctas_per_sm);
         plan->smem = align16(s1);
         plan->smem2 = align16(s2);
         return cudaSuccess;
@@ -2452,6 +2658,7 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         need += kHeadBytes;
         if ((int64_t)need <= smem_optin) {
             plan->chunk = CH;
+            plan->cand_cap = K;
             plan->elems = E;
             plan->span = span;
             plan->nspans = nspans;
@@ -2515,7 +2722,8 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
     if ((e = grow(&ws.row_counter, &ws.row_counter_cap, B, true, stream)) != cudaSuccess) return e;
     if ((e = grow(&ws.row_tau, &ws.row_tau_cap, B * kTauStride, true, stream)) != cudaSuccess) return e;
     if (a.path != kFull) {
-        if ((e = grow(&ws.cand, &ws.cand_cap, B * nch * (size_t)a.K, false, stream)) != cudaSuccess) return e;
+        if ((e = grow(&ws.cand, &ws.cand_cap, B * nch * (size_t)plan.cand_cap, false, stream)) != cudaSuccess)
+            return e;
         if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, B * nch, false, stream)) != cudaSuccess) return e;
     } else {
         // fmax: [B*nch] max keys + [B*nch] probability max keys; fsum: [B*nch] sums + [B*nch] stats.
@@ -2587,8 +2795,8 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
     w.row_tau = (uint32_t*)take(B * kTauStride * sizeof(uint32_t));
     w.row_tau_cap = B * kTauStride;
     if (a.path != kFull) {
-        w.cand = (uint2*)take(B * nch * (size_t)a.K * sizeof(uint2));
-        w.cand_cap = B * nch * (size_t)a.K;
+        w.cand = (uint2*)take(B * nch * (size_t)plan.cand_cap * sizeof(uint2));
+        w.cand_cap = B * nch * (size_t)plan.cand_cap;
         w.chunk_info = (uint2*)take(B * nch * sizeof(uint2));
         w.chunk_info_cap = B * nch;
     } else {
@@ -2606,6 +2814,17 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
     }
     if (off <= cap) ws = w;
     return off;
+}
+
+cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream) {
+    cudaError_t e = cudaSuccess;
+    if (ws.err && (e = cudaMemsetAsync(ws.err, 0, sizeof(int32_t), stream)) != cudaSuccess) return e;
+    if (ws.row_counter && (e = cudaMemsetAsync(ws.row_counter, 0, sizeof(uint32_t) * ws.row_counter_cap, stream)) !=
+                              cudaSuccess)
+        return e;
+    if (ws.row_tau && (e = cudaMemsetAsync(ws.row_tau, 0, sizeof(uint32_t) * ws.row_tau_cap, stream)) != cudaSuccess)
+        return e;
+    return cudaSuccess;
 }
 
 void free_workspace(Workspace& ws) {
@@ -2648,6 +2867,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
         p.pen_stride = (int)std::min<int64_t>(a.hist_stride, kMaxHistory);
     }
     p.cand = ws.cand;
+    p.cand_cap = plan.cand_cap;
     p.chunk_info = ws.chunk_info;
     p.row_counter = ws.row_counter;
     p.row_tau = ws.row_tau;
@@ -2671,6 +2891,14 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     return p;
 }
 
+// Records the optional profiling event and counts launches (diagnostics only).
+static inline cudaError_t mark(const SampleArgs& a, cudaEvent_t ev) {
+    return ev ? cudaEventRecord(ev, a.stream) : cudaSuccess;
+}
+static inline void count(const SampleArgs& a, int n = 1) {
+    if (a.launches) *a.launches += n;
+}
+
 template <typename T>
 static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err) {
     cudaError_t e;
@@ -2685,6 +2913,7 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
                                                            a.hist_stride, a.hist_count, a.penalty, ws.pen_ids,
                                                            ws.pen_vals, ws.pen_cnt, ps);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        count(a);
     }
     (void)err;
     const dim3 grid(plan.nchunks, a.B);
@@ -2693,32 +2922,37 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         if (e != cudaSuccess) return e;
         e = cudaFuncSetAttribute(full_sum_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
         if (e != cudaSuccess) return e;
+        if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
         full_max_kernel<T><<<grid, NT, plan.smem, a.stream>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         full_sum_kernel<T><<<grid, NT, plan.smem, a.stream>>>(p);
-        return cudaGetLastError();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        count(a, 2);
+        return mark(a, a.ev_end);
     }
     const size_t esz = sizeof(T);
     const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0);
     if (plan.stream) {
         void (*k1)(KParams) = nullptr;
         const int R = plan.elems;
-        const int M = 2 * ((a.K + 31) / 32);
-#define VDXS_NET(R_, M_) k1 = vec ? topk_net_kernel<T, true, R_, M_> : topk_net_kernel<T, false, R_, M_>
-        if (R == 1) VDXS_NET(1, 2);
-        else if (R == 2) VDXS_NET(2, 4);
-        else VDXS_NET(4, 8);
-#undef VDXS_NET
-        (void)M;
+#define VDXS_HIST(R_) k1 = vec ? topk_hist_kernel<T, true, R_> : topk_hist_kernel<T, false, R_>
+        if (R == 1) VDXS_HIST(1);
+        else if (R == 2) VDXS_HIST(2);
+        else VDXS_HIST(4);
+#undef VDXS_HIST
         if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem)) != cudaSuccess)
             return e;
         if ((e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)plan.smem2)) != cudaSuccess)
             return e;
+        if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
         k1<<<plan.grid, NT, plan.smem, a.stream>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = mark(a, a.ev_end)) != cudaSuccess) return e;
         finish_kernel<T><<<a.B, NT, plan.smem2, a.stream>>>(p);
-        return cudaGetLastError();
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        count(a, 2);
+        return cudaSuccess;
     }
     const int M = a.K <= NT ? 1 : 4;
     void (*kern)(KParams) = nullptr;
@@ -2726,8 +2960,11 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
     else kern = vec ? topk_span_kernel<T, 16, 4, true> : topk_span_kernel<T, 16, 4, false>;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
     if (e != cudaSuccess) return e;
+    if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
     kern<<<grid, NT, plan.smem, a.stream>>>(p);
-    return cudaGetLastError();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    count(a);
+    return mark(a, a.ev_end);
 }
 
 cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err) {
@@ -2749,7 +2986,9 @@ cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std
         return e;
     }
     merge_draw_kernel<<<a.B, NT, sm, a.stream>>>(p, ws.shard_recv, ranks);
-    return cudaGetLastError();
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    count(a);
+    return cudaSuccess;
 }
 
 }  // namespace vdxs

@@ -69,6 +69,29 @@ class SamplerContext:
     def set_tie_mode(self, mode: int):
         check(self.lib.vdxs_set_tie_mode(self._h, mode), self._h)
 
+    def device_status(self, stream=None):
+        """vdxs_device_status: waits for the stream, raises VdxsError if a kernel of an
+        earlier call reported a timeout or a failed internal check."""
+        check(self.lib.vdxs_device_status(self._h, _stream_ptr(stream)), self._h)
+
+    def set_stage_events(self, ev_begin=None, ev_end=None):
+        """Records two torch.cuda.Event objects around the dominant pass of every later
+        call (None, None stops). The events are created here if torch has not yet."""
+        if ev_begin is None or ev_end is None:
+            check(self.lib.vdxs_set_stage_events(self._h, None, None), self._h)
+            return
+        for ev in (ev_begin, ev_end):
+            if not ev.cuda_event:
+                ev.record()
+        check(self.lib.vdxs_set_stage_events(self._h, C.c_void_p(ev_begin.cuda_event),
+                                             C.c_void_p(ev_end.cuda_event)), self._h)
+
+    def launch_count(self) -> int:
+        """Kernels the library has launched for this context."""
+        n = C.c_int64()
+        check(self.lib.vdxs_get_launch_count(self._h, C.byref(n)), self._h)
+        return n.value
+
     def sample(self, cfg: VdxsConfig, logits, uniforms=None, history=None, history_count=None,
                vocab: int | None = None, out_k: int = 0, want_flags: bool = False, stream=None,
                tokens=None):
