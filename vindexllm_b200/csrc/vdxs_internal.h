@@ -97,6 +97,10 @@ struct LaunchPlan {
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
     int grid = 0;         // stream kernel grid (CTAs)
     int cand_cap = 0;     // top-k path: candidates each stage-1 item may write
+    long long items = 0;  // top-k path: stage-1 item slots (candidate lists)
+    int flat_ng = 0;      // stream path: granules per row of the flat partition (0 = spans)
+    int flat_pmax = 0;    // stream path: pieces per CTA
+    long long flat_ngt = 0;
     size_t smem = 0;
     size_t smem2 = 0;     // finish kernel shared memory
 };

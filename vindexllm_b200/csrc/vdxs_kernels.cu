@@ -83,7 +83,14 @@ struct KParams {
     // workspace
     uint2* cand;        // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
     int cand_cap;       // candidates each stage-1 item may write
-    uint2* chunk_info;  // [rows * nchunks] (candidate count, largest key dropped by an exact cut)
+    uint2* chunk_info;  // [items] (candidate count, largest key dropped by an exact cut)
+    // Flat partition of the stream path (flat_ng > 0): the B x ng granules of kSlice
+    // elements are split evenly over flat_grid CTAs; CTA c writes its pieces (maximal
+    // runs within one row) to items c * flat_pmax + j.
+    int flat_ng;
+    int flat_grid;
+    int flat_pmax;
+    long long flat_ngt;
     uint32_t* row_counter;
     uint32_t* row_tau;  // stream path: per-row lower bound on the K-th key (reset by finish)
     int32_t* err;
@@ -110,6 +117,14 @@ struct KParams {
 // ---------------------------------------------------------------------------------
 // Keys and loads
 // ---------------------------------------------------------------------------------
+// First granule of CTA c in the flat partition, and the CTA that holds granule g.
+__host__ __device__ __forceinline__ long long flat_start(long long ngt, int grid, int c) {
+    return (long long)c * ngt / grid;
+}
+__host__ __device__ __forceinline__ int flat_owner(long long ngt, int grid, long long g) {
+    return (int)(((g + 1) * (long long)grid - 1) / ngt);
+}
+
 __device__ __forceinline__ uint32_t f2key(float f) {
     uint32_t u = __float_as_uint(f);
     if (u == 0x80000000u) u = 0u;  // -0.0 compares equal to +0.0
@@ -1069,10 +1084,23 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     uint32_t* sk = (uint32_t*)region;
     uint32_t* si = sk + K;
     uint32_t* ckey = si + K;
-    const int nsp = p.nchunks;  // stage-1 items (spans) of this row
+    // Stage-1 items of this row: spans b * nchunks + i, or in the flat partition the
+    // pieces of the CTAs that own the row's granules.
+    int nsp = p.nchunks, c_lo = 0;
+    if (p.flat_ng > 0) {
+        const long long g0 = (long long)b * p.flat_ng;
+        c_lo = flat_owner(p.flat_ngt, p.flat_grid, g0);
+        nsp = flat_owner(p.flat_ngt, p.flat_grid, g0 + p.flat_ng - 1) - c_lo + 1;
+    }
+    auto item_of = [&](int i) -> int64_t {
+        if (p.flat_ng <= 0) return (int64_t)b * p.nchunks + i;
+        const int c = c_lo + i;
+        const int jj = b - (int)(flat_start(p.flat_ngt, p.flat_grid, c) / p.flat_ng);
+        return (int64_t)c * p.flat_pmax + jj;
+    };
     const int cc = p.cand_cap;
     uint32_t cnt = 0u;
-    for (int i = tid; i < nsp; i += NT) cnt += min(__ldcg(&p.chunk_info[(int64_t)b * nsp + i].x), (uint32_t)cc);
+    for (int i = tid; i < nsp; i += NT) cnt += min(__ldcg(&p.chunk_info[item_of(i)].x), (uint32_t)cc);
     const int nc = (int)block_sum_u32(cnt, sh + 32);
     const int n2 = nc + npen;
     uint32_t* cidx = ckey + n2;
@@ -1083,7 +1111,7 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
         if (tid == 0) sh[40] = 0u;
         __syncthreads();
         for (int it = tid >> 5; it < nsp; it += NWARPS) {
-            const int64_t ii = (int64_t)b * nsp + it;
+            const int64_t ii = item_of(it);
             const int c = (int)min(__ldcg(&p.chunk_info[ii].x), (uint32_t)cc);
             uint32_t base = 0u;
             if (lane == 0) base = atomicAdd(&sh[40], (uint32_t)c);
@@ -1113,8 +1141,8 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
     kb = block_min_u32(kb, sh + 32);
     uint32_t ck_tie = 0u;
-    for (int i = tid; i < p.nchunks; i += NT) {
-        const uint2 ci = __ldcg(p.chunk_info + (int64_t)b * p.nchunks + i);
+    for (int i = tid; i < nsp; i += NT) {
+        const uint2 ci = __ldcg(p.chunk_info + item_of(i));
         if (ci.y != 0u && ci.y == kb) ck_tie = 1u;
     }
     ck_tie = block_max_u32(ck_tie, sh + 32);
@@ -1712,16 +1740,25 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     uint32_t* G = H + kTBins;
     uint32_t* ckey = G + kTGroups;
     uint32_t* cidx = ckey + kCandTotal;
-    volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current item
+    volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current piece
     uint32_t* s_cnt = sh + 21;         // buffer slots reserved (may pass CAP on a spill)
     uint32_t* s_ovf = sh + 22;         // some warp spilled to its list
     uint32_t* s_out = sh + 23;         // output counter
     uint32_t* s_cut = sh + 24;         // [NWARPS] largest key each warp list dropped
-    const int nsp = p.nchunks;
-    const int SPAN = p.chunk;
-    const int SW = SPAN / NWARPS;
-    const int items = p.B * nsp;
     const float NANF = __uint_as_float(0x7FC00000u);
+    const int ng = p.flat_ng;
+    const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
+    const long long g_end = flat_start(p.flat_ngt, gridDim.x, blockIdx.x + 1);
+    const int b_first = (int)(g_begin / ng);
+    const int npieces = g_end > g_begin ? (int)((g_end - 1) / ng) - b_first + 1 : 0;
+    // This warp's element range of piece j (row b_first + j).
+    auto warp_range = [&](int j, int64_t& lo, int64_t& hi) {
+        const long long rb = (long long)(b_first + j) * ng;
+        const long long glo = max(g_begin, rb) - rb, ghi = min(g_end, rb + ng) - rb;
+        const long long w0 = glo + (ghi - glo) * warp / NWARPS, w1 = glo + (ghi - glo) * (warp + 1) / NWARPS;
+        lo = w0 * kSlice;
+        hi = min(w1 * kSlice, (long long)p.V);
+    };
     for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
     if (tid == 0) {
         sh[20] = 0u;
@@ -1730,30 +1767,28 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     }
     __syncthreads();
 
-    // Producer cursor (lane 0): the warp's slices of its items, in consumption order.
-    int pi = blockIdx.x - (int)gridDim.x, pq = 0, pns = 0;
+    // Producer cursor (lane 0): the warp's slices of its pieces, in consumption order.
+    int pj_prod = -1, pq = 0, pns = 0;
     int64_t pleft = 0;
     const T* psrc = nullptr;
     uint32_t pn = 0;
-    auto next_item = [&]() {
+    auto next_piece = [&]() {
         for (;;) {
-            pi += gridDim.x;
-            if (pi >= items) return;
-            const int bb = pi / nsp, sp0 = pi - bb * nsp;
-            const int64_t a = (int64_t)sp0 * SPAN + (int64_t)warp * SW;
-            const int64_t e = min(a + SW, (int64_t)p.V);
-            if (e > a) {
-                pleft = e - a;
+            if (++pj_prod >= npieces) return;
+            int64_t lo, hi;
+            warp_range(pj_prod, lo, hi);
+            if (hi > lo) {
+                pleft = hi - lo;
                 pns = (int)((pleft + kSlice - 1) / kSlice);
-                psrc = (const T*)p.logits + (int64_t)bb * p.stride + a;
+                psrc = (const T*)p.logits + (int64_t)(b_first + pj_prod) * p.stride + lo;
                 pq = 0;
                 return;
             }
         }
     };
     auto issue = [&]() {
-        if (pq >= pns) next_item();
-        if (pi >= items) return;
+        if (pq >= pns) next_piece();
+        if (pj_prod >= npieces) return;
         const int nn = (int)min((int64_t)kSlice, pleft - (int64_t)pq * kSlice);
         const int slot = (int)(pn % RS);
         const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
@@ -1775,15 +1810,67 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         __syncwarp();
     }
 
+    // Slice loads: 16 values per lane; NaN marks positions past the end.
+    auto load_ring = [&](float (&x)[16], int slot, int n, const T* row, int64_t start) {
+        const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
+        const T* sl = ring + (size_t)slot * kSlice;
+#pragma unroll
+        for (int j = 0; j < 16 / VN; ++j) {
+            const int pos = (j * 32 + lane) * VN;
+            if (pos + VN <= n_tma) {
+                unpack(*reinterpret_cast<const uint4*>(sl + pos), &x[j * VN], T());
+            } else {
+#pragma unroll
+                for (int e = 0; e < VN; ++e) {
+                    const int i = pos + e;
+                    x[j * VN + e] = i < n ? (i < n_tma ? to_f(sl[i]) : ld_elem(row, start + i)) : NANF;
+                }
+            }
+        }
+    };
+    // Penalised history ids are excluded from stage 1 (they re-enter in stage 2).
+    auto mask_penalised = [&](float (&x)[16], const int32_t* pid, int npen, int& pj, int64_t start, int n) {
+        if (lane < kSlice / 32) wbm[lane] = 0u;
+        __syncwarp();
+        for (;;) {
+            const int j = pj + lane;
+            const bool in = j < npen && pid[j] < start + n;
+            if (in) {
+                const int d = (int)(pid[j] - start);
+                atomicOr(&wbm[d >> 5], 1u << (d & 31));
+            }
+            const unsigned m = __ballot_sync(FULL, in);
+            pj += __popc(m);
+            if (m != FULL) break;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+            if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
+        }
+        __syncwarp();
+    };
+    auto count_slice = [&](const float (&x)[16]) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            if (x[e] == x[e]) {
+                const uint32_t k = f2key(x[e]);
+                atomicAdd(&H[k >> 20], 1u);
+                atomicAdd(&G[k >> 26], 1u);
+            }
+        }
+    };
+
     uint32_t cn = 0;
     bool timed_out = false;
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int b = item / nsp, spn = item - b * nsp;
+    for (int j = 0; j < npieces; ++j) {
+        const int b = b_first + j;
         const T* row = (const T*)p.logits + (int64_t)b * p.stride;
         const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
         const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-        const int64_t a0 = (int64_t)spn * SPAN + (int64_t)warp * SW;
-        const int64_t a1 = min(a0 + SW, (int64_t)p.V);
+        int64_t a0, a1;
+        warp_range(j, a0, a1);
         const int ns = a1 > a0 ? (int)((a1 - a0 + kSlice - 1) / kSlice) : 0;
         uint64_t lst[R];
 #pragma unroll
@@ -1794,6 +1881,32 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
         uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
         uint32_t rtau_next = ld_relaxed_u32(rtp);
+        // Counting phase: the first slices already in the ring are counted whole before
+        // any is filtered, so the threshold starts near the K-th key of the CTA's first
+        // NWARPS * RS slices of the piece. Counted elements are not counted again.
+        int ncounted = 0;
+        if constexpr (TMA) {
+            ncounted = min(RS, ns);
+            int pjc = pj;
+            for (int q = 0; q < ncounted; ++q) {
+                const int64_t start = a0 + (int64_t)q * kSlice;
+                const int n = (int)min((int64_t)kSlice, a1 - start);
+                const uint32_t c = cn + (uint32_t)q;
+                if (!mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
+                float x[16];
+                load_ring(x, (int)(c % RS), n, row, start);
+                if (npen > 0) mask_penalised(x, pid, npen, pjc, start, n);
+                count_slice(x);
+            }
+        }
+        if (ncounted > 0) {
+            __syncwarp();
+            const uint32_t t = hist_threshold(H, G, K);
+            if (lane == 0 && t > *s_T) {
+                atomicMax((uint32_t*)s_T, t);
+                if (t > rtau_next) atomicMax(rtp, t);
+            }
+        }
         VDXS_T0(t_item);
 
         for (int q = 0; q < ns; ++q) {
@@ -1806,21 +1919,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             if constexpr (TMA) {
                 const int slot = (int)(cn % RS);
                 if (!mbar_wait_bounded(&full[slot], (cn / RS) & 1u)) timed_out = true;
-                const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
-                const T* sl = ring + (size_t)slot * kSlice;
-#pragma unroll
-                for (int j = 0; j < 16 / VN; ++j) {
-                    const int pos = (j * 32 + lane) * VN;
-                    if (pos + VN <= n_tma) {
-                        unpack(*reinterpret_cast<const uint4*>(sl + pos), &x[j * VN], T());
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < VN; ++e) {
-                            const int i = pos + e;
-                            x[j * VN + e] = i < n ? (i < n_tma ? to_f(sl[i]) : ld_elem(row, start + i)) : NANF;
-                        }
-                    }
-                }
+                load_ring(x, slot, n, row, start);
                 __syncwarp();
                 ++cn;
                 if (lane == 0) issue();  // refill the slot just read
@@ -1831,45 +1930,18 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
                     x[e] = pos < n ? ld_elem(row, start + pos) : NANF;
                 }
             }
-            if (npen > 0) {
-                // Penalised history ids are excluded here (they re-enter in stage 2).
-                if (lane < kSlice / 32) wbm[lane] = 0u;
-                __syncwarp();
-                for (;;) {
-                    const int j = pj + lane;
-                    const bool in = j < npen && pid[j] < start + n;
-                    if (in) {
-                        const int d = (int)(pid[j] - start);
-                        atomicOr(&wbm[d >> 5], 1u << (d & 31));
-                    }
-                    const unsigned m = __ballot_sync(FULL, in);
-                    pj += __popc(m);
-                    if (m != FULL) break;
-                }
-                __syncwarp();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                    if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
-                }
-            }
-            const bool counted = q == 0;
-            if (counted) {
-                // Count the whole first slice, then take the threshold it supports.
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    if (x[e] == x[e]) {
-                        const uint32_t k = f2key(x[e]);
-                        atomicAdd(&H[k >> 20], 1u);
-                        atomicAdd(&G[k >> 26], 1u);
-                    }
-                }
+            if (npen > 0) mask_penalised(x, pid, npen, pj, start, n);
+            bool counted = q < ncounted;
+            if (!TMA && q == 0) {
+                // Plain-load path: count the first slice, then take its threshold.
+                count_slice(x);
                 __syncwarp();
                 const uint32_t t = hist_threshold(H, G, K);
                 if (lane == 0 && t > *s_T) {
                     atomicMax((uint32_t*)s_T, t);
                     if (t > rtau) atomicMax(rtp, t);
                 }
+                counted = true;
             }
             // Threshold: the CTA's, the row's and (after a spill) the warp list's K-th key.
             const uint32_t tg = max(max(*s_T, rtau), tau);
@@ -1942,7 +2014,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
                     e0 = stop;
                 }
             }
-            if (added) {
+            if (added && !counted) {
                 __syncwarp();
                 const uint32_t t = hist_threshold(H, G, K);
                 if (lane == 0 && t > *s_T) {
@@ -1971,6 +2043,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         const uint32_t tfin = sh[19];
         const bool any_ovf = *s_ovf != 0u;
         const int nbuf = (int)min(*s_cnt, (uint32_t)CAP);
+        const int item = (int)blockIdx.x * p.flat_pmax + j;
         uint2* out = p.cand + (size_t)item * p.cand_cap;
         bool done = false;
         if (!any_ovf) {
@@ -2020,7 +2093,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             uint32_t* ok = H;
             uint32_t* oi = H + K;
             const int m_out = block_emit(SmemPairSrc{ckey, cidx}, nin, so, ok, oi, K, &sh[8], IdentIdx{cidx});
-            for (int j = tid; j < m_out; j += NT) out[j] = make_uint2(ok[j], oi[j]);
+            for (int i = tid; i < m_out; i += NT) out[i] = make_uint2(ok[i], oi[i]);
             if (tid == 0) {
                 uint32_t cut = so.tie_cut ? so.kth_key : 0u;
                 for (int w = 0; w < NWARPS; ++w) cut = max(cut, s_cut[w]);
@@ -2603,39 +2676,45 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     const bool faithful = a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit;
     if (K <= kWarpMaxK) {
         // Stream path: persistent stage 1 (two CTAs per SM) + one finish CTA per row.
-        int dev = 0, sms = 148;
+        int dev = 0, sms = 148, per_sm = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        constexpr int unit = NWARPS * kSlice;  // 4096
-        const int64_t units = (V + unit - 1) / unit;
-        const int64_t want = std::max<int64_t>(1, ((int64_t)sms * 8 + a.B - 1) / a.B);
-        int nsp = (int)std::min<int64_t>(units, want);
-        const int64_t span = (units + nsp - 1) / nsp * unit;
-        nsp = (int)((V + span - 1) / span);
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
         const int R = K <= 32 ? 1 : (K <= 64 ? 2 : 4);
         const int rs = esz == 4 ? net_ring_slots<float>() : net_ring_slots<uint16_t>();
         const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(R, rs, (int)esz) + (size_t)4 * hist_area_words();
-        // Each item writes its candidates at or above the final threshold (usually its
+        const int ctas_per_sm = per_sm >= 2 * (int)(align16(s1) + 1024) ? 2 : 1;
+        // Flat partition: granules of kSlice elements, evenly over at most one wave of
+        // CTAs, at least kMinGranules per CTA so small batches keep pieces worth a CTA.
+        constexpr long long kMinGranules = 16;
+        const int ng = (int)((V + kSlice - 1) / kSlice);
+        const long long ngt = (long long)a.B * ng;
+        const int grid = (int)std::max<long long>(1, std::min<long long>((long long)sms * ctas_per_sm, ngt / kMinGranules));
+        const long long gmax_cta = (ngt + grid - 1) / grid, gmin_cta = std::max<long long>(1, ngt / grid);
+        const int pmax = (int)((gmax_cta - 1) / ng + 2);                 // pieces per CTA
+        const int ipr = (int)((ng + gmin_cta - 1) / gmin_cta + 1);       // pieces per row
+        // Each piece writes its candidates at or above the final threshold (usually its
         // share of the row's top-K plus the boundary bin); more than this takes an exact
-        // top-K in the item.
-        const int cc = (int)std::max<int64_t>(K, std::min<int64_t>(4 * K, 8192 / nsp));
-        size_t s2 = std::max(stage2_bytes(K, nsp * cc + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
+        // top-K in the piece.
+        const int cc = (int)std::max<int64_t>(K, std::min<int64_t>(4 * K, 8192 / ipr));
+        size_t s2 = std::max(stage2_bytes(K, (size_t)ipr * cc + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
         s2 += kHeadBytes;
         if ((int64_t)s1 > smem_optin || (int64_t)s2 > smem_optin) {
             if (err) *err = "shared-memory plan exceeds the device limit";
             return cudaErrorInvalidValue;
         }
-        int per_sm = 0;
-        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-        const int ctas_per_sm = per_sm >= 2 * (int)(align16(s1) + 1024) ? 2 : 1;
-        plan->chunk = (int)span;
-        plan->nchunks = nsp;
-        plan->nspans = nsp;
+        plan->chunk = 0;
+        plan->nchunks = ipr;
+        plan->nspans = ipr;
         plan->span = 1;
         plan->elems = R;
         plan->stream = true;
         plan->cand_cap = cc;
-        plan->grid = (int)std::min<int64_t>((int64_t)a.B * nsp, (int64_t)sms * ctas_per_sm);
+        plan->grid = grid;
+        plan->flat_ng = ng;
+        plan->flat_ngt = ngt;
+        plan->flat_pmax = pmax;
+        plan->items = (long long)grid * pmax;
         plan->smem = align16(s1);
         plan->smem2 = align16(s2);
         return cudaSuccess;
@@ -2659,6 +2738,7 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         if ((int64_t)need <= smem_optin) {
             plan->chunk = CH;
             plan->cand_cap = K;
+            plan->items = (long long)a.B * nspans;
             plan->elems = E;
             plan->span = span;
             plan->nspans = nspans;
@@ -2722,9 +2802,10 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
     if ((e = grow(&ws.row_counter, &ws.row_counter_cap, B, true, stream)) != cudaSuccess) return e;
     if ((e = grow(&ws.row_tau, &ws.row_tau_cap, B * kTauStride, true, stream)) != cudaSuccess) return e;
     if (a.path != kFull) {
-        if ((e = grow(&ws.cand, &ws.cand_cap, B * nch * (size_t)plan.cand_cap, false, stream)) != cudaSuccess)
+        if ((e = grow(&ws.cand, &ws.cand_cap, (size_t)plan.items * (size_t)plan.cand_cap, false, stream)) !=
+            cudaSuccess)
             return e;
-        if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, B * nch, false, stream)) != cudaSuccess) return e;
+        if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, (size_t)plan.items, false, stream)) != cudaSuccess) return e;
     } else {
         // fmax: [B*nch] max keys + [B*nch] probability max keys; fsum: [B*nch] sums + [B*nch] stats.
         size_t cap_a = ws.full_cap, cap_b = ws.full_cap;
@@ -2795,10 +2876,10 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
     w.row_tau = (uint32_t*)take(B * kTauStride * sizeof(uint32_t));
     w.row_tau_cap = B * kTauStride;
     if (a.path != kFull) {
-        w.cand = (uint2*)take(B * nch * (size_t)plan.cand_cap * sizeof(uint2));
-        w.cand_cap = B * nch * (size_t)plan.cand_cap;
-        w.chunk_info = (uint2*)take(B * nch * sizeof(uint2));
-        w.chunk_info_cap = B * nch;
+        w.cand = (uint2*)take((size_t)plan.items * (size_t)plan.cand_cap * sizeof(uint2));
+        w.cand_cap = (size_t)plan.items * (size_t)plan.cand_cap;
+        w.chunk_info = (uint2*)take((size_t)plan.items * sizeof(uint2));
+        w.chunk_info_cap = (size_t)plan.items;
     } else {
         w.fmax = (uint32_t*)take(2 * B * nch * sizeof(uint32_t));
         w.fsum = (double*)take(2 * B * nch * sizeof(double));
@@ -2868,6 +2949,10 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     }
     p.cand = ws.cand;
     p.cand_cap = plan.cand_cap;
+    p.flat_ng = plan.flat_ng;
+    p.flat_grid = plan.grid;
+    p.flat_pmax = plan.flat_pmax;
+    p.flat_ngt = plan.flat_ngt;
     p.chunk_info = ws.chunk_info;
     p.row_counter = ws.row_counter;
     p.row_tau = ws.row_tau;
