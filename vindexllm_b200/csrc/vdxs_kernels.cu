@@ -1728,6 +1728,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     constexpr int VN = TMA ? (int)(16 / sizeof(T)) : 1;
     constexpr int NB = 32 * R;  // list and batch length
     constexpr int CAP = kCandTotal - NWARPS * NB;
+    constexpr int WCAP = CAP / NWARPS;  // candidate slots of each warp's region
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K;
     const int WW = net_area_words(R, RS, (int)sizeof(T));
@@ -1741,10 +1742,10 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     uint32_t* ckey = G + kTGroups;
     uint32_t* cidx = ckey + kCandTotal;
     volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current piece
-    uint32_t* s_cnt = sh + 21;         // buffer slots reserved (may pass CAP on a spill)
     uint32_t* s_ovf = sh + 22;         // some warp spilled to its list
     uint32_t* s_out = sh + 23;         // output counter
     uint32_t* s_cut = sh + 24;         // [NWARPS] largest key each warp list dropped
+    uint32_t* s_wcnt = sh + 48;        // [NWARPS] candidates in each warp's region
     const float NANF = __uint_as_float(0x7FC00000u);
     const int ng = p.flat_ng;
     const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
@@ -1851,14 +1852,14 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         }
         __syncwarp();
     };
+    // Counts each lane's maximum of a slice: distinct elements, so any count is still a
+    // valid basis for the threshold, at one atomic pair per lane instead of sixteen.
     auto count_slice = [&](const float (&x)[16]) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            if (x[e] == x[e]) {
-                const uint32_t k = f2key(x[e]);
-                atomicAdd(&H[k >> 20], 1u);
-                atomicAdd(&G[k >> 26], 1u);
-            }
+        const float m = max16(x);
+        if (m == m) {
+            const uint32_t k = f2key(m);
+            atomicAdd(&H[k >> 20], 1u);
+            atomicAdd(&G[k >> 26], 1u);
         }
     };
 
@@ -1878,6 +1879,10 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         int bcount = 0, pj = 0;
         uint32_t tau = 0u, max_cut = 0u;
         bool ovf = false;  // warp-uniform: candidates go to the exact list from now on
+        uint32_t since = 0u;  // candidates counted since the threshold was last raised
+        uint32_t wcnt = 0u;   // candidates in this warp's region of the buffer
+        uint32_t* rkey = ckey + warp * WCAP;
+        uint32_t* ridx = cidx + warp * WCAP;
         if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
         uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
         uint32_t rtau_next = ld_relaxed_u32(rtp);
@@ -1946,42 +1951,76 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             // Threshold: the CTA's, the row's and (after a spill) the warp list's K-th key.
             const uint32_t tg = max(max(*s_T, rtau), tau);
             float thr = key_threshold(tg);
-            if (!__any_sync(FULL, max16(x) >= thr)) continue;
+            const float lmax = max16(x);
+            const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
+            if (lanes == 0u) continue;
             const uint32_t gb = (uint32_t)(p.vocab_offset + start);
-            int e0 = 0;
             bool added = false;
             if (!ovf) {
+                uint32_t pm = 0u;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const bool pass = x[e] >= thr;
-                    const unsigned m = __ballot_sync(FULL, pass);
-                    if (m == 0u) continue;
-                    const uint32_t c = (uint32_t)__popc(m);
-                    uint32_t base = 0u;
-                    if (lane == 0) base = atomicAdd(s_cnt, c);
-                    base = __shfl_sync(FULL, base, 0);
-                    if (base + c > (uint32_t)CAP) {
-                        // Buffer full: blank this warp's share of the reservation and spill.
-                        for (uint32_t i = base + lane; i < (uint32_t)CAP; i += 32) ckey[i] = 0u;
+                for (int e = 0; e < 16; ++e) pm |= (x[e] >= thr ? 1u : 0u) << e;
+                const uint32_t cnt = (uint32_t)__popc(pm);
+                if (!__any_sync(FULL, cnt > 1u)) {
+                    // Common case: at most one candidate per lane, which is then the lane
+                    // maximum; one ballot gives the slots.
+                    const uint32_t total = (uint32_t)__popc(lanes);
+                    if (wcnt + total > (uint32_t)WCAP) {
                         ovf = true;
-                        e0 = e;
-                        break;
+                        if (lane == 0) atomicExch(s_ovf, 1u);
+                    } else {
+                        if (cnt) {
+                            const int e = __ffs((int)pm) - 1;
+                            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                            const uint32_t k = f2key(lmax);
+                            const uint32_t slot = wcnt + __popc(lanes & lanemask_lt());
+                            rkey[slot] = k;
+                            ridx[slot] = gb + (uint32_t)pos;
+                            if (!counted) {
+                                atomicAdd(&H[k >> 20], 1u);
+                                atomicAdd(&G[k >> 26], 1u);
+                            }
+                        }
+                        wcnt += total;
+                        added = true;
+                        since += total;
                     }
-                    if (pass) {
-                        const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                        const uint32_t k = f2key(x[e]);
-                        const uint32_t slot = base + __popc(m & lanemask_lt());
-                        ckey[slot] = k;
-                        cidx[slot] = gb + (uint32_t)pos;
-                        if (!counted) {
-                            atomicAdd(&H[k >> 20], 1u);
-                            atomicAdd(&G[k >> 26], 1u);
+                } else {
+                // General case: a per-lane pass mask, one warp scan, then predicated stores.
+                uint32_t incl = cnt;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const uint32_t o = __shfl_up_sync(FULL, incl, d);
+                    if (lane >= d) incl += o;
+                }
+                const uint32_t total = __shfl_sync(FULL, incl, 31);
+                if (wcnt + total > (uint32_t)WCAP) {
+                    // Region full: spill the whole slice to the exact list.
+                    ovf = true;
+                    if (lane == 0) atomicExch(s_ovf, 1u);
+                } else {
+                    uint32_t slot = wcnt + incl - cnt;
+                    wcnt += total;
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        if ((pm >> e) & 1u) {
+                            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                            const uint32_t k = f2key(x[e]);
+                            rkey[slot] = k;
+                            ridx[slot] = gb + (uint32_t)pos;
+                            ++slot;
+                            if (!counted) {
+                                atomicAdd(&H[k >> 20], 1u);
+                                atomicAdd(&G[k >> 26], 1u);
+                            }
                         }
                     }
                     added = true;
+                    since += total;
                 }
-                if (ovf && lane == 0) atomicExch(s_ovf, 1u);
+                }
             }
+            int e0 = 0;
             if (ovf) {
                 // Exact list: append from element e0 on; merge when the batch would
                 // overflow, then tighten the threshold and resume.
@@ -2014,7 +2053,9 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
                     e0 = stop;
                 }
             }
-            if (added && !counted) {
+            if (added && !counted && since >= 8u) {
+                // Raise the threshold once a few new candidates have been counted.
+                since = 0u;
                 __syncwarp();
                 const uint32_t t = hist_threshold(H, G, K);
                 if (lane == 0 && t > *s_T) {
@@ -2030,30 +2071,36 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             if (K < NB) max_cut = max(max_cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
         }
         VDXS_T1(10, t_item);
-        if (lane == 0) s_cut[warp] = ovf ? max_cut : 0u;
+        if (lane == 0) {
+            s_cut[warp] = ovf ? max_cut : 0u;
+            s_wcnt[warp] = wcnt;
+        }
         __syncthreads();
         VDXS_T0(t_cm);
-        if (tid == 0) {
-            sh[19] = max((uint32_t)*s_T, ld_relaxed_u32(rtp));
-            *s_out = 0u;
+        if (warp == 0) {
+            // Final threshold of the piece from the complete histogram.
+            const uint32_t t = hist_threshold(H, G, K);
+            if (lane == 0) {
+                sh[19] = max(max((uint32_t)*s_T, t), ld_relaxed_u32(rtp));
+                *s_out = 0u;
+            }
         }
         __syncthreads();
         // Every candidate at or above the final threshold leaves; anything below it is
         // below the row's K-th key, so it cannot be selected or tie at the boundary.
         const uint32_t tfin = sh[19];
         const bool any_ovf = *s_ovf != 0u;
-        const int nbuf = (int)min(*s_cnt, (uint32_t)CAP);
         const int item = (int)blockIdx.x * p.flat_pmax + j;
         uint2* out = p.cand + (size_t)item * p.cand_cap;
         bool done = false;
         if (!any_ovf) {
-            for (int i0 = 0; i0 < nbuf; i0 += NT) {
+            for (int i0 = 0; i0 < CAP; i0 += NT) {
                 const int i = i0 + tid;
                 uint32_t k = 0u;
                 bool sel = false;
-                if (i < nbuf) {
+                if (i < CAP && (uint32_t)(i % WCAP) < s_wcnt[i / WCAP]) {
                     k = ckey[i];
-                    sel = k != 0u && k >= tfin;
+                    sel = k >= tfin;
                 }
                 const unsigned m = __ballot_sync(FULL, sel);
                 if (m) {
@@ -2072,8 +2119,11 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             }
         }
         if (!done) {
-            // Exact top-K of the buffer (and of the warp lists after a spill).
-            int nin = nbuf;
+            // Exact top-K of the buffer (and of the warp lists after a spill). Unused
+            // region slots are blanked (key 0 is never selected).
+            for (int i = tid; i < CAP; i += NT)
+                if ((uint32_t)(i % WCAP) >= s_wcnt[i / WCAP]) ckey[i] = 0u;
+            int nin = CAP;
             if (any_ovf) {
 #pragma unroll
                 for (int r = 0; r < R; ++r) {
@@ -2104,7 +2154,6 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
         if (tid == 0) {
             sh[20] = 0u;
-            sh[21] = 0u;
             sh[22] = 0u;
         }
         __syncthreads();
