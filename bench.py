@@ -157,7 +157,7 @@ def run_ours(args, rank, world, local):
     import torch
     import torch.distributed as dist
     from vindexllm_b200 import abi, synth
-    from vindexllm_b200.sampler import SamplerContext, ShardComm
+    from vindexllm_b200.sampler import SamplerContext, ShardComm, broadcast_unique_id, shard_range
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -174,10 +174,9 @@ def run_ours(args, rank, world, local):
     cfg = synth.sampler_config(name)
     mode = abi.TIES_FAITHFUL if args.tie_mode == "faithful" else abi.TIES_CANONICAL
     ctx = SamplerContext(local, tie_mode=mode if world == 1 else abi.TIES_CANONICAL)
-    shard = V // world
-    off = rank * shard
+    off, hi = shard_range(V, world, rank)
     x_full = synth.make_logits(name, step=0, batch=B, device=str(dev))
-    x = x_full[:, off:off + shard].contiguous() if world > 1 else x_full
+    x = x_full[:, off:hi].contiguous() if world > 1 else x_full
     if world > 1:
         del x_full
     esz = x.element_size()
@@ -187,9 +186,7 @@ def run_ours(args, rank, world, local):
     tok = torch.empty(B, dtype=torch.int32, device=dev)
     comm = None
     if world > 1:
-        obj = [ShardComm.unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        comm = ShardComm(ctx, world, rank, obj[0])
+        comm = ShardComm(ctx, world, rank, broadcast_unique_id(rank))
 
     def step(i):
         if comm is not None:
@@ -295,7 +292,7 @@ def run_ours(args, rank, world, local):
             if peak_kind == "measured" else peak_kind,
             "traffic": tr.get("bytes_per_launch") if tr else None,
             "traffic_source": tr.get("source") if tr else None,
-            "kernel": dominant_kernel(cfg, V // world if world > 1 else V, esz),
+            "kernel": dominant_kernel(cfg, hi - off, esz),
             "kernel_ms": round(kern_ms, 5), "alg_bytes_per_launch": alg_bytes,
             "step_frac": round(B * V * esz / (ms_per_step / 1e3) / 1e9 / peak, 4)}
 

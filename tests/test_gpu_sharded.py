@@ -11,7 +11,7 @@ pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
 def _worker(rank, world, uid, name, q):
     import torch
     from vindexllm_b200 import abi, synth
-    from vindexllm_b200.sampler import SamplerContext, ShardComm
+    from vindexllm_b200.sampler import SamplerContext, ShardComm, shard_range
     torch.cuda.set_device(rank)
     ctx = SamplerContext(rank, tie_mode=abi.TIES_CANONICAL)
     comm = ShardComm(ctx, world, rank, uid)
@@ -20,9 +20,9 @@ def _worker(rank, world, uid, name, q):
     V = x.shape[1]
     h, c = synth.make_history(name, step=0, device=f"cuda:{rank}")
     u = torch.as_tensor(synth.make_uniforms(name, 1, batch=x.shape[0])[0], device=f"cuda:{rank}")
-    shard = V // world
-    xs = x[:, rank * shard:(rank + 1) * shard].contiguous()
-    tok = comm.sample(cfg, xs, rank * shard, V, u, h, c)
+    lo, hi = shard_range(V, world, rank)
+    xs = x[:, lo:hi].contiguous()
+    tok = comm.sample(cfg, xs, lo, V, u, h, c)
     torch.cuda.synchronize()
     ref = ctx.sample(cfg, x, u, h, c)
     torch.cuda.synchronize()

@@ -204,6 +204,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 }
 // Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) into this
 // CTA's shared memory; completion is counted on `bar`.
+// Orders this thread's earlier generic-proxy shared-memory accesses (made visible to it
+// by a warp barrier for the other lanes) before its later async-proxy (bulk copy) ones.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                      smem_u32(dst)),
@@ -1925,9 +1930,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
                 const int slot = (int)(cn % RS);
                 if (!mbar_wait_bounded(&full[slot], (cn / RS) & 1u)) timed_out = true;
                 load_ring(x, slot, n, row, start);
-                __syncwarp();
                 ++cn;
-                if (lane == 0) issue();  // refill the slot just read
             } else {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
@@ -1953,6 +1956,13 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             float thr = key_threshold(tg);
             const float lmax = max16(x);
             const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
+            if constexpr (TMA) {
+                // The slot's values are in registers now: refill it.
+                if (lane == 0) {
+                    fence_proxy_async_smem();
+                    issue();
+                }
+            }
             if (lanes == 0u) continue;
             const uint32_t gb = (uint32_t)(p.vocab_offset + start);
             bool added = false;

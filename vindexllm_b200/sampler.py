@@ -17,7 +17,8 @@ from . import abi
 from ._lib import load, check, VdxsError
 from .abi import VdxsConfig, default_config
 
-__all__ = ["SamplerContext", "TVdxSampler", "ShardComm", "VdxsError", "default_config"]
+__all__ = ["SamplerContext", "TVdxSampler", "ShardComm", "VdxsError", "default_config", "shard_range",
+           "broadcast_unique_id"]
 
 
 def _stream_ptr(stream):
@@ -228,6 +229,25 @@ class TVdxSampler:
         check(self.lib.vdxs_sampler_get_history(self._h, row, buf, cap, C.byref(cnt), C.byref(pos)),
               self.ctx.handle)
         return list(buf[: cnt.value]), cnt.value, pos.value
+
+
+def shard_range(vocab: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous vocab shard [lo, hi) of `rank`: the first vocab % world ranks hold one
+    extra token, so every id has exactly one owner and shards are in rank order."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    q, r = divmod(vocab, world)
+    lo = rank * q + min(rank, r)
+    return lo, lo + q + (1 if rank < r else 0)
+
+
+def broadcast_unique_id(rank: int, src: int = 0) -> bytes:
+    """NCCL unique id made on `src` and shared through the caller's torch.distributed
+    process group (any backend): what each rank passes to ShardComm."""
+    import torch.distributed as dist
+    obj = [ShardComm.unique_id() if rank == src else None]
+    dist.broadcast_object_list(obj, src=src)
+    return obj[0]
 
 
 class ShardComm:
