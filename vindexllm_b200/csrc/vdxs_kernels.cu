@@ -787,35 +787,73 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
     const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
     const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
     const float* pvl = p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr;
-    constexpr int R = kFaithfulTile / NT;
 
     // Warp-0 state: per-lane minimum over slots {lane, lane+32, ...} and the global one.
     float mv = -INFINITY;
     int ms = 0;
     if (tid == 0) s_mv = -INFINITY;
+    // Tiles grow geometrically from 256 elements, so the prefilter (the buffer minimum
+    // after the previous tile) tightens before many elements reach the sequential scan.
+    int tsz = 256;
     __syncthreads();
-    for (int64_t base = 0; base < V; base += kFaithfulTile) {
-        const int n = (int)min((int64_t)kFaithfulTile, (int64_t)V - base);
-        for (int i = tid; i < n; i += NT) tile[i] = ld_elem(row, base + i);
+    VDXS_T0(t_floop);
+    for (int64_t base = 0; base < V; base += tsz, tsz = min(2 * tsz, kFaithfulTile)) {
+        VDXS_T0(t_ftile);
+        const int n = (int)min((int64_t)tsz, (int64_t)V - base);
+        {
+            // All loads of the tile are issued before any is stored (one DRAM round trip).
+            constexpr int RT = kFaithfulTile / NT;
+            float v[RT];
+#pragma unroll
+            for (int r = 0; r < RT; ++r) {
+                const int i = tid + r * NT;
+                v[r] = i < n ? ld_elem(row, base + i) : 0.0f;
+            }
+#pragma unroll
+            for (int r = 0; r < RT; ++r) {
+                const int i = tid + r * NT;
+                if (i < n) tile[i] = v[r];
+            }
+        }
         __syncthreads();
         if (npen) {
             const int j0 = lower_bound_i32(pid, npen, base);
             for (int j = j0 + tid; j < npen && pid[j] < base + n; j += NT) tile[pid[j] - base] = pvl[j];
             __syncthreads();
         }
+        // Order-preserving compaction of the elements that can enter the buffer: warp w
+        // takes a contiguous segment in steps of 32 (ballots), then the warps' counts are
+        // scanned; reads are lane-contiguous, so free of bank conflicts.
         const float tau = s_mv;
-        int cnt = 0;
-        for (int r = 0; r < R; ++r) {
-            const int i = tid * R + r;
-            if (i < n && (base + i < K || tile[i] > tau)) ++cnt;
+        const int seg = ((n + NWARPS * 32 - 1) / (NWARPS * 32)) * 32;
+        const int w0 = warp * seg, w1 = min(w0 + seg, n);
+        int wc = 0;
+        for (int i0 = w0; i0 < w1; i0 += 32) {
+            const int i = i0 + lane;
+            const bool c = i < w1 && (base + i < K || tile[i] > tau);
+            wc += __popc(__ballot_sync(FULL, c));
         }
-        int total;
-        int off = block_excl_scan(cnt, s_isum, &total);
-        for (int r = 0; r < R; ++r) {
-            const int i = tid * R + r;
-            if (i < n && (base + i < K || tile[i] > tau)) cpos[off++] = (uint16_t)i;
+        if (lane == 0) s_isum[warp] = wc;
+        __syncthreads();
+        int off = 0, total = 0;
+        for (int w = 0; w < NWARPS; ++w) {
+            const int v = s_isum[w];
+            off += w < warp ? v : 0;
+            total += v;
+        }
+        for (int i0 = w0; i0 < w1; i0 += 32) {
+            const int i = i0 + lane;
+            const bool c = i < w1 && (base + i < K || tile[i] > tau);
+            const unsigned m = __ballot_sync(FULL, c);
+            if (c) cpos[off + __popc(m & lanemask_lt())] = (uint16_t)i;
+            off += __popc(m);
         }
         __syncthreads();
+        VDXS_T1(20, t_ftile);
+#ifdef VDXS_TIMING
+        if (tid == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
+#endif
+        VDXS_T0(t_fscan);
         if (warp == 0) {
             for (int c0 = 0; c0 < total; c0 += 32) {
                 const int c = c0 + lane;
@@ -847,6 +885,9 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
                         changed = true;
                     }
                     __syncwarp();
+#ifdef VDXS_TIMING
+                    if (changed && tid == 0) atomicAdd(&g_phase_count[24], 1ull);
+#endif
                     if (changed) {
                         // Recompute per-lane minima (first slot with strict '<' wins ties).
                         float bv = 0.0f;
@@ -870,8 +911,10 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
             }
             if (lane == 0) s_mv = mv;
         }
+        VDXS_T1(21, t_fscan);
         __syncthreads();
     }
+    VDXS_T1(22, t_floop);
 
     // Sequential stage 2 in slot order (Sampler.pas:385-459).
     int P2 = 32;
