@@ -22,8 +22,10 @@ enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
 struct Workspace {
     uint2* cand = nullptr;          // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
     size_t cand_cap = 0;            // elements
-    uint2* chunk_info = nullptr;    // [rows * nchunks] (chunk k-th key, tie-cut flag)
+    uint2* chunk_info = nullptr;    // [items] (candidate count, largest key cut by an exact decision)
     size_t chunk_info_cap = 0;
+    uint32_t* item_tau = nullptr;   // [items] each item's lower bound on its row's K-th key
+    size_t item_tau_cap = 0;
     uint32_t* row_counter = nullptr;  // [rows] completion counters, self-resetting
     size_t row_counter_cap = 0;
     uint32_t* row_tau = nullptr;      // [rows * kTauStride] stream path K-th key bounds, self-resetting

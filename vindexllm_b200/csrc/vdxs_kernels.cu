@@ -84,6 +84,7 @@ struct KParams {
     uint2* cand;        // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
     int cand_cap;       // candidates each stage-1 item may write
     uint2* chunk_info;  // [items] (candidate count, largest key dropped by an exact cut)
+    uint32_t* item_tau; // [items] the item's lower bound on its row's K-th key (0 = none)
     // Flat partition of the stream path (flat_ng > 0): the B x ng granules of kSlice
     // elements are split evenly over flat_grid CTAs; CTA c writes its pieces (maximal
     // runs within one row) to items c * flat_pmax + j.
@@ -1147,11 +1148,13 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
         return (int64_t)c * p.flat_pmax + jj;
     };
     const int cc = p.cand_cap;
-    uint32_t cnt = 0u;
-    for (int i = tid; i < nsp; i += NT) cnt += min(__ldcg(&p.chunk_info[item_of(i)].x), (uint32_t)cc);
-    const int nc = (int)block_sum_u32(cnt, sh + 32);
-    const int n2 = nc + npen;
-    uint32_t* cidx = ckey + n2;
+    // Every item's bound is a lower bound on the row's K-th key, so is their maximum:
+    // candidates and penalised entries below it can be neither selected nor tied at the
+    // boundary, and are not gathered.
+    uint32_t tb = 0u;
+    for (int i = tid; i < nsp; i += NT) tb = max(tb, __ldcg(&p.item_tau[item_of(i)]));
+    tb = block_max_u32(tb, sh + 32);
+    uint32_t* cidx = ckey + (nsp * cc + npen);  // capacity of the gathered arrays
     uint32_t lm = 0u;
     {
         // Gather the variable-length item lists; warp w takes items w, w+8, ...
@@ -1161,24 +1164,43 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
         for (int it = tid >> 5; it < nsp; it += NWARPS) {
             const int64_t ii = item_of(it);
             const int c = (int)min(__ldcg(&p.chunk_info[ii].x), (uint32_t)cc);
-            uint32_t base = 0u;
-            if (lane == 0) base = atomicAdd(&sh[40], (uint32_t)c);
-            base = __shfl_sync(FULL, base, 0);
             const uint2* src = p.cand + ii * cc;
-            for (int j = lane; j < c; j += 32) {
-                const uint2 e = __ldcg(src + j);
-                ckey[base + j] = e.x;
-                cidx[base + j] = e.y;
-                lm = max(lm, e.x);
+            for (int j0 = 0; j0 < c; j0 += 32) {
+                const int j = j0 + lane;
+                uint2 e = make_uint2(0u, 0u);
+                if (j < c) e = __ldcg(src + j);
+                const bool keep = j < c && e.x >= tb;
+                const unsigned m = __ballot_sync(FULL, keep);
+                uint32_t base = 0u;
+                if (lane == 0 && m) base = atomicAdd(&sh[40], (uint32_t)__popc(m));
+                base = __shfl_sync(FULL, base, 0);
+                if (keep) {
+                    const uint32_t pos = base + __popc(m & lanemask_lt());
+                    ckey[pos] = e.x;
+                    cidx[pos] = e.y;
+                    lm = max(lm, e.x);
+                }
             }
         }
+        for (int j0 = 0; j0 < npen; j0 += NT) {
+            const int j = j0 + tid;
+            uint32_t k = 0u;
+            if (j < npen) k = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
+            const bool keep = j < npen && k >= tb;
+            const unsigned m = __ballot_sync(FULL, keep);
+            uint32_t base = 0u;
+            if (lane == 0 && m) base = atomicAdd(&sh[40], (uint32_t)__popc(m));
+            base = __shfl_sync(FULL, base, 0);
+            if (keep) {
+                const uint32_t pos = base + __popc(m & lanemask_lt());
+                ckey[pos] = k;
+                cidx[pos] = (uint32_t)(pid[j] + p.vocab_offset);
+                lm = max(lm, k);
+            }
+        }
+        __syncthreads();
     }
-    for (int j = tid; j < npen; j += NT) {
-        const uint32_t k = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
-        ckey[nc + j] = k;
-        cidx[nc + j] = (uint32_t)(pid[j] + p.vocab_offset);
-        lm = max(lm, k);
-    }
+    const int n2 = (int)sh[40];
     const uint32_t gmax = block_max_u32(lm, sh + 32);
     const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
     const SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
@@ -2167,7 +2189,10 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             __syncthreads();
             const uint32_t total = *s_out;
             if (total <= (uint32_t)p.cand_cap) {
-                if (tid == 0) p.chunk_info[item] = make_uint2(total, 0u);
+                if (tid == 0) {
+                    p.chunk_info[item] = make_uint2(total, 0u);
+                    p.item_tau[item] = tfin;
+                }
                 done = true;
             }
         }
@@ -2201,6 +2226,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
                 uint32_t cut = so.tie_cut ? so.kth_key : 0u;
                 for (int w = 0; w < NWARPS; ++w) cut = max(cut, s_cut[w]);
                 p.chunk_info[item] = make_uint2((uint32_t)m_out, cut);
+                p.item_tau[item] = tfin;
             }
         }
         __syncthreads();
@@ -2218,6 +2244,8 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         if (lane == 0)
             for (int s = 0; s < RS; ++s) mbar_inval(&full[s]);
     }
+    // This CTA is done: the finish kernel may start launching (it waits for the grid).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // Stage 2 as its own kernel (one CTA per row) after topk_stream_kernel.
@@ -2227,6 +2255,9 @@ __global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
     uint32_t* hist = (uint32_t*)smem_raw;
     uint32_t* sh = hist + kHistWords;
     unsigned char* region = smem_raw + kHeadBytes;
+    // Launched as a programmatic dependent of stage 1: wait until that grid has completed
+    // and its writes are visible (a no-op for an ordinary launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     VDXS_T0(t_fin);
     finish_row<T>(p, blockIdx.x, region, hist, sh);
     if (threadIdx.x == 0 && p.row_tau) p.row_tau[(size_t)blockIdx.x * kTauStride] = 0u;  // ready for the next launch
@@ -2444,7 +2475,10 @@ __global__ void __launch_bounds__(NT) topk_span_kernel(KParams p) {
     // Publish the span's list (padded) and its boundary-tie evidence.
     uint2* out = p.cand + ((int64_t)b * p.nchunks + sp) * p.cand_cap;
     for (int s = tid; s < L; s += NT) out[s] = make_uint2(lk[s], li[s]);
-    if (tid == 0) p.chunk_info[(int64_t)b * p.nchunks + sp] = make_uint2((uint32_t)L, max_cut);
+    if (tid == 0) {
+        p.chunk_info[(int64_t)b * p.nchunks + sp] = make_uint2((uint32_t)L, max_cut);
+        p.item_tau[(int64_t)b * p.nchunks + sp] = L == K ? tau : 0u;  // a full span's K-th key
+    }
 
     VDXS_T1(0, t_all);
     // Completion: the last CTA of the row runs stage 2.
@@ -2908,6 +2942,7 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
             cudaSuccess)
             return e;
         if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, (size_t)plan.items, false, stream)) != cudaSuccess) return e;
+        if ((e = grow(&ws.item_tau, &ws.item_tau_cap, (size_t)plan.items, false, stream)) != cudaSuccess) return e;
     } else {
         // fmax: [B*nch] max keys + [B*nch] probability max keys; fsum: [B*nch] sums + [B*nch] stats.
         size_t cap_a = ws.full_cap, cap_b = ws.full_cap;
@@ -2982,6 +3017,8 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
         w.cand_cap = (size_t)plan.items * (size_t)plan.cand_cap;
         w.chunk_info = (uint2*)take((size_t)plan.items * sizeof(uint2));
         w.chunk_info_cap = (size_t)plan.items;
+        w.item_tau = (uint32_t*)take((size_t)plan.items * sizeof(uint32_t));
+        w.item_tau_cap = (size_t)plan.items;
     } else {
         w.fmax = (uint32_t*)take(2 * B * nch * sizeof(uint32_t));
         w.fsum = (double*)take(2 * B * nch * sizeof(double));
@@ -3013,6 +3050,7 @@ cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream) {
 void free_workspace(Workspace& ws) {
     cudaFree(ws.cand);
     cudaFree(ws.chunk_info);
+    cudaFree(ws.item_tau);
     cudaFree(ws.row_counter);
     cudaFree(ws.row_tau);
     cudaFree(ws.pen_ids);
@@ -3056,6 +3094,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.flat_pmax = plan.flat_pmax;
     p.flat_ngt = plan.flat_ngt;
     p.chunk_info = ws.chunk_info;
+    p.item_tau = ws.item_tau;
     p.row_counter = ws.row_counter;
     p.row_tau = ws.row_tau;
     p.err = ws.err;
@@ -3136,8 +3175,22 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         k1<<<plan.grid, NT, plan.smem, a.stream>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         if ((e = mark(a, a.ev_end)) != cudaSuccess) return e;
-        finish_kernel<T><<<a.B, NT, plan.smem2, a.stream>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        {
+            // Programmatic dependent launch: finish CTAs are scheduled as stage-1 CTAs
+            // retire, hiding the launch gap; they wait for the whole grid in the kernel.
+            // (A recorded event between the two launches makes it an ordinary launch.)
+            cudaLaunchConfig_t lc = {};
+            lc.gridDim = dim3(a.B);
+            lc.blockDim = dim3(NT);
+            lc.dynamicSmemBytes = plan.smem2;
+            lc.stream = a.stream;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[0].val.programmaticStreamSerializationAllowed = 1;
+            lc.attrs = at;
+            lc.numAttrs = 1;
+            if ((e = cudaLaunchKernelEx(&lc, finish_kernel<T>, p)) != cudaSuccess) return e;
+        }
         count(a, 2);
         return cudaSuccess;
     }
