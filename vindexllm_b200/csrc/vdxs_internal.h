@@ -97,6 +97,7 @@ struct LaunchPlan {
     int nspans = 0;   // CTAs per row of the top-k path
     int elems = 32;   // keys per thread per chunk
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
+    bool cluster = false; // top-k path, small batches: one thread-block cluster per row
     int grid = 0;         // stream kernel grid (CTAs)
     int cand_cap = 0;     // top-k path: candidates each stage-1 item may write
     long long items = 0;  // top-k path: stage-1 item slots (candidate lists)

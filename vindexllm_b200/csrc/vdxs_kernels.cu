@@ -24,6 +24,7 @@
 #include "../../include/vdx_sampler.h"
 
 #include <cuda_runtime.h>
+#include <cooperative_groups.h>
 #include <algorithm>
 #include <climits>
 #include <cstdint>
@@ -1124,6 +1125,66 @@ struct OffsetIdx {
 
 // Stage 2 for one row, run by the last CTA of the row: merge the span candidates and
 // the penalised history entries, then greedy / draw (or publish for the all-gather).
+// Stage 2 of one row from gathered candidates (ckey, cidx)[0, n2) in shared memory:
+// exact top-K (block_select), boundary-tie evidence (selection cuts, and cut_of(i) for
+// the ncut stage-1 items), then greedy / draw / publication for the all-gather, and
+// the faithful re-resolution when the row needs it. sk/si are placed at `region`.
+template <typename T, class CutOf>
+__device__ void finish_select(const KParams& p, int b, uint32_t* ckey, uint32_t* cidx, int n2, uint32_t gmax,
+                              int ncut, CutOf cut_of, unsigned char* region, uint32_t* hist, uint32_t* sh) {
+    const int tid = threadIdx.x;
+    const int K = p.K;
+    uint32_t* sk = (uint32_t*)region;
+    uint32_t* si = sk + K;
+    const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
+    const SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
+    const int nsel = block_emit(SmemPairSrc{ckey, cidx}, n2, s2, sk, si, K, &sh[8], IdentIdx{cidx});
+    // The boundary value is the smallest selected key. A boundary tie exists when the
+    // merge cut elements of that value, or a span cut elements of that value.
+    uint32_t kb = 0xFFFFFFFFu;
+    for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
+    kb = block_min_u32(kb, sh + 32);
+    uint32_t ck_tie = 0u;
+    for (int i = tid; i < ncut; i += NT) {
+        const uint32_t c = cut_of(i);
+        if (c != 0u && c == kb) ck_tie = 1u;
+    }
+    ck_tie = block_max_u32(ck_tie, sh + 32);
+    const uint32_t btie = (s2.tie_cut || ck_tie) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
+    if (tid == 0) p.row_counter[b] = 0u;  // ready for the next launch
+
+    if (p.local_emit) {
+        // Vocab-sharded: publish the local top-K and tie evidence for the all-gather.
+        uint2* eo = p.emit_out + (int64_t)b * (K + 1);
+        for (int s = tid; s < K; s += NT) eo[s] = s < nsel ? make_uint2(sk[s], si[s]) : make_uint2(0u, 0xFFFFFFFFu);
+        if (tid == 0) eo[K] = make_uint2(kb, btie ? 1u : 0u);
+        return;
+    }
+    if (p.path == kGreedy) {
+        // Greedy (Sampler.pas:305-322): the canonical top-1 is the first maximum.
+        if (tid == 0) {
+            p.tokens[b] = (int32_t)si[0];
+            if (p.flags) p.flags[b] = VDXS_FLAG_GREEDY;
+        }
+        for (int s = tid; s < p.out_k; s += NT) {
+            if (p.out_idx) p.out_idx[(int64_t)b * p.out_k + s] = s == 0 ? (int32_t)si[0] : -1;
+            if (p.out_prob) p.out_prob[(int64_t)b * p.out_k + s] = 0.0f;
+        }
+        return;
+    }
+    unsigned char* work = (unsigned char*)(ckey);
+    work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
+    uint32_t f2;
+    VDXS_T0(t_s2);
+    const bool faithful = stage2_canonical(p, b, sk, si, nsel, gmax, kb, btie, work, sh + 32, &f2);
+    VDXS_T1(6, t_s2);
+    if (faithful) {
+        VDXS_T0(t_ff);
+        faithful_row<T>(p, b, f2, region, sh + 32);
+        VDXS_T1(7, t_ff);
+    }
+}
+
 template <typename T>
 __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint32_t* hist, uint32_t* sh) {
     const int tid = threadIdx.x;
@@ -1202,53 +1263,8 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     }
     const int n2 = (int)sh[40];
     const uint32_t gmax = block_max_u32(lm, sh + 32);
-    const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
-    const SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
-    const int nsel = block_emit(SmemPairSrc{ckey, cidx}, n2, s2, sk, si, K, &sh[8], IdentIdx{cidx});
-    // The boundary value is the smallest selected key. A boundary tie exists when the
-    // merge cut elements of that value, or a span cut elements of that value.
-    uint32_t kb = 0xFFFFFFFFu;
-    for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
-    kb = block_min_u32(kb, sh + 32);
-    uint32_t ck_tie = 0u;
-    for (int i = tid; i < nsp; i += NT) {
-        const uint2 ci = __ldcg(p.chunk_info + item_of(i));
-        if (ci.y != 0u && ci.y == kb) ck_tie = 1u;
-    }
-    ck_tie = block_max_u32(ck_tie, sh + 32);
-    const uint32_t btie = (s2.tie_cut || ck_tie) ? VDXS_FLAG_BOUNDARY_TIE : 0u;
-    if (tid == 0) p.row_counter[b] = 0u;  // ready for the next launch
-
-    if (p.local_emit) {
-        // Vocab-sharded: publish the local top-K and tie evidence for the all-gather.
-        uint2* eo = p.emit_out + (int64_t)b * (K + 1);
-        for (int s = tid; s < K; s += NT) eo[s] = s < nsel ? make_uint2(sk[s], si[s]) : make_uint2(0u, 0xFFFFFFFFu);
-        if (tid == 0) eo[K] = make_uint2(kb, btie ? 1u : 0u);
-        return;
-    }
-    if (p.path == kGreedy) {
-        // Greedy (Sampler.pas:305-322): the canonical top-1 is the first maximum.
-        if (tid == 0) {
-            p.tokens[b] = (int32_t)si[0];
-            if (p.flags) p.flags[b] = VDXS_FLAG_GREEDY;
-        }
-        for (int s = tid; s < p.out_k; s += NT) {
-            if (p.out_idx) p.out_idx[(int64_t)b * p.out_k + s] = s == 0 ? (int32_t)si[0] : -1;
-            if (p.out_prob) p.out_prob[(int64_t)b * p.out_k + s] = 0.0f;
-        }
-        return;
-    }
-    unsigned char* work = (unsigned char*)(ckey);
-    work = (unsigned char*)(((uintptr_t)work + 15) & ~(uintptr_t)15);
-    uint32_t f2;
-    VDXS_T0(t_s2);
-    const bool faithful = stage2_canonical(p, b, sk, si, nsel, gmax, kb, btie, work, sh + 32, &f2);
-    VDXS_T1(6, t_s2);
-    if (faithful) {
-        VDXS_T0(t_ff);
-        faithful_row<T>(p, b, f2, region, sh + 32);
-        VDXS_T1(7, t_ff);
-    }
+    finish_select<T>(p, b, ckey, cidx, n2, gmax, nsp,
+                     [&](int i) -> uint32_t { return __ldcg(&p.chunk_info[item_of(i)].y); }, region, hist, sh);
 }
 
 template <typename T>
@@ -2248,6 +2264,206 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------------
+// Small batches: one thread-block cluster of kClusterCTAs CTAs per row. Each CTA copies
+// its 1/kClusterCTAs of the row into shared memory (one bulk copy stream, no
+// multicast), masks the penalised ids, and sends each thread's maximum to the leader
+// CTA through distributed shared memory. The K-th largest of those maxima is a lower
+// bound on the row's K-th key (they are K distinct elements of the row); every CTA then
+// sends the leader its elements at or above it, or, if more than its slot holds, its
+// exact top-K with tie evidence. The leader runs stage 2 on what it gathered.
+// ---------------------------------------------------------------------------------
+constexpr int kClusterCTAs = 8;
+constexpr int kClusterMaxRows = 8;  // batches up to this size take the cluster path
+
+template <typename T>
+__device__ __forceinline__ T nan_bits();
+template <>
+__device__ __forceinline__ float nan_bits<float>() { return __uint_as_float(0x7FC00000u); }
+template <>
+__device__ __forceinline__ uint16_t nan_bits<uint16_t>() { return (uint16_t)0x7FC0u; }
+
+template <typename T>
+struct ChunkKeySrc {  // keys of a row chunk in shared memory (NaN: no element), tie-break = position
+    const T* xs;
+    int n;
+    __device__ __forceinline__ uint32_t key(int i) const {
+        if (i >= n) return 0u;
+        const float v = to_f(xs[i]);
+        return v == v ? f2key(v) : 0u;
+    }
+    __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
+};
+
+template <typename T, bool TMA>
+__global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) row_cluster_kernel(KParams p) {
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    __shared__ uint64_t s_bar;
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int r = (int)cl.block_rank();
+    const int b = blockIdx.y;
+    const int K = p.K;
+    const int L = p.chunk;      // elements per CTA (a multiple of 16)
+    const int cap = p.cand_cap; // candidate slots per CTA at the leader (>= K)
+    const int64_t lo = (int64_t)r * L;
+    const int n = (int)max((int64_t)0, min((int64_t)L, (int64_t)p.V - lo));
+    T* xs = (T*)region;
+    uint32_t* maxk = (uint32_t*)(region + p.span);  // p.span: bytes of the chunk area
+    const int ncap = kClusterCTAs * cap + p.pen_stride;
+    uint32_t* ckey = maxk + kClusterCTAs * NT;
+    uint32_t* cidx = ckey + ncap;
+    uint32_t* cuts = cidx + ncap;  // [kClusterCTAs]
+    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+
+    // 1. The chunk into shared memory.
+    VDXS_T0(t_c1);
+    bool timed_out = false;
+    if constexpr (TMA) {
+        const uint32_t bytes = (uint32_t)((size_t)n * sizeof(T)) & ~15u;
+        if (tid == 0) {
+            mbar_init(&s_bar, 1);
+            fence_mbar_init();
+            if (bytes) {
+                mbar_arrive_expect_tx(&s_bar, bytes);
+                for (uint32_t off = 0; off < bytes; off += 32768u)
+                    tma_load_1d((unsigned char*)xs + off, (const unsigned char*)(row + lo) + off, min(32768u, bytes - off),
+                                &s_bar);
+            } else {
+                mbar_arrive(&s_bar);
+            }
+        }
+        __syncthreads();
+        for (int i = (int)(bytes / sizeof(T)) + tid; i < n; i += NT) xs[i] = row[lo + i];  // ragged tail
+        if (!mbar_wait_bounded(&s_bar, 0u)) timed_out = true;
+        __syncthreads();
+        if (tid == 0) mbar_inval(&s_bar);
+    } else {
+        for (int i = tid; i < n; i += NT) xs[i] = row[lo + i];
+    }
+    __syncthreads();
+    if (timed_out && tid == 0) atomicExch(p.err, kErrTimeout);
+    VDXS_T1(20, t_c1);
+    VDXS_T0(t_c2);
+    // 2. Penalised ids are excluded here (they re-enter in stage 2 with their values).
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+    if (npen > 0) {
+        for (int j = tid; j < npen; j += NT) {
+            const int64_t id = pid[j];
+            if (id >= lo && id < lo + n) xs[id - lo] = nan_bits<T>();
+        }
+        __syncthreads();
+    }
+    // 3. Bound: this CTA's K-th largest thread maximum (K distinct elements of the row at
+    // or above it), raised into the leader's bound; the leader keeps the largest.
+    if (r == 0 && tid == 0) {
+        sh[19] = 0u;  // bound
+        sh[41] = 0u;  // candidates reserved
+        sh[42] = 0u;  // overflow
+    }
+    float m0 = __uint_as_float(0x7FC00000u), m1 = m0, m2 = m0, m3 = m0;
+    int i = tid;
+    for (; i + 3 * NT < n; i += 4 * NT) {
+        m0 = fmaxf(m0, to_f(xs[i]));
+        m1 = fmaxf(m1, to_f(xs[i + NT]));
+        m2 = fmaxf(m2, to_f(xs[i + 2 * NT]));
+        m3 = fmaxf(m3, to_f(xs[i + 3 * NT]));
+    }
+    for (; i < n; i += NT) m0 = fmaxf(m0, to_f(xs[i]));
+    const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+    // (key, thread) composites are distinct, so exactly one thread has rank K-1.
+    uint64_t* mk = (uint64_t*)maxk;
+    const uint64_t mine = ((uint64_t)(mx == mx ? f2key(mx) : 0u) << 32) | (uint32_t)tid;
+    mk[tid] = mine;
+    cl.sync();  // also publishes the leader's zeroed scalars
+    if (K <= NT) {
+        int rank = 0;
+        for (int j = 0; j < NT; ++j) rank += mk[j] > mine ? 1 : 0;
+        if (rank == K - 1 && (uint32_t)(mine >> 32) != 0u) atomicMax(cl.map_shared_rank(&sh[19], 0), (uint32_t)(mine >> 32));
+    }
+    cl.sync();
+    VDXS_T1(21, t_c2);
+    VDXS_T0(t_c3);
+    const uint32_t t0 = *cl.map_shared_rank(&sh[19], 0);
+    // 4. Elements at or above the bound go to the leader, packed by warp reservations.
+    uint32_t* lkey = cl.map_shared_rank(ckey, 0);
+    uint32_t* lidx = cl.map_shared_rank(cidx, 0);
+    uint32_t* lcnt = cl.map_shared_rank(&sh[41], 0);
+    uint32_t* lovf = cl.map_shared_rank(&sh[42], 0);
+    const uint32_t gbase = (uint32_t)(p.vocab_offset + lo);
+    const uint32_t total_cap = (uint32_t)(kClusterCTAs * cap);
+    for (int i0 = 0; i0 < n; i0 += NT) {
+        const int ii = i0 + tid;
+        float v = 0.0f;
+        bool sel = false;
+        if (ii < n) {
+            v = to_f(xs[ii]);
+            sel = v == v && f2key(v) >= t0;
+        }
+        const unsigned mm = __ballot_sync(FULL, sel);
+        if (mm == 0u) continue;
+        uint32_t base = 0u;
+        if (lane == 0) base = atomicAdd(lcnt, (uint32_t)__popc(mm));
+        base = __shfl_sync(FULL, base, 0);
+        if (base + (uint32_t)__popc(mm) > total_cap) {
+            if (lane == 0) atomicOr(lovf, 1u);
+            continue;
+        }
+        if (sel) {
+            const uint32_t s2 = base + __popc(mm & lanemask_lt());
+            lkey[s2] = f2key(v);
+            lidx[s2] = gbase + (uint32_t)ii;
+        }
+    }
+    cl.sync();
+    const bool overflow = *lovf != 0u;
+    if (overflow) {
+        // Many keys at the bound (e.g. equal logits): every CTA sends its exact top-K
+        // with tie evidence to its own slot instead.
+        uint32_t km = 0u;
+        for (int j = tid; j < n; j += NT) km = max(km, ChunkKeySrc<T>{xs, n}.key(j));
+        km = block_max_u32(km, sh + 32);
+        const SelectOut so = block_select(ChunkKeySrc<T>{xs, n}, n, K, km, bits_for((uint32_t)max(n - 1, 1)), hist, sh);
+        const int sent = block_emit(ChunkKeySrc<T>{xs, n}, n, so, lkey + r * cap, lidx + r * cap, cap, &sh[8],
+                                    OffsetIdx{gbase});
+        if (tid == 0) {
+            cl.map_shared_rank(sh + 48, 0)[r] = (uint32_t)sent;
+            cl.map_shared_rank(cuts, 0)[r] = so.tie_cut ? so.kth_key : 0u;
+        }
+        cl.sync();
+    }
+    VDXS_T1(22, t_c3);
+    if (r != 0) return;
+    VDXS_T0(t_c4);
+    // 5. Leader: stage 2 on the gathered candidates and penalised entries.
+    int nc;
+    if (overflow) {
+        for (int j = tid; j < kClusterCTAs * cap; j += NT)
+            if ((uint32_t)(j % cap) >= sh[48 + j / cap]) ckey[j] = 0u;  // unused slots: no element
+        nc = kClusterCTAs * cap;
+    } else {
+        nc = (int)sh[41];
+        for (int j = tid; j < kClusterCTAs; j += NT) cuts[j] = 0u;
+    }
+    for (int j = tid; j < npen; j += NT) {
+        ckey[nc + j] = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
+        cidx[nc + j] = (uint32_t)(pid[j] + p.vocab_offset);
+    }
+    __syncthreads();
+    const int n2 = nc + npen;
+    uint32_t gm = 0u;
+    for (int j = tid; j < n2; j += NT) gm = max(gm, ckey[j]);
+    gm = block_max_u32(gm, sh + 32);
+    finish_select<T>(p, b, ckey, cidx, n2, gm, kClusterCTAs, [&](int i) -> uint32_t { return cuts[i]; }, region, hist,
+                     sh);
+    VDXS_T1(23, t_c4);
+}
+
 // Stage 2 as its own kernel (one CTA per row) after topk_stream_kernel.
 template <typename T>
 __global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
@@ -2810,6 +3026,30 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     const int pen_stride = a.penalty_on ? (int)std::min<int64_t>(a.hist_stride, kMaxHistory) : 0;
     const size_t esz = a.dtype == VDXS_DTYPE_BF16 ? 2 : 4;
     const bool faithful = a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit;
+    if (a.B <= kClusterMaxRows) {
+        // Small batches: one cluster per row when a row's 1/8 fits in shared memory.
+        const int64_t L = ((V + kClusterCTAs - 1) / kClusterCTAs + 15) / 16 * 16;
+        const int cap = std::max(K, 512);
+        size_t xs_area = align16((size_t)L * esz);
+        xs_area = std::max(xs_area, align16((size_t)8 * K + 16));  // finish_select's sk / si
+        if (faithful) xs_area = std::max(xs_area, align16(faithful_bytes(K)));
+        const size_t ncap = (size_t)kClusterCTAs * cap + pen_stride;
+        const int P2 = pow2_at_least(K, 32);
+        const size_t cand_area = std::max((size_t)8 * ncap, (size_t)24 * P2 + 64);  // also stage 2's work
+        const size_t need = kHeadBytes + xs_area + (size_t)4 * kClusterCTAs * NT + cand_area + 4 * kClusterCTAs + 16;
+        if ((int64_t)need + 1024 <= smem_optin && L <= INT32_MAX) {  // 1 KB: the kernel's static shared memory
+            plan->cluster = true;
+            plan->stream = false;
+            plan->chunk = (int)L;
+            plan->span = (int)xs_area;
+            plan->cand_cap = cap;
+            plan->nchunks = 1;
+            plan->nspans = 1;
+            plan->items = 0;
+            plan->smem = align16(need);
+            return cudaSuccess;
+        }
+    }
     if (K <= kWarpMaxK) {
         // Stream path: persistent stage 1 (two CTAs per SM) + one finish CTA per row.
         int dev = 0, sms = 148, per_sm = 0;
@@ -3158,6 +3398,16 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
     }
     const size_t esz = sizeof(T);
     const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0);
+    if (plan.cluster) {
+        void (*kc)(KParams) = vec ? row_cluster_kernel<T, true> : row_cluster_kernel<T, false>;
+        if ((e = cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem)) != cudaSuccess)
+            return e;
+        if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
+        kc<<<dim3(kClusterCTAs, a.B), NT, plan.smem, a.stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        count(a);
+        return mark(a, a.ev_end);
+    }
     if (plan.stream) {
         void (*k1)(KParams) = nullptr;
         const int R = plan.elems;
