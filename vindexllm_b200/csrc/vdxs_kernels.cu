@@ -2397,29 +2397,67 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     uint32_t* lovf = cl.map_shared_rank(&sh[42], 0);
     const uint32_t gbase = (uint32_t)(p.vocab_offset + lo);
     const uint32_t total_cap = (uint32_t)(kClusterCTAs * cap);
-    for (int i0 = 0; i0 < n; i0 += NT) {
-        const int ii = i0 + tid;
-        float v = 0.0f;
-        bool sel = false;
-        if (ii < n) {
-            v = to_f(xs[ii]);
-            sel = v == v && f2key(v) >= t0;
-        }
-        const unsigned mm = __ballot_sync(FULL, sel);
-        if (mm == 0u) continue;
+    // Each warp gathers its candidates locally (its 1 KB of the maxima area, free now)
+    // and reserves the leader's slots once per batch of up to kWarpBatch.
+    constexpr int kWarpBatch = (kClusterCTAs * NT * 4) / (NWARPS * 8);  // 128 (key, index) pairs
+    uint32_t* wk = maxk + (size_t)(tid >> 5) * (2 * kWarpBatch);
+    uint32_t* wi = wk + kWarpBatch;
+    int wn = 0;
+    auto flush = [&]() {
         uint32_t base = 0u;
-        if (lane == 0) base = atomicAdd(lcnt, (uint32_t)__popc(mm));
+        if (lane == 0) base = atomicAdd(lcnt, (uint32_t)wn);
         base = __shfl_sync(FULL, base, 0);
-        if (base + (uint32_t)__popc(mm) > total_cap) {
+        if (base + (uint32_t)wn > total_cap) {
             if (lane == 0) atomicOr(lovf, 1u);
-            continue;
+        } else {
+            for (int j = lane; j < wn; j += 32) {
+                lkey[base + j] = wk[j];
+                lidx[base + j] = wi[j];
+            }
         }
+        wn = 0;
+        __syncwarp();
+    };
+    __syncthreads();  // every thread is done with the maxima area
+    const float thr = key_threshold(t0);
+    auto append = [&](bool sel, float v, int ii) {
+        const unsigned mm = __ballot_sync(FULL, sel);
+        if (mm == 0u) return;
+        if (wn + __popc(mm) > kWarpBatch) flush();
         if (sel) {
-            const uint32_t s2 = base + __popc(mm & lanemask_lt());
-            lkey[s2] = f2key(v);
-            lidx[s2] = gbase + (uint32_t)ii;
+            const int s2 = wn + __popc(mm & lanemask_lt());
+            wk[s2] = f2key(v);
+            wi[s2] = gbase + (uint32_t)ii;
         }
+        wn += __popc(mm);
+        __syncwarp();
+    };
+    // 16-byte groups: one lane-maximum test per group, per-element appends only when
+    // some lane of the warp has a candidate.
+    constexpr int VN = (int)(16 / sizeof(T));
+    const int ngrp = n / VN;
+    for (int g0 = (tid >> 5) * 32; g0 < ngrp; g0 += NT) {
+        const int g = g0 + lane;
+        float x[VN];
+        if (g < ngrp) {
+            unpack(*reinterpret_cast<const uint4*>(xs + (size_t)g * VN), x, T());
+        } else {
+#pragma unroll
+            for (int e = 0; e < VN; ++e) x[e] = __uint_as_float(0x7FC00000u);
+        }
+        float gm = x[0];
+#pragma unroll
+        for (int e = 1; e < VN; ++e) gm = fmaxf(gm, x[e]);
+        if (!__any_sync(FULL, gm >= thr)) continue;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) append(x[e] >= thr, x[e], g * VN + e);
     }
+    for (int i0 = ngrp * VN + (tid >> 5) * 32; i0 < n; i0 += NT) {  // the last < VN elements
+        const int ii = i0 + lane;
+        const float v = ii < n ? to_f(xs[ii]) : __uint_as_float(0x7FC00000u);
+        append(v >= thr, v, ii);
+    }
+    if (wn > 0) flush();
     cl.sync();
     const bool overflow = *lovf != 0u;
     if (overflow) {
