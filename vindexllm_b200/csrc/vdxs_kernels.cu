@@ -352,6 +352,24 @@ __device__ void bitonic_sort_desc(uint64_t* a, int n) {
     }
 }
 
+// Descending sort of a[0, n) (n <= P2, a power of two) where a[0, nvalid) are distinct
+// non-zero keys and a[nvalid, P2) are zero. Up to NT keys: each thread's rank among the
+// valid keys is its position (two barriers); above that, the bitonic network.
+__device__ void block_sort_desc_distinct(uint64_t* a, int nvalid, int P2) {
+    if (P2 > NT) {
+        bitonic_sort_desc(a, P2);
+        return;
+    }
+    const int tid = threadIdx.x;
+    const uint64_t mine = tid < nvalid ? a[tid] : 0ull;
+    int rank = 0;
+    if (tid < nvalid)
+        for (int j = 0; j < nvalid; ++j) rank += a[j] > mine ? 1 : 0;
+    __syncthreads();
+    if (tid < nvalid) a[rank] = mine;
+    __syncthreads();
+}
+
 // Warp 0 only: first bin g of hist[0..nb) whose inclusive prefix reaches `need`.
 // Writes sh[0] = g (or -1), sh[1] = count before g, sh[2] = total.
 __device__ void warp_find(const uint32_t* hist, int nb, uint32_t need, uint32_t* sh) {
@@ -631,7 +649,7 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
     for (int s = tid; s < P2; s += NT)
         sortb[s] = s < nsel ? (((uint64_t)__float_as_uint(q[s]) << 32) | (uint64_t)(~si[s])) : 0ull;
     __syncthreads();
-    bitonic_sort_desc(sortb, P2);
+    block_sort_desc_distinct(sortb, nsel, P2);  // indices are distinct, ~index is non-zero
     uint32_t cnt = 0u, emin = 0xFFFFFFFFu;
     for (int s = tid; s < P2; s += NT) {
         float v = s < nsel ? __uint_as_float((uint32_t)(sortb[s] >> 32)) : 0.0f;
@@ -953,7 +971,7 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
         for (int s = tid; s < P2; s += NT)
             sortb[s] = s < K ? (((uint64_t)__float_as_uint(prob[s]) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)s)) : 0ull;
         __syncthreads();
-        bitonic_sort_desc(sortb, P2);
+        block_sort_desc_distinct(sortb, K, P2);  // slots are distinct, 0xFFFFFFFF - slot is non-zero
         for (int s = tid; s < K; s += NT) {
             const uint32_t slot = 0xFFFFFFFFu - (uint32_t)sortb[s];
             wid[s] = sidx[slot];
