@@ -793,88 +793,81 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
 template <typename T>
 __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigned char* work,
                              uint32_t* shu) {
-    __shared__ float s_mv;
-    __shared__ int s_isum[NWARPS + 1];
+    // Pipeline in one CTA: warp 0 is the scanner (the reference's strict-'>' insertions
+    // and lowest-slot minimum in index order); warps 1-7 are producers that load the next
+    // tile into one of two slots, overlay the penalised values, and compact, in index
+    // order, the elements that can still enter the buffer. Their prefilter is the
+    // scanner's current buffer minimum: it only grows, so it is a lower bound on the
+    // minimum when each element is scanned. Slots are handed over by flags; every wait
+    // is bounded and an abort flag ends both sides.
+    __shared__ volatile float s_mv;
+    __shared__ volatile int s_ready[2], s_done[2], s_abort;
+    __shared__ int s_cnt[2];
+    __shared__ int s_wc[NWARPS];
+    __shared__ int s_pstop;      // producers' stop decision for this tile (one writer)
+    __shared__ float s_ptau;     // producers' prefilter bound for this tile (one writer)
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K, V = p.V;
     const T* row = (const T*)p.logits + (int64_t)b * p.stride;
     float* sval = (float*)work;
     int32_t* sidx = (int32_t*)(sval + K);
-    float* tile = (float*)(sidx + K);
-    uint16_t* cpos = (uint16_t*)(tile + kFaithfulTile);
-    unsigned char* tail = (unsigned char*)(cpos + kFaithfulTile);
+    float* tiles = (float*)(sidx + K);                          // [2][kFaithfulTile]
+    uint16_t* cposs = (uint16_t*)(tiles + 2 * kFaithfulTile);  // [2][kFaithfulTile]
+    unsigned char* tail = (unsigned char*)(cposs + 2 * kFaithfulTile);
     tail = (unsigned char*)(((uintptr_t)tail + 15) & ~(uintptr_t)15);
     const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
     const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
     const float* pvl = p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr;
-
-    // Warp-0 state: per-lane minimum over slots {lane, lane+32, ...} and the global one.
-    float mv = -INFINITY;
-    int ms = 0;
-    if (tid == 0) s_mv = -INFINITY;
-    // Tiles grow geometrically from 256 elements, so the prefilter (the buffer minimum
-    // after the previous tile) tightens before many elements reach the sequential scan.
-    int tsz = 256;
+    // Tiles grow from 256 elements (so the prefilter tightens before many elements reach
+    // the scanner) to kFaithfulTile.
+    auto tile_base = [](int t) -> int64_t {
+        return t < 4 ? (int64_t)256 * ((1 << t) - 1) : (int64_t)3840 + (int64_t)(t - 4) * kFaithfulTile;
+    };
+    auto tile_size = [](int t) -> int { return t < 4 ? 256 << t : kFaithfulTile; };
+    int ntiles = 0;
+    while (tile_base(ntiles) < V) ++ntiles;
+    // Bounded wait of one thread until *f >= target; false on abort or timeout.
+    auto wait_at_least = [&](volatile int* f, int target) -> bool {
+        const uint64_t t0 = global_ns();
+        while (*f < target) {
+            if (s_abort) return false;
+            if (global_ns() - t0 > 2000000000ull) {
+                s_abort = 1;
+                return false;
+            }
+        }
+        __threadfence_block();
+        return true;
+    };
+    if (tid == 0) {
+        s_mv = -INFINITY;
+        s_ready[0] = s_ready[1] = 0;
+        s_done[0] = s_done[1] = 0;
+        s_abort = 0;
+    }
     __syncthreads();
     VDXS_T0(t_floop);
-    for (int64_t base = 0; base < V; base += tsz, tsz = min(2 * tsz, kFaithfulTile)) {
-        VDXS_T0(t_ftile);
-        const int n = (int)min((int64_t)tsz, (int64_t)V - base);
-        {
-            // All loads of the tile are issued before any is stored (one DRAM round trip).
-            constexpr int RT = kFaithfulTile / NT;
-            float v[RT];
-#pragma unroll
-            for (int r = 0; r < RT; ++r) {
-                const int i = tid + r * NT;
-                v[r] = i < n ? ld_elem(row, base + i) : 0.0f;
-            }
-#pragma unroll
-            for (int r = 0; r < RT; ++r) {
-                const int i = tid + r * NT;
-                if (i < n) tile[i] = v[r];
-            }
-        }
-        __syncthreads();
-        if (npen) {
-            const int j0 = lower_bound_i32(pid, npen, base);
-            for (int j = j0 + tid; j < npen && pid[j] < base + n; j += NT) tile[pid[j] - base] = pvl[j];
-            __syncthreads();
-        }
-        // Order-preserving compaction of the elements that can enter the buffer: warp w
-        // takes a contiguous segment in steps of 32 (ballots), then the warps' counts are
-        // scanned; reads are lane-contiguous, so free of bank conflicts.
-        const float tau = s_mv;
-        const int seg = ((n + NWARPS * 32 - 1) / (NWARPS * 32)) * 32;
-        const int w0 = warp * seg, w1 = min(w0 + seg, n);
-        int wc = 0;
-        for (int i0 = w0; i0 < w1; i0 += 32) {
-            const int i = i0 + lane;
-            const bool c = i < w1 && (base + i < K || tile[i] > tau);
-            wc += __popc(__ballot_sync(FULL, c));
-        }
-        if (lane == 0) s_isum[warp] = wc;
-        __syncthreads();
-        int off = 0, total = 0;
-        for (int w = 0; w < NWARPS; ++w) {
-            const int v = s_isum[w];
-            off += w < warp ? v : 0;
-            total += v;
-        }
-        for (int i0 = w0; i0 < w1; i0 += 32) {
-            const int i = i0 + lane;
-            const bool c = i < w1 && (base + i < K || tile[i] > tau);
-            const unsigned m = __ballot_sync(FULL, c);
-            if (c) cpos[off + __popc(m & lanemask_lt())] = (uint16_t)i;
-            off += __popc(m);
-        }
-        __syncthreads();
-        VDXS_T1(20, t_ftile);
+    if (warp == 0) {
+        // Scanner. Per-lane state: the buffer minimum and its slot.
+        float mv = -INFINITY;
+        int ms = 0;
+        for (int t = 0; t < ntiles; ++t) {
+            const int sl = t & 1;
+            bool ok = true;
+            VDXS_T0(t_sw);
+            if (lane == 0) ok = wait_at_least(&s_ready[sl], t + 1);
+            ok = __shfl_sync(FULL, ok, 0);
+            __syncwarp();
+            VDXS_T1(25, t_sw);
+            if (!ok) break;
+            VDXS_T0(t_ss);
+            const int64_t base = tile_base(t);
+            const int total = s_cnt[sl];
+            const float* tile = tiles + (size_t)sl * kFaithfulTile;
+            const uint16_t* cpos = cposs + (size_t)sl * kFaithfulTile;
 #ifdef VDXS_TIMING
-        if (tid == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
+            if (lane == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
 #endif
-        VDXS_T0(t_fscan);
-        if (warp == 0) {
             for (int c0 = 0; c0 < total; c0 += 32) {
                 const int c = c0 + lane;
                 const bool valid = c < total;
@@ -906,17 +899,17 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
                     }
                     __syncwarp();
 #ifdef VDXS_TIMING
-                    if (changed && tid == 0) atomicAdd(&g_phase_count[24], 1ull);
+                    if (changed && lane == 0) atomicAdd(&g_phase_count[24], 1ull);
 #endif
                     if (changed) {
                         // Recompute per-lane minima (first slot with strict '<' wins ties).
                         float bv = 0.0f;
                         int bs = INT_MAX;
-                        for (int s = lane; s < K; s += 32) {
-                            const float x = sval[s];
+                        for (int s2 = lane; s2 < K; s2 += 32) {
+                            const float x = sval[s2];
                             if (bs == INT_MAX || x < bv) {
                                 bv = x;
-                                bs = s;
+                                bs = s2;
                             }
                         }
                         const uint32_t kv = bs == INT_MAX ? 0xFFFFFFFFu : f2key(bv);
@@ -929,12 +922,106 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
                     pend &= __ballot_sync(FULL, valid && (gi < K || v > mv));
                 }
             }
-            if (lane == 0) s_mv = mv;
+            __syncwarp();
+            VDXS_T1(26, t_ss);
+            if (lane == 0) {
+                s_mv = mv;
+                __threadfence_block();
+                s_done[sl] = t + 1;  // the slot may be refilled
+            }
         }
-        VDXS_T1(21, t_fscan);
-        __syncthreads();
+    } else {
+        // Producers (warps 1..7, named barrier 1).
+        const int pt = tid - 32, pw = warp - 1;
+        constexpr int NP = NT - 32;
+        auto pbar = [] { asm volatile("bar.sync 1, %0;" ::"n"(NT - 32) : "memory"); };
+        for (int t = 0; t < ntiles; ++t) {
+            const int sl = t & 1;
+            // One thread decides for the group (stop, and the prefilter bound); everyone
+            // reads its decision after the barrier, so the group stays together.
+#ifdef VDXS_TIMING
+            long long t_pw = clock64();
+#endif
+            if (pt == 0) {
+                const bool ok = wait_at_least(&s_done[sl], t - 1);  // tile t-2 scanned
+                if (!ok) s_abort = 1;
+                s_pstop = ok ? 0 : 1;
+                s_ptau = s_mv;
+            }
+            pbar();
+#ifdef VDXS_TIMING
+            if (pt == 0) { atomicAdd(&g_phase_cycles[27], (unsigned long long)(clock64() - t_pw)); atomicAdd(&g_phase_count[27], 1ull); }
+            long long t_pl = clock64();
+#endif
+            if (s_pstop) break;
+            const int64_t base = tile_base(t);
+            const int n = (int)min((int64_t)tile_size(t), (int64_t)V - base);
+            float* tile = tiles + (size_t)sl * kFaithfulTile;
+            uint16_t* cpos = cposs + (size_t)sl * kFaithfulTile;
+            {
+                // All loads of this thread are issued before any is stored.
+                constexpr int RT = (kFaithfulTile + NP - 1) / NP;
+                float v[RT];
+#pragma unroll
+                for (int r = 0; r < RT; ++r) {
+                    const int i = pt + r * NP;
+                    v[r] = i < n ? ld_elem(row, base + i) : 0.0f;
+                }
+#pragma unroll
+                for (int r = 0; r < RT; ++r) {
+                    const int i = pt + r * NP;
+                    if (i < n) tile[i] = v[r];
+                }
+            }
+            pbar();
+            if (npen) {
+                const int j0 = lower_bound_i32(pid, npen, base);
+                for (int j = j0 + pt; j < npen && pid[j] < base + n; j += NP) tile[pid[j] - base] = pvl[j];
+                pbar();
+            }
+            // Order-preserving compaction: producer warp pw takes a contiguous segment.
+            const float tau = s_ptau;
+            const int seg = ((n + (NWARPS - 1) * 32 - 1) / ((NWARPS - 1) * 32)) * 32;
+            const int w0 = min(pw * seg, n), w1 = min(w0 + seg, n);
+            int wc = 0;
+            for (int i0 = w0; i0 < w1; i0 += 32) {
+                const int i = i0 + lane;
+                const bool c = i < w1 && (base + i < K || tile[i] > tau);
+                wc += __popc(__ballot_sync(FULL, c));
+            }
+            if (lane == 0) s_wc[pw] = wc;
+            pbar();
+            int off = 0, total = 0;
+            for (int w = 0; w < NWARPS - 1; ++w) {
+                const int v = s_wc[w];
+                off += w < pw ? v : 0;
+                total += v;
+            }
+            for (int i0 = w0; i0 < w1; i0 += 32) {
+                const int i = i0 + lane;
+                const bool c = i < w1 && (base + i < K || tile[i] > tau);
+                const unsigned m = __ballot_sync(FULL, c);
+                if (c) cpos[off + __popc(m & lanemask_lt())] = (uint16_t)i;
+                off += __popc(m);
+            }
+            pbar();  // also: every producer has read s_wc before it is rewritten
+#ifdef VDXS_TIMING
+            if (pt == 0) { atomicAdd(&g_phase_cycles[28], (unsigned long long)(clock64() - t_pl)); atomicAdd(&g_phase_count[28], 1ull); }
+#endif
+            if (pt == 0) {
+                s_cnt[sl] = total;
+                __threadfence_block();
+                s_ready[sl] = t + 1;
+            }
+        }
     }
+    __syncthreads();
     VDXS_T1(22, t_floop);
+    if (s_abort) {
+        // A wait ran out: report it; the token of this row is not valid.
+        if (tid == 0) atomicExch(p.err, kErrTimeout);
+        return;
+    }
 
     // Sequential stage 2 in slot order (Sampler.pas:385-459).
     int P2 = 32;
@@ -3071,9 +3158,9 @@ static size_t stage2_bytes(int K, int n2) {
     return (size_t)8 * K + std::max(math, cands) + 16;
 }
 
-static size_t faithful_bytes(int K) {
+static size_t faithful_bytes(int K) {  // sval/sidx, two (tile, positions) slots, stage-2 tail
     const int P2 = pow2_at_least(K, 32);
-    return (size_t)8 * K + (size_t)6 * kFaithfulTile + 16 + (size_t)16 * P2 + 16;
+    return (size_t)8 * K + (size_t)12 * kFaithfulTile + 16 + (size_t)16 * P2 + 16;
 }
 
 cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std::string* err) {
