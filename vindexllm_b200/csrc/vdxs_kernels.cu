@@ -937,11 +937,22 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
         auto pbar = [] { asm volatile("bar.sync 1, %0;" ::"n"(NT - 32) : "memory"); };
         for (int t = 0; t < ntiles; ++t) {
             const int sl = t & 1;
-            // One thread decides for the group (stop, and the prefilter bound); everyone
-            // reads its decision after the barrier, so the group stays together.
+            const int64_t base = tile_base(t);
+            const int n = (int)min((int64_t)tile_size(t), (int64_t)V - base);
+            // Issue this tile's loads first (into registers): they fly while the group
+            // waits for its slot.
+            constexpr int RT = (kFaithfulTile + NP - 1) / NP;
+            float v[RT];
+#pragma unroll
+            for (int r = 0; r < RT; ++r) {
+                const int i = pt + r * NP;
+                v[r] = i < n ? ld_elem(row, base + i) : 0.0f;
+            }
 #ifdef VDXS_TIMING
             long long t_pw = clock64();
 #endif
+            // One thread decides for the group (stop, and the prefilter bound); everyone
+            // reads its decision after the barrier, so the group stays together.
             if (pt == 0) {
                 const bool ok = wait_at_least(&s_done[sl], t - 1);  // tile t-2 scanned
                 if (!ok) s_abort = 1;
@@ -954,24 +965,12 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
             long long t_pl = clock64();
 #endif
             if (s_pstop) break;
-            const int64_t base = tile_base(t);
-            const int n = (int)min((int64_t)tile_size(t), (int64_t)V - base);
             float* tile = tiles + (size_t)sl * kFaithfulTile;
             uint16_t* cpos = cposs + (size_t)sl * kFaithfulTile;
-            {
-                // All loads of this thread are issued before any is stored.
-                constexpr int RT = (kFaithfulTile + NP - 1) / NP;
-                float v[RT];
 #pragma unroll
-                for (int r = 0; r < RT; ++r) {
-                    const int i = pt + r * NP;
-                    v[r] = i < n ? ld_elem(row, base + i) : 0.0f;
-                }
-#pragma unroll
-                for (int r = 0; r < RT; ++r) {
-                    const int i = pt + r * NP;
-                    if (i < n) tile[i] = v[r];
-                }
+            for (int r = 0; r < RT; ++r) {
+                const int i = pt + r * NP;
+                if (i < n) tile[i] = v[r];
             }
             pbar();
             if (npen) {
