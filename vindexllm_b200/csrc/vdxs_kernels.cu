@@ -785,49 +785,45 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
 // ---------------------------------------------------------------------------------
 // Faithful emulation of the reference min-buffer (Sampler.pas:341-383) over one row,
 // followed by the reference's sequential double arithmetic (Sampler.pas:385-459).
-// Tiles of the row are staged in shared memory; all threads pre-filter each tile
-// against the current buffer minimum (it only grows, so nothing that the reference
-// would insert is filtered out) and warp 0 replays the candidates in index order.
-// `work` must hold 8*K + 6*kFaithfulTile + 24*1024 + 64 bytes.
+// `work` must hold faithful_bytes(K) bytes (8*K for the buffer, the candidate ring,
+// then the stage-2 tail).
 // ---------------------------------------------------------------------------------
 template <typename T>
 __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigned char* work,
                              uint32_t* shu) {
-    // Pipeline in one CTA: warp 0 is the scanner (the reference's strict-'>' insertions
-    // and lowest-slot minimum in index order); warps 1-7 are producers that load the next
-    // tile into one of two slots, overlay the penalised values, and compact, in index
-    // order, the elements that can still enter the buffer. Their prefilter is the
-    // scanner's current buffer minimum: it only grows, so it is a lower bound on the
-    // minimum when each element is scanned. Slots are handed over by flags; every wait
-    // is bounded and an abort flag ends both sides.
+    // The first K elements fill the buffer in slot order (Sampler.pas:352-356); that is
+    // one parallel pass. The rest of the row runs as a pipeline inside the CTA:
+    // - producer warps 1..7 each take every 7th sub-tile of kFaithfulSub elements,
+    //   overlay the penalised values, and compact, in index order, the elements above
+    //   the scanner's last published buffer minimum into one of kFaithfulSlots ring
+    //   slots. The minimum only grows, so it is a lower bound on the minimum that each
+    //   element meets and nothing the reference would insert is dropped;
+    // - warp 0 (the scanner) replays the candidates in index order: an element strictly
+    //   above the minimum replaces the minimum's slot, and the lowest slot holding the
+    //   minimum value becomes the next one. Lane l keeps the minimum of the slots
+    //   s = l (mod 32); an insertion rescans only the owning lane's slots, and two warp
+    //   reductions give the new (minimum, lowest slot).
+    // Slots are handed over by flags; every wait is bounded and an abort flag ends both
+    // sides.
     __shared__ volatile float s_mv;
-    __shared__ volatile int s_ready[2], s_done[2], s_abort;
-    __shared__ int s_cnt[2];
-    __shared__ int s_wc[NWARPS];
-    __shared__ int s_pstop;      // producers' stop decision for this tile (one writer)
-    __shared__ float s_ptau;     // producers' prefilter bound for this tile (one writer)
+    __shared__ volatile int s_ready[kFaithfulSlots];
+    __shared__ volatile int s_scanned, s_abort;
+    __shared__ int s_cnt[kFaithfulSlots];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K, V = p.V;
     const T* row = (const T*)p.logits + (int64_t)b * p.stride;
     float* sval = (float*)work;
     int32_t* sidx = (int32_t*)(sval + K);
-    float* tiles = (float*)(sidx + K);                          // [2][kFaithfulTile]
-    uint16_t* cposs = (uint16_t*)(tiles + 2 * kFaithfulTile);  // [2][kFaithfulTile]
-    unsigned char* tail = (unsigned char*)(cposs + 2 * kFaithfulTile);
+    float* rval = (float*)(sidx + K);                                   // [slots][sub]
+    int32_t* ridx = (int32_t*)(rval + kFaithfulSlots * kFaithfulSub);  // [slots][sub]
+    unsigned char* tail = (unsigned char*)(ridx + kFaithfulSlots * kFaithfulSub);
     tail = (unsigned char*)(((uintptr_t)tail + 15) & ~(uintptr_t)15);
     const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
     const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
     const float* pvl = p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr;
-    // Tiles grow from 256 elements (so the prefilter tightens before many elements reach
-    // the scanner) to kFaithfulTile.
-    auto tile_base = [](int t) -> int64_t {
-        return t < 4 ? (int64_t)256 * ((1 << t) - 1) : (int64_t)3840 + (int64_t)(t - 4) * kFaithfulTile;
-    };
-    auto tile_size = [](int t) -> int { return t < 4 ? 256 << t : kFaithfulTile; };
-    int ntiles = 0;
-    while (tile_base(ntiles) < V) ++ntiles;
+    const int nsub = (int)(((int64_t)V - K + kFaithfulSub - 1) / kFaithfulSub);  // K < V
     // Bounded wait of one thread until *f >= target; false on abort or timeout.
-    auto wait_at_least = [&](volatile int* f, int target) -> bool {
+    auto wait_at_least = [&](volatile int* f, int target, bool nap) -> bool {
         const uint64_t t0 = global_ns();
         while (*f < target) {
             if (s_abort) return false;
@@ -835,182 +831,207 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
                 s_abort = 1;
                 return false;
             }
+            if (nap) __nanosleep(64);
         }
         __threadfence_block();
         return true;
     };
+    // Minimum of the slots this lane owns; the first slot wins ties (strict '<'). Eight
+    // slots are loaded at a time so that their latencies overlap.
+    auto lane_min = [&](int& bs) -> uint32_t {
+        float bv = 0.0f;
+        bs = INT_MAX;
+        for (int s0 = lane; s0 < K; s0 += 32 * 8) {
+            float x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = s0 + 32 * u < K ? sval[s0 + 32 * u] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int s2 = s0 + 32 * u;
+                if (s2 < K && (bs == INT_MAX || x[u] < bv)) {
+                    bv = x[u];
+                    bs = s2;
+                }
+            }
+        }
+        return bs == INT_MAX ? 0xFFFFFFFFu : f2key(bv);
+    };
+
+    for (int s = tid; s < K; s += NT) {
+        sval[s] = ld_elem(row, s);
+        sidx[s] = s;
+    }
+    if (tid < kFaithfulSlots) s_ready[tid] = 0;
     if (tid == 0) {
-        s_mv = -INFINITY;
-        s_ready[0] = s_ready[1] = 0;
-        s_done[0] = s_done[1] = 0;
+        s_scanned = 0;
         s_abort = 0;
+    }
+    __syncthreads();
+    for (int j = tid; j < npen; j += NT) {  // penalised ids ascend
+        const int id = pid[j];
+        if (id >= K) break;
+        sval[id] = pvl[j];
+    }
+    __syncthreads();
+    // Scanner state: per lane the key and slot of its minimum; warp-uniform the buffer
+    // minimum mv and its slot ms.
+    uint32_t kv = 0xFFFFFFFFu;
+    int bs = INT_MAX, ms = 0;
+    float mv = -INFINITY;
+    if (warp == 0) {
+        kv = lane_min(bs);
+        const uint32_t mk = __reduce_min_sync(FULL, kv);
+        ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
+        mv = key2f(mk);
+        if (lane == 0) s_mv = mv;
     }
     __syncthreads();
     VDXS_T0(t_floop);
     if (warp == 0) {
-        // Scanner. Per-lane state: the buffer minimum and its slot.
-        float mv = -INFINITY;
-        int ms = 0;
-        for (int t = 0; t < ntiles; ++t) {
-            const int sl = t & 1;
+        // Every sub-tile that is ready is replayed before the minimum and the scanned
+        // count are published, so the handoff cost is paid once per batch.
+        int t = 0;
+        while (t < nsub) {
             bool ok = true;
             VDXS_T0(t_sw);
-            if (lane == 0) ok = wait_at_least(&s_ready[sl], t + 1);
+            if (lane == 0) ok = wait_at_least(&s_ready[t % kFaithfulSlots], t + 1, false);
             ok = __shfl_sync(FULL, ok, 0);
+            if (!ok) break;
+            const int tl = t + lane;
+            const bool rdy = lane < kFaithfulSlots && tl < nsub && s_ready[tl % kFaithfulSlots] >= tl + 1;
+            const int nready = __ffs(~__ballot_sync(FULL, rdy) | (1u << 31)) - 1;  // >= 1
+            __threadfence_block();
             __syncwarp();
             VDXS_T1(25, t_sw);
-            if (!ok) break;
             VDXS_T0(t_ss);
-            const int64_t base = tile_base(t);
-            const int total = s_cnt[sl];
-            const float* tile = tiles + (size_t)sl * kFaithfulTile;
-            const uint16_t* cpos = cposs + (size_t)sl * kFaithfulTile;
+            for (int k = 0; k < nready; ++k) {
+                const int sl = (t + k) % kFaithfulSlots;
+                const int total = s_cnt[sl];
+                const float* cv = rval + sl * kFaithfulSub;
+                const int32_t* ci = ridx + sl * kFaithfulSub;
 #ifdef VDXS_TIMING
-            if (lane == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
+                if (lane == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
 #endif
-            for (int c0 = 0; c0 < total; c0 += 32) {
-                const int c = c0 + lane;
-                const bool valid = c < total;
-                float v = 0.0f;
-                int64_t gi = -1;
-                if (valid) {
-                    const int i = cpos[c];
-                    v = tile[i];
-                    gi = base + i;
-                }
-                unsigned pend = __ballot_sync(FULL, valid && (gi < K || v > mv));
-                while (pend) {
-                    const int l = __ffs(pend) - 1;
-                    const float vl = __shfl_sync(FULL, v, l);
-                    const int64_t gl = __shfl_sync(FULL, gi, l);
-                    bool changed = false;
-                    if (gl < K) {
-                        if (lane == 0) {
-                            sval[gl] = vl;
-                            sidx[gl] = (int32_t)gl;
+                for (int c0 = 0; c0 < total; c0 += 32) {
+                    const int c = c0 + lane;
+                    const bool valid = c < total;
+                    const float v = valid ? cv[c] : 0.0f;
+                    const int32_t gi = valid ? ci[c] : 0;
+                    unsigned pend = __ballot_sync(FULL, valid && v > mv);
+                    while (pend) {
+                        const int l = __ffs(pend) - 1;
+                        if (lane == l) {
+                            sval[ms] = v;
+                            sidx[ms] = gi;
                         }
-                        changed = gl == K - 1;
-                    } else if (vl > mv) {
-                        if (lane == 0) {
-                            sval[ms] = vl;
-                            sidx[ms] = (int32_t)gl;
-                        }
-                        changed = true;
-                    }
-                    __syncwarp();
+                        __syncwarp();
 #ifdef VDXS_TIMING
-                    if (changed && lane == 0) atomicAdd(&g_phase_count[24], 1ull);
+                        if (lane == 0) atomicAdd(&g_phase_count[24], 1ull);
+                        const long long tq0 = clock64();
 #endif
-                    if (changed) {
-                        // Recompute per-lane minima (first slot with strict '<' wins ties).
-                        float bv = 0.0f;
-                        int bs = INT_MAX;
-                        for (int s2 = lane; s2 < K; s2 += 32) {
-                            const float x = sval[s2];
-                            if (bs == INT_MAX || x < bv) {
-                                bv = x;
-                                bs = s2;
-                            }
-                        }
-                        const uint32_t kv = bs == INT_MAX ? 0xFFFFFFFFu : f2key(bv);
+                        if (lane == (ms & 31)) kv = lane_min(bs);
+#ifdef VDXS_TIMING
+                        __syncwarp();
+                        const long long tq1 = clock64();
+#endif
                         const uint32_t mk = __reduce_min_sync(FULL, kv);
-                        const uint32_t cs = kv == mk ? (uint32_t)bs : 0xFFFFFFFFu;
-                        ms = (int)__reduce_min_sync(FULL, cs);
-                        mv = sval[ms];
+                        ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
+                        mv = key2f(mk);
+#ifdef VDXS_TIMING
+                        if (lane == 0 && threadIdx.x == 0) {
+                            const long long tq2 = clock64();
+                            atomicAdd(&g_phase_cycles[27], (unsigned long long)(tq1 - tq0));
+                            atomicAdd(&g_phase_count[27], 1ull);
+                            atomicAdd(&g_phase_cycles[28], (unsigned long long)(tq2 - tq1));
+                            atomicAdd(&g_phase_count[28], 1ull);
+                        }
+#endif
+                        pend &= ~(1u << l);
+                        pend &= __ballot_sync(FULL, valid && v > mv);
                     }
-                    pend &= ~(1u << l);
-                    pend &= __ballot_sync(FULL, valid && (gi < K || v > mv));
                 }
             }
+            t += nready;
             __syncwarp();
             VDXS_T1(26, t_ss);
             if (lane == 0) {
                 s_mv = mv;
                 __threadfence_block();
-                s_done[sl] = t + 1;  // the slot may be refilled
+                s_scanned = t;  // slots of sub-tiles below t may be refilled
             }
         }
     } else {
-        // Producers (warps 1..7, named barrier 1).
-        const int pt = tid - 32, pw = warp - 1;
-        constexpr int NP = NT - 32;
-        auto pbar = [] { asm volatile("bar.sync 1, %0;" ::"n"(NT - 32) : "memory"); };
-        for (int t = 0; t < ntiles; ++t) {
-            const int sl = t & 1;
-            const int64_t base = tile_base(t);
-            const int n = (int)min((int64_t)tile_size(t), (int64_t)V - base);
-            // Issue this tile's loads first (into registers): they fly while the group
-            // waits for its slot.
-            constexpr int RT = (kFaithfulTile + NP - 1) / NP;
-            float v[RT];
+        // Producer warp w takes sub-tiles w-1, w-1+7, ...; the loads of its next sub-tile
+        // are issued as soon as the current one is published.
+        constexpr int NPW = NWARPS - 1;
+        constexpr int RS = kFaithfulSub / 32;
+        int jc = 0;  // penalty cursor: entries before it lie below the current sub-tile
+        float v[RS];
+        int t = warp - 1;
+        int64_t a = (int64_t)K + (int64_t)t * kFaithfulSub;
 #pragma unroll
-            for (int r = 0; r < RT; ++r) {
-                const int i = pt + r * NP;
-                v[r] = i < n ? ld_elem(row, base + i) : 0.0f;
-            }
-#ifdef VDXS_TIMING
-            long long t_pw = clock64();
-#endif
-            // One thread decides for the group (stop, and the prefilter bound); everyone
-            // reads its decision after the barrier, so the group stays together.
-            if (pt == 0) {
-                const bool ok = wait_at_least(&s_done[sl], t - 1);  // tile t-2 scanned
-                if (!ok) s_abort = 1;
-                s_pstop = ok ? 0 : 1;
-                s_ptau = s_mv;
-            }
-            pbar();
-#ifdef VDXS_TIMING
-            if (pt == 0) { atomicAdd(&g_phase_cycles[27], (unsigned long long)(clock64() - t_pw)); atomicAdd(&g_phase_count[27], 1ull); }
-            long long t_pl = clock64();
-#endif
-            if (s_pstop) break;
-            float* tile = tiles + (size_t)sl * kFaithfulTile;
-            uint16_t* cpos = cposs + (size_t)sl * kFaithfulTile;
+        for (int r = 0; r < RS; ++r) {
+            const int64_t i = a + r * 32 + lane;
+            v[r] = (t < nsub && i < V) ? ld_elem(row, i) : 0.0f;
+        }
+        while (t < nsub) {
+            const int sl = t % kFaithfulSlots;
+            while (npen) {
+                const int j = jc + lane;
+                const int id = j < npen ? pid[j] : INT_MAX;
+                const bool in = id >= a && id < a + kFaithfulSub;
+                const unsigned mb = __ballot_sync(FULL, id < a), mi = __ballot_sync(FULL, in);
+                const float pv = in ? pvl[j] : 0.0f;
+                for (unsigned m = mi; m; m &= m - 1) {
+                    const int l = __ffs(m) - 1;
+                    const int off = (int)(__shfl_sync(FULL, id, l) - a);
+                    const float val = __shfl_sync(FULL, pv, l);
+                    // Select form (no store indexed by a run-time value, so v stays in
+                    // registers).
+                    const int hit = lane == (off & 31) ? (off >> 5) : -1;
 #pragma unroll
-            for (int r = 0; r < RT; ++r) {
-                const int i = pt + r * NP;
-                if (i < n) tile[i] = v[r];
+                    for (int r = 0; r < RS; ++r) v[r] = r == hit ? val : v[r];
+                }
+                const int adv = __popc(mb | mi);
+                jc += adv;
+                if (adv < 32) break;
             }
-            pbar();
-            if (npen) {
-                const int j0 = lower_bound_i32(pid, npen, base);
-                for (int j = j0 + pt; j < npen && pid[j] < base + n; j += NP) tile[pid[j] - base] = pvl[j];
-                pbar();
+            bool ok = true;
+            float tau = 0.0f;
+            if (lane == 0) {
+                ok = wait_at_least(&s_scanned, t - kFaithfulSlots + 1, true);
+                tau = s_mv;
             }
-            // Order-preserving compaction: producer warp pw takes a contiguous segment.
-            const float tau = s_ptau;
-            const int seg = ((n + (NWARPS - 1) * 32 - 1) / ((NWARPS - 1) * 32)) * 32;
-            const int w0 = min(pw * seg, n), w1 = min(w0 + seg, n);
-            int wc = 0;
-            for (int i0 = w0; i0 < w1; i0 += 32) {
-                const int i = i0 + lane;
-                const bool c = i < w1 && (base + i < K || tile[i] > tau);
-                wc += __popc(__ballot_sync(FULL, c));
-            }
-            if (lane == 0) s_wc[pw] = wc;
-            pbar();
-            int off = 0, total = 0;
-            for (int w = 0; w < NWARPS - 1; ++w) {
-                const int v = s_wc[w];
-                off += w < pw ? v : 0;
-                total += v;
-            }
-            for (int i0 = w0; i0 < w1; i0 += 32) {
-                const int i = i0 + lane;
-                const bool c = i < w1 && (base + i < K || tile[i] > tau);
+            ok = __shfl_sync(FULL, ok, 0);
+            tau = __shfl_sync(FULL, tau, 0);
+            if (!ok) break;
+            float* cv = rval + sl * kFaithfulSub;
+            int32_t* ci = ridx + sl * kFaithfulSub;
+            int cnt = 0;
+#pragma unroll
+            for (int r = 0; r < RS; ++r) {
+                const int64_t i = a + r * 32 + lane;
+                const bool c = i < V && v[r] > tau;
                 const unsigned m = __ballot_sync(FULL, c);
-                if (c) cpos[off + __popc(m & lanemask_lt())] = (uint16_t)i;
-                off += __popc(m);
+                if (c) {
+                    const int pos = cnt + __popc(m & lanemask_lt());
+                    cv[pos] = v[r];
+                    ci[pos] = (int32_t)i;
+                }
+                cnt += __popc(m);
             }
-            pbar();  // also: every producer has read s_wc before it is rewritten
-#ifdef VDXS_TIMING
-            if (pt == 0) { atomicAdd(&g_phase_cycles[28], (unsigned long long)(clock64() - t_pl)); atomicAdd(&g_phase_count[28], 1ull); }
-#endif
-            if (pt == 0) {
-                s_cnt[sl] = total;
+            __syncwarp();
+            if (lane == 0) {
+                s_cnt[sl] = cnt;
                 __threadfence_block();
                 s_ready[sl] = t + 1;
+            }
+            t += NPW;
+            a += (int64_t)NPW * kFaithfulSub;
+#pragma unroll
+            for (int r = 0; r < RS; ++r) {
+                const int64_t i = a + r * 32 + lane;
+                v[r] = (t < nsub && i < V) ? ld_elem(row, i) : 0.0f;
             }
         }
     }
@@ -1704,95 +1725,24 @@ __device__ __forceinline__ int warp_compact_selected(uint32_t* k, uint32_t* t, i
     return out;
 }
 
-__device__ __forceinline__ uint32_t warp_min_u32(uint32_t v) { return __reduce_min_sync(FULL, v); }
-__device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) { return __reduce_max_sync(FULL, v); }
-
 // ---------------------------------------------------------------------------------
-// Stream stage 1 for top_k <= kWarpMaxK (persistent; one CTA per SM).
-// Work item = (row, span of span_elems elements). Warp w of the CTA streams the
-// contiguous sub-range [w*SW, (w+1)*SW) of the span (SW = span_elems / 8) through its
-// own ring of TMA slices (kSlice elements each), so warps never wait on one another
-// and each ring keeps loading the next items while the warp computes. Each warp keeps
-// a running top-K of its own stream: its first slice sets a threshold by binary search
-// over the lanes' top-M keys (a lower bound on that slice's K-th key); later slices are
-// filtered strictly against the warp's K-th key (its stream is in index order), the
-// survivors are buffered and merged with a warp-level select when the buffer fills.
-// At the end of an item warp 0 merges the 8 warp lists and publishes the span's top-K.
+// Stream stage 1 (topk_hist_kernel) serves top_k <= kWarpMaxK. Each warp streams
+// kSlice-element TMA slices of its pieces through its own ring of net_ring_slots()
+// slots and keeps the 32*R best (key, index) composites of its stream sorted in
+// registers; candidates above the row threshold are batched in shared memory and
+// merged into that list with a bitonic network when a warp's region overflows.
 // ---------------------------------------------------------------------------------
 constexpr int kWarpMaxK = 128;
 constexpr int kSlice = 512;     // elements per ring slot (16 per lane)
-constexpr int kWarpBuf = 576;   // candidate room per warp beyond its list
-template <typename T>
-__host__ __device__ constexpr int ring_slots() { return sizeof(T) == 4 ? 8 : 16; }
-// Per-warp shared-memory area in 32-bit words, rounded to 128 bytes so that every
-// warp's ring slots stay 16-byte aligned (TMA destinations, 128-bit loads).
-__host__ __device__ constexpr int warp_area_words(int K, int slots, int esz) {
-    return ((slots * kSlice * esz) / 4 + 2 * slots + 2 * (K + kWarpBuf) + kHistBins + kSlice / 32 + 31) & ~31;
-}
 
-struct VirtListSrc {  // the 8 warp lists as one index space: i -> (warp i / K, entry i % K)
-    const uint32_t* base;
-    int stride_words;
-    int K;
-    int cap;
-    const int* cnt;
-    __device__ __forceinline__ uint32_t key(int i) const {
-        const int w = i / K, j = i - w * K;
-        return j < cnt[w] ? base[(size_t)w * stride_words + j] : 0u;
-    }
-    __device__ __forceinline__ uint32_t tb(int i) const {
-        const int w = i / K, j = i - w * K;
-        return base[(size_t)w * stride_words + cap + j];
-    }
-};
-
-template <int M>
-__device__ __forceinline__ uint32_t warp_kth_lower_bound(const uint32_t (&keys)[16], int K) {
-    uint32_t top[M];
-#pragma unroll
-    for (int m = 0; m < M; ++m) top[m] = 0u;
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        uint32_t k = keys[e];
-#pragma unroll
-        for (int m = 0; m < M; ++m) {
-            const uint32_t hi = max(top[m], k);
-            k = min(top[m], k);
-            top[m] = hi;
-        }
-    }
-    int c1 = 0;
-#pragma unroll
-    for (int m = 0; m < M; ++m) c1 += top[m] != 0u;
-    if ((int)__reduce_add_sync(FULL, (uint32_t)c1) < K) return 0u;
-    // Largest t with at least K of the lanes' top-M keys >= t.
-    uint32_t lo = 1u, hi = __reduce_max_sync(FULL, top[0]);
-    while (lo < hi) {
-        const uint32_t mid = lo + ((hi - lo + 1u) >> 1);
-        int c = 0;
-#pragma unroll
-        for (int m = 0; m < M; ++m) c += top[m] >= mid;
-        if ((int)__reduce_add_sync(FULL, (uint32_t)c) >= K) lo = mid;
-        else hi = mid - 1u;
-    }
-    return lo;
-}
-
-// Per-warp area (32-bit words) of topk_net_kernel, rounded to 128 bytes.
 template <typename T>
 __host__ __device__ constexpr int net_ring_slots() { return sizeof(T) == 4 ? 4 : 8; }
+// Per-warp area in 32-bit words, rounded to 128 bytes so that every warp's ring slots
+// stay 16-byte aligned (TMA destinations, 128-bit loads).
 __host__ __device__ constexpr int net_area_words(int R, int slots, int esz) {
     return ((slots * kSlice * esz) / 4 + 2 * slots + 64 * R + kSlice / 32 + 31) & ~31;
 }
 
-// Stream stage 1 on register-resident sorted lists (top_k <= 32*R, R <= 4).
-// Persistent CTAs (two per SM), 8 warps each. Work item = (row, span); warp w streams
-// the contiguous sub-range [w*SW, (w+1)*SW) of the span through its own ring of TMA
-// slices. Each warp keeps the 32*R best (key, index) composites of its stream sorted
-// in registers; candidates that beat the warp's K-th key are batched in shared memory
-// and merged with a bitonic network once the batch holds 32*R entries. The first
-// slice of an item is filtered against a lower bound on its K-th key (binary search
-// over the lanes' top-M keys). At the end of an item warp 0 merges the 8 lists.
 // Merges a warp's candidate batch (bcount entries of buf) into its sorted list, then
 // refreshes its K-th key `tau` and the largest dropped key `max_cut`.
 template <int R>
@@ -1814,14 +1764,6 @@ __device__ __forceinline__ void net_merge_batch(uint64_t (&lst)[R], const uint64
     tau = max(tau, (uint32_t)(kth >> 32));
     __syncwarp();
     VDXS_T1(11, t_mg);
-}
-
-template <int M>
-__device__ __forceinline__ uint32_t warp_kth_lower_bound_f(const float (&x)[16], int K) {
-    uint32_t keys[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) keys[e] = x[e] == x[e] ? f2key(x[e]) : 0u;  // NaN marks an empty slot
-    return warp_kth_lower_bound<M>(keys, K);
 }
 
 // ---------------------------------------------------------------------------------
@@ -2606,7 +2548,7 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     VDXS_T1(23, t_c4);
 }
 
-// Stage 2 as its own kernel (one CTA per row) after topk_stream_kernel.
+// Per-row finish (one CTA per row), launched as a programmatic dependent of topk_hist_kernel.
 template <typename T>
 __global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -3157,9 +3099,9 @@ static size_t stage2_bytes(int K, int n2) {
     return (size_t)8 * K + std::max(math, cands) + 16;
 }
 
-static size_t faithful_bytes(int K) {  // sval/sidx, two (tile, positions) slots, stage-2 tail
+static size_t faithful_bytes(int K) {  // sval/sidx, the (value, index) candidate ring, stage-2 tail
     const int P2 = pow2_at_least(K, 32);
-    return (size_t)8 * K + (size_t)12 * kFaithfulTile + 16 + (size_t)16 * P2 + 16;
+    return (size_t)8 * K + (size_t)8 * kFaithfulSlots * kFaithfulSub + 16 + (size_t)16 * P2 + 16;
 }
 
 cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std::string* err) {
