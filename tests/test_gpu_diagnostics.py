@@ -25,11 +25,11 @@ def test_device_status_clean_after_calls(gpu_ctx):
     gpu_ctx.device_status()  # raises VdxsError on a non-zero device error word
 
 
-@pytest.mark.parametrize("name,batch,per_call", [("c4", 16, 2), ("c1", 16, 3), ("c3", 16, 1), ("c4", 2, 1),
+@pytest.mark.parametrize("name,batch,per_call", [("c4", 16, 2), ("c1", 16, 3), ("c3", 16, 2), ("c4", 2, 1),
                                                  ("c1", 2, 2)])
 def test_launch_count(gpu_ctx, name, batch, per_call):
-    """Kernels per call: stream select + finish (k <= 128), one fused span kernel for
-    k > 128, one cluster kernel for batches of at most 8; + penalty prep when a history
+    """Kernels per call: stream stage 1 + finish (k <= 128, and the wide stream for
+    k > 128), one cluster kernel for batches of at most 8; + penalty prep when a history
     is given."""
     x, h, c, u = _inputs(name, batch)
     cfg = synth.sampler_config(name)

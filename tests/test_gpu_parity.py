@@ -91,6 +91,32 @@ def test_edge_cases(gpu_ctx, oracle_mod, mode):
 
 
 @pytest.mark.parametrize("mode", MODES)
+def test_wide_topk_edge_cases(gpu_ctx, oracle_mod, mode):
+    """top_k above 128 at batches above 8 (the wide stream path). Constant rows make
+    every piece's list outgrow its capacity and one-bin rows overflow the finish gather,
+    so both reach the exact whole-row fallback; ascending rows and tied rows with a
+    repetition penalty take the ordinary gather."""
+    rng = np.random.default_rng(23)
+    B = 12
+    cases = [("constant", np.zeros((B, 262144), np.float32), 200)]
+    V = 40000
+    cases.append(("ascending", (np.arange(V, dtype=np.float32) * 1e-3)[None, :].repeat(B, 0), 300))
+    d = (1.0 + np.arange(V, dtype=np.float64) * 2.0 ** -22).astype(np.float32)[None, :].repeat(B, 0)
+    cases.append(("one_bin_shuffled", rng.permuted(d, axis=1), 1024))
+    q = (np.round(rng.normal(size=(B, 100000)) * 4) / 4).astype(np.float32)
+    cases.append(("quantised", q, 512))
+    for name, x, K in cases:
+        hist = rng.integers(0, x.shape[1], size=(B, 64)).astype(np.int32)
+        cnt = np.full(B, 64, np.int32)
+        for cfg in [default_config(temperature=1.0, top_k=K, top_p=0.9, repeat_penalty=1.2),
+                    default_config(temperature=0.0, top_k=K)]:
+            u = rng.random(B).astype(np.float32)
+            g = gpu_run(gpu_ctx, cfg, _t(x), u, _t(hist), _t(cnt), mode, out_k=K)
+            o = oracle_run(oracle_mod, cfg, x, u, hist, cnt, mode, out_k=K)
+            compare(g, o, mode, label=f"{name} K{K} {cfg.as_dict()}")
+
+
+@pytest.mark.parametrize("mode", MODES)
 def test_strided_and_unaligned_rows(gpu_ctx, oracle_mod, mode):
     import torch
     rng = np.random.default_rng(7)

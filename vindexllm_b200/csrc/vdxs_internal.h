@@ -101,6 +101,7 @@ struct LaunchPlan {
     bool cluster = false; // top-k path, small batches: one thread-block cluster per row
     int grid = 0;         // stream kernel grid (CTAs)
     int cand_cap = 0;     // top-k path: candidates each stage-1 item may write
+    int gather_cap = 0;   // wide stream path: finish kernel gather capacity (0 = other paths)
     long long items = 0;  // top-k path: stage-1 item slots (candidate lists)
     int flat_ng = 0;      // stream path: granules per row of the flat partition (0 = spans)
     int flat_pmax = 0;    // stream path: pieces per CTA

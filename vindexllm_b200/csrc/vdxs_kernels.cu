@@ -84,6 +84,7 @@ struct KParams {
     // workspace
     uint2* cand;        // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
     int cand_cap;       // candidates each stage-1 item may write
+    int gather_cap;     // finish kernel: fixed gather capacity (0 = nsp * cand_cap)
     uint2* chunk_info;  // [items] (candidate count, largest key dropped by an exact cut)
     uint32_t* item_tau; // [items] the item's lower bound on its row's K-th key (0 = none)
     // Flat partition of the stream path (flat_ng > 0): the B x ng granules of kSlice
@@ -438,9 +439,15 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
     r.tie_cut = 0;
     for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
     __syncthreads();
-    for (int i = tid; i < n; i += NT) {
-        uint32_t k = src.key(i);
-        if (k) atomicAdd(&hist[logbin(kmax - k)], 1u);
+    // Every pass loads four elements per thread before it counts them, so that reads
+    // from global memory (a row source) overlap.
+    for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+        uint32_t k[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (k[u]) atomicAdd(&hist[logbin(kmax - k[u])], 1u);
     }
     __syncthreads();
     if (tid < 32) warp_find(hist, kHistBins, (uint32_t)K, sh);
@@ -466,11 +473,14 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
         const uint32_t width = 1u << bits;
         for (int i = tid; i < 256; i += NT) hist[i] = 0u;
         __syncthreads();
-        for (int i = tid; i < n; i += NT) {
-            uint32_t k = src.key(i);
-            if (k) {
-                uint32_t dd = (kmax - k) - dlo;
-                if (dd < width) atomicAdd(&hist[dd >> shift], 1u);
+        for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+            uint32_t k[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t dd = (kmax - k[u]) - dlo;
+                if (k[u] && dd < width) atomicAdd(&hist[dd >> shift], 1u);
             }
         }
         __syncthreads();
@@ -499,10 +509,16 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
         const uint32_t hi_mask = tbits >= 32 ? 0u : (0xFFFFFFFFu << tbits);
         for (int i = tid; i < 256; i += NT) hist[i] = 0u;
         __syncthreads();
-        for (int i = tid; i < n; i += NT) {
-            if (src.key(i) == r.kth_key) {
-                uint32_t t = src.tb(i);
-                if (((t ^ tlo) & hi_mask) == 0u) atomicAdd(&hist[(t >> shift) & ((1u << w) - 1u)], 1u);
+        for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+            bool eq[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) eq[u] = i0 + u * NT < n && src.key(i0 + u * NT) == r.kth_key;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (eq[u]) {
+                    const uint32_t t = src.tb(i0 + u * NT);
+                    if (((t ^ tlo) & hi_mask) == 0u) atomicAdd(&hist[(t >> shift) & ((1u << w) - 1u)], 1u);
+                }
             }
         }
         __syncthreads();
@@ -1210,25 +1226,26 @@ __device__ int block_emit(const Src& src, int n, const SelectOut& s, uint32_t* o
     const int tid = threadIdx.x;
     if (tid == 0) *counter = 0u;
     __syncthreads();
-    const int rounds = (n + NT - 1) / NT;
-    for (int j = 0; j < rounds; ++j) {
-        const int i = j * NT + tid;
-        uint32_t k = 0u;
-        bool sel = false;
-        if (i < n) {
-            k = src.key(i);
-            sel = selected(k, src.tb(i), s);
-        }
-        const unsigned m = __ballot_sync(FULL, sel);
-        if (m) {
-            uint32_t base = 0u;
-            if ((tid & 31) == 0) base = atomicAdd(counter, (uint32_t)__popc(m));
-            base = __shfl_sync(FULL, base, 0);
-            if (sel) {
-                const uint32_t slot = base + __popc(m & lanemask_lt());
-                if (slot < (uint32_t)cap) {
-                    ok[slot] = k;
-                    oi[slot] = idx_of(i);
+    for (int i0 = tid; i0 - tid < n; i0 += 4 * NT) {
+        uint32_t k[4];
+        bool sel[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sel[u] = i0 + u * NT < n && selected(k[u], src.tb(i0 + u * NT), s);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const unsigned m = __ballot_sync(FULL, sel[u]);
+            if (m) {
+                uint32_t base = 0u;
+                if ((tid & 31) == 0) base = atomicAdd(counter, (uint32_t)__popc(m));
+                base = __shfl_sync(FULL, base, 0);
+                if (sel[u]) {
+                    const uint32_t slot = base + __popc(m & lanemask_lt());
+                    if (slot < (uint32_t)cap) {
+                        ok[slot] = k[u];
+                        oi[slot] = idx_of(i0 + u * NT);
+                    }
                 }
             }
         }
@@ -1311,6 +1328,59 @@ __device__ void finish_select(const KParams& p, int b, uint32_t* ckey, uint32_t*
 }
 
 template <typename T>
+struct RowKeySrc {  // a row in global memory (NaN: no element), tie-break = position
+    const T* row;
+    __device__ __forceinline__ uint32_t key(int i) const {
+        const float v = ld_elem(row, i);
+        return v == v ? f2key(v) : 0u;
+    }
+    __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
+};
+
+// Exact fallback of the finish for a row whose stage-1 lists are incomplete or do not
+// fit the gather: the top (K + npen) of the raw row (penalties not applied) contain the
+// top K of its non-penalised elements, so that select, with the penalised ids among it
+// replaced by their penalised entries, gives finish_select the same candidates as a
+// complete gather. Elements equal to the select's boundary key that it left out are
+// reported as a cut. ckey/cidx hold gcap >= K + npen entries each (cidx = ckey + gcap).
+template <typename T>
+__device__ __noinline__ void finish_row_exact(const KParams& p, int b, uint32_t* ckey, int gcap, unsigned char* region,
+                                 uint32_t* hist, uint32_t* sh) {
+    const int tid = threadIdx.x;
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+    const float* pvl = p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr;
+    uint32_t* cidx = ckey + gcap;
+    const RowKeySrc<T> src{(const T*)p.logits + (int64_t)b * p.stride};
+    uint32_t km = 0u;
+    for (int i0 = tid; i0 < p.V; i0 += 4 * NT) {
+        uint32_t k[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < p.V ? src.key(i0 + u * NT) : 0u;
+        km = max(max(km, max(k[0], k[1])), max(k[2], k[3]));
+    }
+    km = block_max_u32(km, sh + 32);
+    const int kx = min(p.K + npen, gcap - npen);  // the plan makes gcap - npen >= K + npen
+    const SelectOut so = block_select(src, p.V, kx, km, bits_for((uint32_t)(p.V - 1)), hist, sh);
+    const int m = block_emit(src, p.V, so, ckey, cidx, gcap - npen, &sh[8], OffsetIdx{(uint32_t)p.vocab_offset});
+    for (int i = tid; i < m; i += NT) {
+        const int64_t local = (int64_t)cidx[i] - p.vocab_offset;
+        const int j = lower_bound_i32(pid, npen, local);
+        if (j < npen && pid[j] == local) ckey[i] = 0u;  // re-enters with its penalised value
+    }
+    for (int j = tid; j < npen; j += NT) {
+        ckey[m + j] = f2key(pvl[j]);
+        cidx[m + j] = (uint32_t)(pid[j] + p.vocab_offset);
+    }
+    __syncthreads();
+    uint32_t gm = 0u;
+    for (int i = tid; i < m + npen; i += NT) gm = max(gm, ckey[i]);
+    gm = block_max_u32(gm, sh + 32);
+    const uint32_t cut = so.tie_cut ? so.kth_key : 0u;
+    finish_select<T>(p, b, ckey, cidx, m + npen, gm, 1, [&](int) -> uint32_t { return cut; }, region, hist, sh);
+}
+
+template <typename T>
 __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint32_t* hist, uint32_t* sh) {
     const int tid = threadIdx.x;
     const int K = p.K;
@@ -1340,31 +1410,64 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     uint32_t tb = 0u;
     for (int i = tid; i < nsp; i += NT) tb = max(tb, __ldcg(&p.item_tau[item_of(i)]));
     tb = block_max_u32(tb, sh + 32);
-    uint32_t* cidx = ckey + (nsp * cc + npen);  // capacity of the gathered arrays
+    // Capacity of the gathered arrays. The wide stream path gathers into a fixed
+    // capacity; an incomplete item list (count > cand_cap) or a gather that does not fit
+    // sends the row to the exact fallback below.
+    const bool wide = p.gather_cap > 0;
+    const int gcap = wide ? p.gather_cap + npen : nsp * cc + npen;
+    uint32_t* cidx = ckey + gcap;
     uint32_t lm = 0u;
+    bool incomplete = false;
+    VDXS_T0(t_gather);
     {
-        // Gather the variable-length item lists; warp w takes items w, w+8, ...
         const int lane = tid & 31;
         if (tid == 0) sh[40] = 0u;
         __syncthreads();
-        for (int it = tid >> 5; it < nsp; it += NWARPS) {
-            const int64_t ii = item_of(it);
-            const int c = (int)min(__ldcg(&p.chunk_info[ii].x), (uint32_t)cc);
-            const uint2* src = p.cand + ii * cc;
-            for (int j0 = 0; j0 < c; j0 += 32) {
-                const int j = j0 + lane;
-                uint2 e = make_uint2(0u, 0u);
-                if (j < c) e = __ldcg(src + j);
-                const bool keep = j < c && e.x >= tb;
-                const unsigned m = __ballot_sync(FULL, keep);
-                uint32_t base = 0u;
-                if (lane == 0 && m) base = atomicAdd(&sh[40], (uint32_t)__popc(m));
-                base = __shfl_sync(FULL, base, 0);
-                if (keep) {
-                    const uint32_t pos = base + __popc(m & lanemask_lt());
-                    ckey[pos] = e.x;
-                    cidx[pos] = e.y;
-                    lm = max(lm, e.x);
+        // Appends the kept entries of a warp-uniform step at slots from a shared counter.
+        auto put = [&](bool keep, uint32_t k, uint32_t ix) {
+            const unsigned m = __ballot_sync(FULL, keep);
+            uint32_t base = 0u;
+            if (lane == 0 && m) base = atomicAdd(&sh[40], (uint32_t)__popc(m));
+            base = __shfl_sync(FULL, base, 0);
+            if (keep) {
+                const uint32_t pos = base + __popc(m & lanemask_lt());
+                if (pos < (uint32_t)gcap) {
+                    ckey[pos] = k;
+                    cidx[pos] = ix;
+                }
+                lm = max(lm, k);
+            }
+        };
+        if (wide) {
+            // Long raw lists: the whole CTA walks each list, four loads in flight per thread.
+            for (int it = 0; it < nsp; ++it) {
+                const int64_t ii = item_of(it);
+                const uint32_t craw = __ldcg(&p.chunk_info[ii].x);
+                incomplete |= craw > (uint32_t)cc;
+                const int c = (int)min(craw, (uint32_t)cc);
+                const uint2* src = p.cand + ii * cc;
+                for (int j0 = 0; j0 < c; j0 += 4 * NT) {
+                    uint2 e[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = j0 + u * NT + tid;
+                        e[u] = j < c ? __ldcg(src + j) : make_uint2(0u, 0u);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) put(j0 + u * NT + tid < c && e[u].x >= tb, e[u].x, e[u].y);
+                }
+            }
+        } else {
+            // Short lists: warp w takes items w, w+8, ...
+            for (int it = tid >> 5; it < nsp; it += NWARPS) {
+                const int64_t ii = item_of(it);
+                const int c = (int)min(__ldcg(&p.chunk_info[ii].x), (uint32_t)cc);
+                const uint2* src = p.cand + ii * cc;
+                for (int j0 = 0; j0 < c; j0 += 32) {
+                    const int j = j0 + lane;
+                    uint2 e = make_uint2(0u, 0u);
+                    if (j < c) e = __ldcg(src + j);
+                    put(j < c && e.x >= tb, e.x, e.y);
                 }
             }
         }
@@ -1372,21 +1475,19 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
             const int j = j0 + tid;
             uint32_t k = 0u;
             if (j < npen) k = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
-            const bool keep = j < npen && k >= tb;
-            const unsigned m = __ballot_sync(FULL, keep);
-            uint32_t base = 0u;
-            if (lane == 0 && m) base = atomicAdd(&sh[40], (uint32_t)__popc(m));
-            base = __shfl_sync(FULL, base, 0);
-            if (keep) {
-                const uint32_t pos = base + __popc(m & lanemask_lt());
-                ckey[pos] = k;
-                cidx[pos] = (uint32_t)(pid[j] + p.vocab_offset);
-                lm = max(lm, k);
-            }
+            put(j < npen && k >= tb, k, j < npen ? (uint32_t)(pid[j] + p.vocab_offset) : 0u);
         }
         __syncthreads();
     }
+    VDXS_T1(29, t_gather);
     const int n2 = (int)sh[40];
+    if (__syncthreads_or(incomplete) || n2 > gcap) {
+#ifdef VDXS_TIMING
+        if (tid == 0) atomicAdd(&g_phase_count[30], 1ull);
+#endif
+        finish_row_exact<T>(p, b, ckey, gcap, region, hist, sh);
+        return;
+    }
     const uint32_t gmax = block_max_u32(lm, sh + 32);
     finish_select<T>(p, b, ckey, cidx, n2, gmax, nsp,
                      [&](int i) -> uint32_t { return __ldcg(&p.chunk_info[item_of(i)].y); }, region, hist, sh);
@@ -2311,6 +2412,333 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
 }
 
 // ---------------------------------------------------------------------------------
+// Stream stage 1 for kWarpMaxK < top_k <= kMaxTopK. Same flat partition, per-warp TMA
+// rings and threshold histogram as topk_hist_kernel, but a warp appends the elements
+// of a slice that reach the threshold straight to its piece's candidate list in global
+// memory (one shared-memory reservation per warp and slice), and nothing is selected
+// here: every element at or above the piece's final threshold is in the list, so no
+// key at or above the row's K-th key is ever dropped. The finish kernel gathers the
+// entries at or above the row's best bound and selects; a list that outgrows its
+// capacity (count > cand_cap) sends the row to the finish kernel's exact fallback.
+// ---------------------------------------------------------------------------------
+template <typename T, bool TMA>
+__global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint32_t* hist = (uint32_t*)smem_raw;
+    uint32_t* sh = hist + kHistWords;
+    unsigned char* region = smem_raw + kHeadBytes;
+    constexpr int RS = net_ring_slots<T>();
+    constexpr int VN = TMA ? (int)(16 / sizeof(T)) : 1;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int K = p.K;
+    const int WW = net_area_words(0, RS, (int)sizeof(T));
+    uint32_t* wa = (uint32_t*)region + (size_t)warp * WW;
+    T* ring = (T*)wa;
+    uint64_t* full = (uint64_t*)(wa + (RS * kSlice * (int)sizeof(T)) / 4);
+    uint32_t* wbm = (uint32_t*)(full + RS);
+    uint32_t* H = (uint32_t*)region + (size_t)NWARPS * WW;
+    uint32_t* G = H + kTBins;
+    volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current piece
+    uint32_t* s_out = sh + 23;         // entries appended to the current piece's list
+    const float NANF = __uint_as_float(0x7FC00000u);
+    const uint32_t cap = (uint32_t)p.cand_cap;
+    // The threshold is re-derived from the histogram after this many new candidates.
+    const uint32_t raise_every = (uint32_t)max(8, K / 32);
+    const int ng = p.flat_ng;
+    const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
+    const long long g_end = flat_start(p.flat_ngt, gridDim.x, blockIdx.x + 1);
+    const int b_first = (int)(g_begin / ng);
+    const int npieces = g_end > g_begin ? (int)((g_end - 1) / ng) - b_first + 1 : 0;
+    auto warp_range = [&](int j, int64_t& lo, int64_t& hi) {
+        const long long rb = (long long)(b_first + j) * ng;
+        const long long glo = max(g_begin, rb) - rb, ghi = min(g_end, rb + ng) - rb;
+        const long long w0 = glo + (ghi - glo) * warp / NWARPS, w1 = glo + (ghi - glo) * (warp + 1) / NWARPS;
+        lo = w0 * kSlice;
+        hi = min(w1 * kSlice, (long long)p.V);
+    };
+    for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
+    if (tid == 0) {
+        sh[20] = 0u;
+        sh[23] = 0u;
+    }
+    __syncthreads();
+
+    int pj_prod = -1, pq = 0, pns = 0;
+    int64_t pleft = 0;
+    const T* psrc = nullptr;
+    uint32_t pn = 0;
+    auto next_piece = [&]() {
+        for (;;) {
+            if (++pj_prod >= npieces) return;
+            int64_t lo, hi;
+            warp_range(pj_prod, lo, hi);
+            if (hi > lo) {
+                pleft = hi - lo;
+                pns = (int)((pleft + kSlice - 1) / kSlice);
+                psrc = (const T*)p.logits + (int64_t)(b_first + pj_prod) * p.stride + lo;
+                pq = 0;
+                return;
+            }
+        }
+    };
+    auto issue = [&]() {
+        if (pq >= pns) next_piece();
+        if (pj_prod >= npieces) return;
+        const int nn = (int)min((int64_t)kSlice, pleft - (int64_t)pq * kSlice);
+        const int slot = (int)(pn % RS);
+        const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
+        if (bytes) {
+            mbar_arrive_expect_tx(&full[slot], bytes);
+            tma_load_1d(ring + (size_t)slot * kSlice, psrc + (int64_t)pq * kSlice, bytes, &full[slot]);
+        } else {
+            mbar_arrive(&full[slot]);
+        }
+        ++pn;
+        ++pq;
+    };
+    if constexpr (TMA) {
+        if (lane == 0) {
+            for (int s = 0; s < RS; ++s) mbar_init(&full[s], 1);
+            fence_mbar_init();
+            for (int s = 0; s < RS; ++s) issue();
+        }
+        __syncwarp();
+    }
+    auto load_ring = [&](float (&x)[16], int slot, int n, const T* row, int64_t start) {
+        const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
+        const T* sl = ring + (size_t)slot * kSlice;
+#pragma unroll
+        for (int j = 0; j < 16 / VN; ++j) {
+            const int pos = (j * 32 + lane) * VN;
+            if (pos + VN <= n_tma) {
+                unpack(*reinterpret_cast<const uint4*>(sl + pos), &x[j * VN], T());
+            } else {
+#pragma unroll
+                for (int e = 0; e < VN; ++e) {
+                    const int i = pos + e;
+                    x[j * VN + e] = i < n ? (i < n_tma ? to_f(sl[i]) : ld_elem(row, start + i)) : NANF;
+                }
+            }
+        }
+    };
+    // Penalised history ids are excluded from stage 1 (they re-enter in stage 2).
+    auto mask_penalised = [&](float (&x)[16], const int32_t* pid, int npen, int& pj, int64_t start, int n) {
+        if (lane < kSlice / 32) wbm[lane] = 0u;
+        __syncwarp();
+        for (;;) {
+            const int j = pj + lane;
+            const bool in = j < npen && pid[j] < start + n;
+            if (in) {
+                const int d = (int)(pid[j] - start);
+                atomicOr(&wbm[d >> 5], 1u << (d & 31));
+            }
+            const unsigned m = __ballot_sync(FULL, in);
+            pj += __popc(m);
+            if (m != FULL) break;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+            if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
+        }
+        __syncwarp();
+    };
+    auto count_slice = [&](const float (&x)[16]) {
+        const float m = max16(x);
+        if (m == m) {
+            const uint32_t k = f2key(m);
+            atomicAdd(&H[k >> 20], 1u);
+            atomicAdd(&G[k >> 26], 1u);
+        }
+    };
+
+    uint32_t cn = 0;
+    bool timed_out = false;
+    for (int j = 0; j < npieces; ++j) {
+        const int b = b_first + j;
+        const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+        const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+        const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+        const int item = (int)blockIdx.x * p.flat_pmax + j;
+        uint2* out = p.cand + (size_t)item * p.cand_cap;
+        int64_t a0, a1;
+        warp_range(j, a0, a1);
+        const int ns = a1 > a0 ? (int)((a1 - a0 + kSlice - 1) / kSlice) : 0;
+        int pj = 0;
+        uint32_t since = 0u;
+        if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
+        uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
+        uint32_t rtau_next = ld_relaxed_u32(rtp);
+        int ncounted = 0;
+        if constexpr (TMA) {
+            // Counting phase: every element of the first slices already in the rings is
+            // counted into the bins (a large K needs more than one lane maximum per lane
+            // to start near the K-th key); the group totals are then summed from the
+            // bins once, and every warp takes the threshold.
+            ncounted = min(RS, ns);
+            int pjc = pj;
+            for (int q = 0; q < ncounted; ++q) {
+                const int64_t start = a0 + (int64_t)q * kSlice;
+                const int n = (int)min((int64_t)kSlice, a1 - start);
+                const uint32_t c = cn + (uint32_t)q;
+                if (!mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
+                float x[16];
+                load_ring(x, (int)(c % RS), n, row, start);
+                if (npen > 0) mask_penalised(x, pid, npen, pjc, start, n);
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                    if (x[e] == x[e]) atomicAdd(&H[f2key(x[e]) >> 20], 1u);
+            }
+            __syncthreads();
+            {
+                constexpr int BPT = kTBins / NT;  // bins summed per thread, within one group
+                uint32_t sum = 0u;
+#pragma unroll
+                for (int i = 0; i < BPT; ++i) sum += H[tid * BPT + i];
+                if (sum) atomicAdd(&G[(tid * BPT) >> 6], sum);
+            }
+            __syncthreads();
+            const uint32_t t = hist_threshold(H, G, K);
+            if (lane == 0 && t > *s_T) {
+                atomicMax((uint32_t*)s_T, t);
+                if (t > rtau_next) atomicMax(rtp, t);
+            }
+        }
+        VDXS_T0(t_item);
+        for (int q = 0; q < ns; ++q) {
+            const int64_t start = a0 + (int64_t)q * kSlice;
+            const int n = (int)min((int64_t)kSlice, a1 - start);
+            const uint32_t rtau = rtau_next;
+            rtau_next = ld_relaxed_u32(rtp);
+            float x[16];
+            if constexpr (TMA) {
+                const int slot = (int)(cn % RS);
+                if (!mbar_wait_bounded(&full[slot], (cn / RS) & 1u)) timed_out = true;
+                load_ring(x, slot, n, row, start);
+                ++cn;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const int pos = e * 32 + lane;
+                    x[e] = pos < n ? ld_elem(row, start + pos) : NANF;
+                }
+            }
+            if (npen > 0) mask_penalised(x, pid, npen, pj, start, n);
+            bool counted = q < ncounted;
+            if (!TMA && q == 0) {
+                count_slice(x);
+                __syncwarp();
+                const uint32_t t = hist_threshold(H, G, K);
+                if (lane == 0 && t > *s_T) {
+                    atomicMax((uint32_t*)s_T, t);
+                    if (t > rtau) atomicMax(rtp, t);
+                }
+                counted = true;
+            }
+            const float thr = key_threshold(max((uint32_t)*s_T, rtau));
+            const float lmax = max16(x);
+            const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
+            if constexpr (TMA) {
+                if (lane == 0) {
+                    fence_proxy_async_smem();
+                    issue();
+                }
+            }
+            if (lanes == 0u) continue;
+            const uint32_t gb = (uint32_t)(p.vocab_offset + start);
+            uint32_t pm = 0u;
+#pragma unroll
+            for (int e = 0; e < 16; ++e) pm |= (x[e] >= thr ? 1u : 0u) << e;
+            const uint32_t cnt = (uint32_t)__popc(pm);
+            uint32_t total;
+            if (!__any_sync(FULL, cnt > 1u)) {
+                // At most one candidate per lane (the lane maximum): contiguous slots.
+                total = (uint32_t)__popc(lanes);
+                uint32_t base = 0u;
+                if (lane == 0) base = atomicAdd(s_out, total);
+                base = __shfl_sync(FULL, base, 0);
+                if (cnt) {
+                    const int e = __ffs((int)pm) - 1;
+                    const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                    const uint32_t k = f2key(lmax);
+                    const uint32_t slot = base + __popc(lanes & lanemask_lt());
+                    if (slot < cap) out[slot] = make_uint2(k, gb + (uint32_t)pos);
+                    if (!counted) {
+                        atomicAdd(&H[k >> 20], 1u);
+                        atomicAdd(&G[k >> 26], 1u);
+                    }
+                }
+            } else {
+                uint32_t incl = cnt;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const uint32_t o = __shfl_up_sync(FULL, incl, d);
+                    if (lane >= d) incl += o;
+                }
+                total = __shfl_sync(FULL, incl, 31);
+                uint32_t base = 0u;
+                if (lane == 0) base = atomicAdd(s_out, total);
+                base = __shfl_sync(FULL, base, 0);
+                uint32_t slot = base + incl - cnt;
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    if ((pm >> e) & 1u) {
+                        const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
+                        const uint32_t k = f2key(x[e]);
+                        if (slot < cap) out[slot] = make_uint2(k, gb + (uint32_t)pos);
+                        ++slot;
+                        if (!counted) {
+                            atomicAdd(&H[k >> 20], 1u);
+                            atomicAdd(&G[k >> 26], 1u);
+                        }
+                    }
+                }
+            }
+            since += total;
+            if (!counted && since >= raise_every) {
+                since = 0u;
+                __syncwarp();
+                const uint32_t t = hist_threshold(H, G, K);
+                if (lane == 0 && t > *s_T) {
+                    atomicMax((uint32_t*)s_T, t);
+                    if (t > rtau) atomicMax(rtp, t);
+                }
+            }
+            __syncwarp();
+        }
+        VDXS_T1(10, t_item);
+        __syncthreads();
+        if (warp == 0) {
+            // Final threshold of the piece from the complete histogram.
+            const uint32_t t = hist_threshold(H, G, K);
+            if (lane == 0) {
+                const uint32_t tfin = max(max((uint32_t)*s_T, t), ld_relaxed_u32(rtp));
+                p.chunk_info[item] = make_uint2(*s_out, 0u);  // count > cand_cap: list incomplete
+                p.item_tau[item] = tfin;
+#ifdef VDXS_TIMING
+                atomicAdd(&g_phase_count[31], (unsigned long long)*s_out);
+#endif
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
+        if (tid == 0) {
+            sh[20] = 0u;
+            sh[23] = 0u;
+        }
+        __syncthreads();
+    }
+    if (__any_sync(FULL, timed_out) && lane == 0) atomicExch(p.err, kErrTimeout);
+    if constexpr (TMA) {
+        __syncwarp();
+        if (lane == 0)
+            for (int s = 0; s < RS; ++s) mbar_inval(&full[s]);
+    }
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------
 // Small batches: one thread-block cluster of kClusterCTAs CTAs per row. Each CTA copies
 // its 1/kClusterCTAs of the row into shared memory (one bulk copy stream, no
 // multicast), masks the penalised ids, and sends each thread's maximum to the leader
@@ -3179,6 +3607,50 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         plan->smem2 = align16(s2);
         return cudaSuccess;
     }
+    if (K <= kMaxTopK) {
+        // Wide stream path: the same persistent stage 1 without per-warp lists; pieces
+        // append raw candidate lists that the finish kernel gathers at the row's bound.
+        int dev = 0, sms = 148, per_sm = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+        const int rs = esz == 4 ? net_ring_slots<float>() : net_ring_slots<uint16_t>();
+        const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(0, rs, (int)esz) +
+                          (size_t)4 * (kTBins + kTGroups);
+        const int ctas_per_sm = per_sm >= 2 * (int)(align16(s1) + 1024) ? 2 : 1;
+        constexpr long long kMinGranules = 16;
+        const int ng = (int)((V + kSlice - 1) / kSlice);
+        const long long ngt = (long long)a.B * ng;
+        const int grid = (int)std::max<long long>(1, std::min<long long>((long long)sms * ctas_per_sm, ngt / kMinGranules));
+        const long long gmax_cta = (ngt + grid - 1) / grid, gmin_cta = std::max<long long>(1, ngt / grid);
+        const int pmax = (int)((gmax_cta - 1) / ng + 2);
+        const int ipr = (int)((ng + gmin_cta - 1) / gmin_cta + 1);
+        // Raw list of a piece: its elements that met the running threshold (about
+        // K * (1 + ln(piece / K)) plus the boundary bin); a longer list is incomplete and
+        // the row takes the finish kernel's exact fallback.
+        const int cc = (int)std::min<int64_t>(std::max<int64_t>(16LL * K, 8192), (int64_t)ng * kSlice);
+        const int gather = std::max(8192, K + pen_stride);
+        size_t s2 = std::max(stage2_bytes(K, gather + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
+        s2 += kHeadBytes;
+        if ((int64_t)align16(s1) <= smem_optin && (int64_t)align16(s2) <= smem_optin) {
+            plan->chunk = 0;
+            plan->nchunks = ipr;
+            plan->nspans = ipr;
+            plan->span = 1;
+            plan->elems = 0;
+            plan->stream = true;
+            plan->cand_cap = cc;
+            plan->gather_cap = gather;
+            plan->grid = grid;
+            plan->flat_ng = ng;
+            plan->flat_ngt = ngt;
+            plan->flat_pmax = pmax;
+            plan->items = (long long)grid * pmax;
+            plan->smem = align16(s1);
+            plan->smem2 = align16(s2);
+            return cudaSuccess;
+        }
+    }
     const int nst = esz == 4 ? stage_count<float>() : stage_count<uint16_t>();
     // Enough CTAs for several waves at two resident CTAs per SM; otherwise long spans,
     // so that each CTA filters most elements against an established K-th key.
@@ -3413,6 +3885,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     }
     p.cand = ws.cand;
     p.cand_cap = plan.cand_cap;
+    p.gather_cap = plan.gather_cap;
     p.flat_ng = plan.flat_ng;
     p.flat_grid = plan.grid;
     p.flat_pmax = plan.flat_pmax;
@@ -3496,7 +3969,8 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         void (*k1)(KParams) = nullptr;
         const int R = plan.elems;
 #define VDXS_HIST(R_) k1 = vec ? topk_hist_kernel<T, true, R_> : topk_hist_kernel<T, false, R_>
-        if (R == 1) VDXS_HIST(1);
+        if (R == 0) k1 = vec ? topk_wide_kernel<T, true> : topk_wide_kernel<T, false>;
+        else if (R == 1) VDXS_HIST(1);
         else if (R == 2) VDXS_HIST(2);
         else VDXS_HIST(4);
 #undef VDXS_HIST
