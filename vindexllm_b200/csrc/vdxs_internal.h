@@ -92,11 +92,11 @@ struct SampleArgs {
 };
 
 struct LaunchPlan {
-    int chunk = 0;    // elements per chunk (one register tile of the CTA)
+    int chunk = 0;    // full path: elements per CTA; cluster path: elements per CTA of a row
     int nchunks = 0;  // chunks per row (full-softmax path: CTAs per row)
-    int span = 1;     // chunks walked by one CTA of the top-k path
-    int nspans = 0;   // CTAs per row of the top-k path
-    int elems = 32;   // keys per thread per chunk
+    int span = 1;     // cluster path: bytes of the staged row chunk
+    int nspans = 0;   // stream paths: stage-1 pieces per row
+    int elems = 32;   // stream path: warp list registers R (0 = wide stream path)
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
     bool cluster = false; // top-k path, small batches: one thread-block cluster per row
     int grid = 0;         // stream kernel grid (CTAs)

@@ -4,14 +4,20 @@
 // [B, V] device-resident logits.
 //
 //   penalty_prep_kernel   Sampler.pas:285-303  history ids -> sorted unique (id, f^n(x))
-//   topk_span_kernel      Sampler.pas:305-459  one CTA per (row, span of chunks): stream
-//                         each chunk once from HBM with 128-bit loads into registers as
-//                         order-preserving keys, keep a running top-K of the span; the last
-//                         CTA of a row merges the span candidates plus the penalised
-//                         history entries, then applies exp / min-p / sort / top-p / draw.
-//                         Rows whose token depends on the reference's min-buffer slot
-//                         order are re-resolved in the same CTA by an exact emulation of
-//                         the scan (faithful mode).
+//   topk_hist_kernel      Sampler.pas:305-383  top_k <= 128: persistent CTAs stream flat
+//                         pieces of rows through per-warp TMA rings, filter against a
+//                         threshold taken from a key histogram (raised as candidates are
+//                         counted and shared per row), and write each piece's candidates.
+//   topk_wide_kernel      the same stage 1 for 128 < top_k <= 1024, appending raw lists.
+//   finish_kernel         Sampler.pas:305-459  one CTA per row (programmatic dependent
+//                         launch): gathers the candidates at the row's bound plus the
+//                         penalised history entries, selects the exact top-K, then exp /
+//                         min-p / sort / top-p / draw. Rows whose token depends on the
+//                         reference's min-buffer slot order are re-resolved in the same
+//                         CTA by an exact emulation of the scan (faithful mode).
+//   row_cluster_kernel    batches of at most 8 rows: one 8-CTA cluster per row, the row
+//                         staged in shared memory, candidates sent to the leader CTA
+//                         through distributed shared memory; the leader finishes.
 //   full_max_kernel,      Sampler.pas:461-527  full-softmax path: max pass, then an
 //   full_sum_kernel       exp/sum pass whose last CTA per row locates the draw.
 //   merge_draw_kernel     vocab-sharded path: merge the all-gathered candidates, draw.
@@ -72,8 +78,8 @@ struct KParams {
     int V;
     int B;
     int chunk;    // elements per chunk (top-k path: NT * keys per thread)
-    int nchunks;  // CTAs per row (top-k path: spans; full path: chunks)
-    int span;     // chunks per span (top-k path)
+    int nchunks;  // full path: CTAs (chunks) per row; stream paths: pieces per row
+    int span;     // cluster path: bytes of the staged row chunk
     int K;
     int path;
     // penalty list (sorted unique local ids and their penalised values); null when off
@@ -353,10 +359,84 @@ __device__ void bitonic_sort_desc(uint64_t* a, int n) {
     }
 }
 
+__device__ __forceinline__ uint64_t shfl64_xor(uint64_t v, int m) {
+    const uint32_t lo = __shfl_xor_sync(FULL, (uint32_t)v, m), hi = __shfl_xor_sync(FULL, (uint32_t)(v >> 32), m);
+    return ((uint64_t)hi << 32) | lo;
+}
+
+// Bitonic sort (descending) of a[0, EPT*NT) with EPT consecutive elements per thread in
+// registers: exchanges between elements of one thread stay in registers, partners in
+// the same warp are reached by shuffles, and only the widest stages (partner distance
+// of a warp's span or more) go through shared memory.
+template <int EPT>
+__device__ void block_bitonic_desc_regs(uint64_t* a) {
+    constexpr int N = EPT * NT;
+    const int tid = threadIdx.x;
+    uint64_t v[EPT];
+#pragma unroll
+    for (int u = 0; u < EPT; ++u) v[u] = a[EPT * tid + u];
+    for (int k = 2; k <= N; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j >= 32 * EPT) {
+                __syncthreads();
+#pragma unroll
+                for (int u = 0; u < EPT; ++u) a[EPT * tid + u] = v[u];
+                __syncthreads();
+#pragma unroll
+                for (int u = 0; u < EPT; ++u) {
+                    const int i = EPT * tid + u;
+                    const uint64_t y = a[i ^ j];
+                    const bool hi = ((i & k) == 0) == (i < (i ^ j));  // keep the larger
+                    v[u] = hi ? max(v[u], y) : min(v[u], y);
+                }
+            } else if (j >= EPT) {
+#pragma unroll
+                for (int u = 0; u < EPT; ++u) {
+                    const int i = EPT * tid + u;
+                    const uint64_t y = shfl64_xor(v[u], j / EPT);
+                    const bool hi = ((i & k) == 0) == (i < (i ^ j));
+                    v[u] = hi ? max(v[u], y) : min(v[u], y);
+                }
+            } else {
+                // Partner in this thread; jj is a compile-time copy of j, so v stays in
+                // registers.
+#pragma unroll
+                for (int jj = 1; jj < EPT; jj <<= 1) {
+                    if (jj == j) {
+#pragma unroll
+                        for (int u = 0; u < EPT; ++u) {
+                            if ((u & jj) == 0) {
+                                const int i = EPT * tid + u;
+                                const uint64_t x = v[u], y = v[u ^ jj];
+                                const bool desc = (i & k) == 0;
+                                v[u] = desc ? max(x, y) : min(x, y);
+                                v[u ^ jj] = desc ? min(x, y) : max(x, y);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < EPT; ++u) a[EPT * tid + u] = v[u];
+    __syncthreads();
+}
+
 // Descending sort of a[0, n) (n <= P2, a power of two) where a[0, nvalid) are distinct
 // non-zero keys and a[nvalid, P2) are zero. Up to NT keys: each thread's rank among the
-// valid keys is its position (two barriers); above that, the bitonic network.
+// valid keys is its position (two barriers); 512 and 1024 keys: the register bitonic
+// network; above that, the shared-memory one.
 __device__ void block_sort_desc_distinct(uint64_t* a, int nvalid, int P2) {
+    if (P2 == 2 * NT) {
+        block_bitonic_desc_regs<2>(a);
+        return;
+    }
+    if (P2 == 4 * NT) {
+        block_bitonic_desc_regs<4>(a);
+        return;
+    }
     if (P2 > NT) {
         bitonic_sort_desc(a, P2);
         return;
@@ -645,6 +725,7 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
     int32_t* qid = (int32_t*)(q + P2);
     double* pre = (double*)(qid + P2);  // [P2 + 1]
 
+    VDXS_T0(t_e);
     const float M = key2f(kmax);
     const double Md = (double)M, it = (double)p.inv_temp;
     for (int s = tid; s < P2; s += NT) q[s] = s < nsel ? (float)exp(((double)key2f(sk[s]) - Md) * it) : 0.0f;
@@ -665,7 +746,11 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
     for (int s = tid; s < P2; s += NT)
         sortb[s] = s < nsel ? (((uint64_t)__float_as_uint(q[s]) << 32) | (uint64_t)(~si[s])) : 0ull;
     __syncthreads();
+    VDXS_T1(1, t_e);
+    VDXS_T0(t_so);
     block_sort_desc_distinct(sortb, nsel, P2);  // indices are distinct, ~index is non-zero
+    VDXS_T1(2, t_so);
+    VDXS_T0(t_wk);
     uint32_t cnt = 0u, emin = 0xFFFFFFFFu;
     for (int s = tid; s < P2; s += NT) {
         float v = s < nsel ? __uint_as_float((uint32_t)(sortb[s] >> 32)) : 0.0f;
@@ -762,6 +847,7 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
         s_d[2] = before;
     }
     __syncthreads();
+    VDXS_T1(3, t_wk);
     int j = s_i[0];
     const bool fallback = j < 0 || j >= nsel;
     if (fallback) j = nsel - 1;
@@ -852,6 +938,10 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
         __threadfence_block();
         return true;
     };
+    // Slots per lane. Up to four, the owning lane rescans its own slots after an
+    // insertion; beyond that the whole warp rescans them (lane u reads slot owner + 32*u)
+    // and two warp reductions give the owner's (minimum key, lowest slot).
+    const int RL = (K + 31) / 32;
     // Minimum of the slots this lane owns; the first slot wins ties (strict '<'). Eight
     // slots are loaded at a time so that their latencies overlap.
     auto lane_min = [&](int& bs) -> uint32_t {
@@ -945,7 +1035,18 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
                         if (lane == 0) atomicAdd(&g_phase_count[24], 1ull);
                         const long long tq0 = clock64();
 #endif
-                        if (lane == (ms & 31)) kv = lane_min(bs);
+                        if (RL <= 4) {
+                            if (lane == (ms & 31)) kv = lane_min(bs);
+                        } else {
+                            const int owner = ms & 31, s2 = owner + 32 * lane;
+                            const uint32_t ok = lane < RL && s2 < K ? f2key(sval[s2]) : 0xFFFFFFFFu;
+                            const uint32_t omk = __reduce_min_sync(FULL, ok);
+                            const uint32_t obs = __reduce_min_sync(FULL, ok == omk ? (uint32_t)s2 : 0xFFFFFFFFu);
+                            if (lane == owner) {
+                                kv = omk;
+                                bs = (int)obs;
+                            }
+                        }
 #ifdef VDXS_TIMING
                         __syncwarp();
                         const long long tq1 = clock64();
@@ -1157,67 +1258,9 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
     __syncthreads();
 }
 
-// ---------------------------------------------------------------------------------
-// Stage 1 (top-k and greedy paths): one CTA walks a span of consecutive chunks of a
-// row. Each chunk (NT*E elements) is streamed once from HBM with 128-bit loads into
-// registers as order-preserving keys. The CTA keeps a running top-K of its span in
-// shared memory; after the first chunk every element costs one register compare
-// against the running K-th key (later elements lose ties, so the compare is strict).
-// The first chunk's threshold is a lower bound on its K-th key taken from a log-bin
-// histogram of each thread's top-M keys, so only about K candidates reach the exact
-// select. Candidate overflow falls back to an exact select over the whole chunk.
-// ---------------------------------------------------------------------------------
+// Element loads as float (bf16 widened exactly).
 __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
-
-// Keys of one chunk from its shared-memory stage (first n_tma elements) and, for a
-// ragged tail, from global memory. Element (j, e) of thread t is chunk position
-// (t + j*NT)*VN + e. Excluded (history) and out-of-range elements get key 0.
-template <typename T, int E>
-__device__ __forceinline__ void load_stage_keys(const T* stage, int n_tma, const T* row, int64_t start, int n,
-                                                const uint32_t* bitmap, bool excl, uint32_t (&keys)[E]) {
-    constexpr int VN = 16 / sizeof(T);
-    constexpr int NV = E / VN;
-    static_assert(E % VN == 0, "keys per thread must be a multiple of the vector width");
-    const int tid = threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-        const int pos = (tid + j * NT) * VN;
-        float x[VN];
-        if (pos + VN <= n_tma) {
-            unpack(*reinterpret_cast<const uint4*>(stage + pos), x, T());
-        } else {
-#pragma unroll
-            for (int e = 0; e < VN; ++e) {
-                const int i = pos + e;
-                x[e] = i < n ? (i < n_tma ? to_f(stage[i]) : ld_elem(row, start + i)) : 0.0f;
-            }
-        }
-        const uint32_t ex = excl ? (bitmap[pos >> 5] >> (pos & 31)) : 0u;
-#pragma unroll
-        for (int e = 0; e < VN; ++e) keys[j * VN + e] = (pos + e < n && !((ex >> e) & 1u)) ? f2key(x[e]) : 0u;
-    }
-}
-
-// Keys of one chunk straight from global memory (rows that are not 16-byte aligned).
-template <typename T, int E>
-__device__ __forceinline__ void load_global_keys(const T* row, int64_t start, int n, const uint32_t* bitmap,
-                                                 bool excl, uint32_t (&keys)[E]) {
-    const int tid = threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < E; ++j) {
-        const int pos = tid + j * NT;
-        const bool ex = excl && ((bitmap[pos >> 5] >> (pos & 31)) & 1u);
-        keys[j] = (pos < n && !ex) ? f2key(ld_elem(row, start + pos)) : 0u;
-    }
-}
-
-// Chunk position of register key e of this thread.
-template <typename T, int E, bool VEC>
-__device__ __forceinline__ int key_pos(int e) {
-    constexpr int VN = VEC ? (int)(16 / sizeof(T)) : 1;
-    return (threadIdx.x + (e / VN) * NT) * VN + (e % VN);
-}
 
 // Writes every selected element of src to (ok, oi), returns the count (uniform).
 template <class Src, class IdxF>
@@ -1265,8 +1308,6 @@ struct OffsetIdx {
     __device__ __forceinline__ uint32_t operator()(int i) const { return base + (uint32_t)i; }
 };
 
-// Stage 2 for one row, run by the last CTA of the row: merge the span candidates and
-// the penalised history entries, then greedy / draw (or publish for the all-gather).
 // Stage 2 of one row from gathered candidates (ckey, cidx)[0, n2) in shared memory:
 // exact top-K (block_select), boundary-tie evidence (selection cuts, and cut_of(i) for
 // the ncut stage-1 items), then greedy / draw / publication for the all-gather, and
@@ -1279,10 +1320,12 @@ __device__ void finish_select(const KParams& p, int b, uint32_t* ckey, uint32_t*
     uint32_t* sk = (uint32_t*)region;
     uint32_t* si = sk + K;
     const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
+    VDXS_T0(t_sel);
     const SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
     const int nsel = block_emit(SmemPairSrc{ckey, cidx}, n2, s2, sk, si, K, &sh[8], IdentIdx{cidx});
+    VDXS_T1(4, t_sel);
     // The boundary value is the smallest selected key. A boundary tie exists when the
-    // merge cut elements of that value, or a span cut elements of that value.
+    // merge cut elements of that value, or a stage-1 item cut elements of that value.
     uint32_t kb = 0xFFFFFFFFu;
     for (int s = tid; s < nsel; s += NT) kb = min(kb, sk[s]);
     kb = block_min_u32(kb, sh + 32);
@@ -1389,16 +1432,12 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     uint32_t* sk = (uint32_t*)region;
     uint32_t* si = sk + K;
     uint32_t* ckey = si + K;
-    // Stage-1 items of this row: spans b * nchunks + i, or in the flat partition the
-    // pieces of the CTAs that own the row's granules.
-    int nsp = p.nchunks, c_lo = 0;
-    if (p.flat_ng > 0) {
-        const long long g0 = (long long)b * p.flat_ng;
-        c_lo = flat_owner(p.flat_ngt, p.flat_grid, g0);
-        nsp = flat_owner(p.flat_ngt, p.flat_grid, g0 + p.flat_ng - 1) - c_lo + 1;
-    }
+    // Stage-1 items of this row: the pieces of the CTAs that own the row's granules in
+    // the flat partition.
+    const long long g0 = (long long)b * p.flat_ng;
+    const int c_lo = flat_owner(p.flat_ngt, p.flat_grid, g0);
+    const int nsp = flat_owner(p.flat_ngt, p.flat_grid, g0 + p.flat_ng - 1) - c_lo + 1;
     auto item_of = [&](int i) -> int64_t {
-        if (p.flat_ng <= 0) return (int64_t)b * p.nchunks + i;
         const int c = c_lo + i;
         const int jj = b - (int)(flat_start(p.flat_ngt, p.flat_grid, c) / p.flat_ng);
         return (int64_t)c * p.flat_pmax + jj;
@@ -1492,9 +1531,6 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     finish_select<T>(p, b, ckey, cidx, n2, gmax, nsp,
                      [&](int i) -> uint32_t { return __ldcg(&p.chunk_info[item_of(i)].y); }, region, hist, sh);
 }
-
-template <typename T>
-__host__ __device__ constexpr int stage_count() { return sizeof(T) == 4 ? 4 : 6; }
 
 // ---------------------------------------------------------------------------------
 // Warp-level select (one warp, warp-private histogram; __syncwarp only). Same result
@@ -1939,8 +1975,8 @@ __device__ __forceinline__ float max16(const float (&x)[16]) {
 }
 
 // Stream stage 1 for top_k <= 128. Persistent CTAs (two per SM), 8 warps each. Work
-// item = (row, span); warp w streams the contiguous sub-range [w*SW, (w+1)*SW) of the
-// span through its own ring of TMA bulk copies (plain loads when the rows are not
+// item = (row, piece); warp w streams the contiguous sub-range [w*SW, (w+1)*SW) of the
+// piece through its own ring of TMA bulk copies (plain loads when the rows are not
 // 16-byte aligned). Elements at or above the CTA threshold are appended to a shared
 // candidate buffer and counted in the threshold histogram; the threshold is then
 // raised to the histogram's K-th edge and published per row, so every CTA of the row
@@ -2636,7 +2672,11 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
                 }
                 counted = true;
             }
-            const float thr = key_threshold(max((uint32_t)*s_T, rtau));
+            const uint32_t tkey = max((uint32_t)*s_T, rtau);
+            const float thr = key_threshold(tkey);
+            // A candidate in the threshold's own bin cannot raise the threshold (that
+            // needs K counts at a higher edge), so only candidates above it are counted.
+            const uint32_t tbin = tkey >> 20;
             const float lmax = max16(x);
             const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
             if constexpr (TMA) {
@@ -2664,7 +2704,7 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
                     const uint32_t k = f2key(lmax);
                     const uint32_t slot = base + __popc(lanes & lanemask_lt());
                     if (slot < cap) out[slot] = make_uint2(k, gb + (uint32_t)pos);
-                    if (!counted) {
+                    if (!counted && (k >> 20) > tbin) {
                         atomicAdd(&H[k >> 20], 1u);
                         atomicAdd(&G[k >> 26], 1u);
                     }
@@ -2688,7 +2728,7 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
                         const uint32_t k = f2key(x[e]);
                         if (slot < cap) out[slot] = make_uint2(k, gb + (uint32_t)pos);
                         ++slot;
-                        if (!counted) {
+                        if (!counted && (k >> 20) > tbin) {
                             atomicAdd(&H[k >> 20], 1u);
                             atomicAdd(&G[k >> 26], 1u);
                         }
@@ -2989,238 +3029,6 @@ __global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
     VDXS_T0(t_fin);
     finish_row<T>(p, blockIdx.x, region, hist, sh);
     if (threadIdx.x == 0 && p.row_tau) p.row_tau[(size_t)blockIdx.x * kTauStride] = 0u;  // ready for the next launch
-    VDXS_T1(5, t_fin);
-}
-
-template <typename T, int E, int M, bool TMA>
-__global__ void __launch_bounds__(NT) topk_span_kernel(KParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint32_t* hist = (uint32_t*)smem_raw;
-    uint32_t* sh = hist + kHistWords;
-    unsigned char* region = smem_raw + kHeadBytes;
-    const int tid = threadIdx.x;
-    const int sp = blockIdx.x, b = blockIdx.y;
-    const int K = p.K;
-    constexpr int CH = NT * E;
-    constexpr int CAP = CH / 2;
-    constexpr int NST = stage_count<T>();
-    T* stages = (T*)region;                                                  // [NST][CH]
-    uint64_t* bars = (uint64_t*)(region + (size_t)NST * CH * sizeof(T));    // [NST]
-    uint32_t* lk = (uint32_t*)(bars + NST);  // running top-K of the span
-    uint32_t* li = lk + K;
-    uint32_t* bk = li + K;                   // select output
-    uint32_t* bi = bk + K;
-    uint32_t* ak = bi + K;                   // [K + CAP] list + candidates, aliased by fk[CH]
-    uint32_t* ai = ak + K + CAP;
-    uint32_t* fk = ak;
-    uint32_t* bitmap = ai + K + CAP;         // [CH / 32]
-    int* scan_sh = (int*)(sh + 48);
-
-    const T* row = (const T*)p.logits + (int64_t)b * p.stride;
-    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
-    const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-    const int c0 = sp * p.span, c1 = min(c0 + p.span, (p.V + CH - 1) / CH);
-    const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
-    int L = 0;              // entries in the running list
-    uint32_t tau = 0u;      // its smallest key once L == K
-    uint32_t lmaxk = 0u;    // its largest key
-    uint32_t max_cut = 0u;  // largest key at which elements equal to it were dropped
-    VDXS_T0(t_all);
-
-    // One elected thread streams chunk c into stage (c - c0) % NST.
-    auto issue = [&](int c) {
-        const int stg = (c - c0) % NST;
-        const int64_t st0 = (int64_t)c * CH;
-        const int nn = (int)min((int64_t)CH, (int64_t)p.V - st0);
-        const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
-        if (bytes) {
-            mbar_arrive_expect_tx(&bars[stg], bytes);
-            tma_load_1d(stages + (size_t)stg * CH, row + st0, bytes, &bars[stg]);
-        } else {
-            mbar_arrive(&bars[stg]);
-        }
-    };
-    if constexpr (TMA) {
-        if (tid == 0) {
-            for (int s = 0; s < NST; ++s) mbar_init(&bars[s], 1);
-            fence_mbar_init();
-        }
-        __syncthreads();
-        if (tid == 0)
-            for (int c = c0; c < c1 && c < c0 + NST; ++c) issue(c);
-    }
-
-    for (int c = c0; c < c1; ++c) {
-        const int64_t start = (int64_t)c * CH;
-        const int n = (int)min((int64_t)CH, (int64_t)p.V - start);
-        VDXS_T0(t_w);
-        if (npen > 0) {
-            for (int i = tid; i < CH / 32; i += NT) bitmap[i] = 0u;
-            __syncthreads();
-            const int j0 = lower_bound_i32(pid, npen, start);
-            for (int j = j0 + tid; j < npen && pid[j] < start + n; j += NT) {
-                const int e = pid[j] - (int)start;
-                atomicOr(&bitmap[e >> 5], 1u << (e & 31));
-            }
-            __syncthreads();
-        }
-        uint32_t keys[E];
-        if constexpr (TMA) {
-            const int it = c - c0, stg = it % NST;
-            if (!mbar_wait_bounded(&bars[stg], (uint32_t)((it / NST) & 1))) atomicExch(p.err, kErrTimeout);
-            const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
-            load_stage_keys<T, E>(stages + (size_t)stg * CH, n_tma, row, start, n, bitmap, npen > 0, keys);
-            __syncthreads();  // every thread has its keys: the stage can be refilled
-            if (tid == 0 && c + NST < c1) issue(c + NST);
-        } else {
-            load_global_keys<T, E>(row, start, n, bitmap, npen > 0, keys);
-        }
-        VDXS_T1(1, t_w);
-        VDXS_T0(t_e);
-
-        uint32_t thr = 1u;
-        const bool strict = L == K;
-        if (strict) {
-            thr = tau;
-        } else {
-            // Lower bound on this chunk's K-th key from each thread's top-M keys.
-            uint32_t top[M];
-#pragma unroll
-            for (int m = 0; m < M; ++m) top[m] = 0u;
-#pragma unroll
-            for (int e = 0; e < E; ++e) {
-                uint32_t k = keys[e];
-#pragma unroll
-                for (int m = 0; m < M; ++m) {
-                    const uint32_t hi = max(top[m], k);
-                    k = min(top[m], k);
-                    top[m] = hi;
-                }
-            }
-            const uint32_t kmx = block_max_u32(top[0], sh + 32);
-            if (kmx == 0u) continue;  // nothing valid in this chunk (uniform)
-            for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
-            __syncthreads();
-#pragma unroll
-            for (int m = 0; m < M; ++m)
-                if (top[m]) atomicAdd(&hist[logbin(kmx - top[m])], 1u);
-            __syncthreads();
-            if (tid < 32) warp_find(hist, kHistBins, (uint32_t)K, sh);
-            __syncthreads();
-            if (sh[0] != 0xFFFFFFFFu) {
-                uint32_t lo;
-                int bits;
-                logbin_range((int)sh[0], &lo, &bits);
-                const uint32_t dmax = min(lo + ((1u << bits) - 1u), kmx - 1u);
-                thr = kmx - dmax;
-            }
-            __syncthreads();
-        }
-        VDXS_T1(2, t_e);
-        VDXS_T0(t_f);
-        int cnt = 0;
-        bool eqd = false;
-        uint32_t cmax = 0u;
-#pragma unroll
-        for (int e = 0; e < E; ++e) {
-            const uint32_t k = keys[e];
-            const bool pass = k != 0u && (strict ? k > thr : k >= thr);
-            cnt += pass ? 1 : 0;
-            cmax = pass ? max(cmax, k) : cmax;
-            eqd |= strict && k == thr;
-        }
-        if (strict && __syncthreads_or(eqd)) max_cut = max(max_cut, thr);
-        int total;
-        int off = block_excl_scan(cnt, scan_sh, &total);
-        VDXS_T1(3, t_f);
-        if (total == 0) continue;
-        VDXS_T0(t_m);
-        const uint32_t gbase = (uint32_t)(p.vocab_offset + start);
-        int m_new;
-        if (L + total <= K + CAP) {
-            for (int s = tid; s < L; s += NT) {
-                ak[s] = lk[s];
-                ai[s] = li[s];
-            }
-#pragma unroll
-            for (int e = 0; e < E; ++e) {
-                const uint32_t k = keys[e];
-                if (k != 0u && (strict ? k > thr : k >= thr)) {
-                    ak[L + off] = k;
-                    ai[L + off] = gbase + (uint32_t)key_pos<T, E, TMA>(e);
-                    ++off;
-                }
-            }
-            const uint32_t kall = max(block_max_u32(cmax, sh + 32), lmaxk);
-            const SelectOut so = block_select(SmemPairSrc{ak, ai}, L + total, K, kall, tbb, hist, sh);
-            if (so.tie_cut) max_cut = max(max_cut, so.kth_key);
-            m_new = block_emit(SmemPairSrc{ak, ai}, L + total, so, bk, bi, K, &sh[8], IdentIdx{ai});
-        } else {
-            // Candidate overflow: exact select over the whole chunk, then merge.
-            uint32_t km = 0u;
-#pragma unroll
-            for (int e = 0; e < E; ++e) {
-                fk[key_pos<T, E, TMA>(e)] = keys[e];
-                km = max(km, keys[e]);
-            }
-            km = block_max_u32(km, sh + 32);
-            const SelectOut sc = block_select(SmemKeySrc{fk}, CH, K, km, bits_for((uint32_t)(CH - 1)), hist, sh);
-            if (sc.tie_cut) max_cut = max(max_cut, sc.kth_key);
-            const int mc = block_emit(SmemKeySrc{fk}, CH, sc, bk, bi, K, &sh[8], OffsetIdx{gbase});
-            for (int s = tid; s < L; s += NT) {
-                ak[s] = lk[s];
-                ai[s] = li[s];
-            }
-            for (int s = tid; s < mc; s += NT) {
-                ak[L + s] = bk[s];
-                ai[L + s] = bi[s];
-            }
-            __syncthreads();
-            const uint32_t kall = max(km, lmaxk);
-            const SelectOut so = block_select(SmemPairSrc{ak, ai}, L + mc, K, kall, tbb, hist, sh);
-            if (so.tie_cut) max_cut = max(max_cut, so.kth_key);
-            m_new = block_emit(SmemPairSrc{ak, ai}, L + mc, so, bk, bi, K, &sh[8], IdentIdx{ai});
-        }
-        uint32_t mn = 0xFFFFFFFFu, mx = 0u;
-        for (int s = tid; s < m_new; s += NT) {
-            lk[s] = bk[s];
-            li[s] = bi[s];
-            mn = min(mn, bk[s]);
-            mx = max(mx, bk[s]);
-        }
-        L = m_new;
-        mn = block_min_u32(mn, sh + 32);
-        lmaxk = block_max_u32(mx, sh + 32);
-        tau = L == K ? mn : 0u;
-        VDXS_T1(4, t_m);
-    }
-    if constexpr (TMA) {
-        __syncthreads();
-        if (tid == 0)
-            for (int s = 0; s < NST; ++s) mbar_inval(&bars[s]);
-    }
-
-    // Publish the span's list (padded) and its boundary-tie evidence.
-    uint2* out = p.cand + ((int64_t)b * p.nchunks + sp) * p.cand_cap;
-    for (int s = tid; s < L; s += NT) out[s] = make_uint2(lk[s], li[s]);
-    if (tid == 0) {
-        p.chunk_info[(int64_t)b * p.nchunks + sp] = make_uint2((uint32_t)L, max_cut);
-        p.item_tau[(int64_t)b * p.nchunks + sp] = L == K ? tau : 0u;  // a full span's K-th key
-    }
-
-    VDXS_T1(0, t_all);
-    // Completion: the last CTA of the row runs stage 2.
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) {
-        const uint32_t prev = atomicAdd(&p.row_counter[b], 1u);
-        sh[9] = prev == (uint32_t)(p.nchunks - 1) ? 1u : 0u;
-    }
-    __syncthreads();
-    if (sh[9] == 0u) return;
-    __threadfence();
-    VDXS_T0(t_fin);
-    finish_row<T>(p, b, region, hist, sh);
     VDXS_T1(5, t_fin);
 }
 
@@ -3651,37 +3459,6 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
             return cudaSuccess;
         }
     }
-    const int nst = esz == 4 ? stage_count<float>() : stage_count<uint16_t>();
-    // Enough CTAs for several waves at two resident CTAs per SM; otherwise long spans,
-    // so that each CTA filters most elements against an established K-th key.
-    const int64_t target = 148 * 8;
-    const int E = 16;
-    const int CH = NT * E;
-    const int nch = (int)((V + CH - 1) / CH);
-    int span = 1;
-    while (span < nch && (int64_t)a.B * ((nch + 2 * span - 1) / (2 * span)) >= target) span <<= 1;
-    for (;;) {
-        const int nspans = (nch + span - 1) / span;
-        const size_t s1 = (size_t)nst * CH * esz + 8 * (size_t)nst + (size_t)16 * K + (size_t)8 * (K + CH / 2) +
-                          (size_t)CH / 8;
-        size_t need = std::max(s1, stage2_bytes(K, nspans * K + pen_stride));
-        if (faithful) need = std::max(need, faithful_bytes(K));
-        need += kHeadBytes;
-        if ((int64_t)need <= smem_optin) {
-            plan->chunk = CH;
-            plan->cand_cap = K;
-            plan->items = (long long)a.B * nspans;
-            plan->elems = E;
-            plan->span = span;
-            plan->nspans = nspans;
-            plan->nchunks = nspans;
-            plan->stream = false;
-            plan->smem = align16(need);
-            return cudaSuccess;
-        }
-        if (span >= nch) break;
-        span <<= 1;
-    }
     if (err) *err = "top_k too large for the shared-memory plan (top_k=" + std::to_string(K) + ")";
     return cudaErrorInvalidValue;
 }
@@ -4002,17 +3779,8 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         count(a, 2);
         return cudaSuccess;
     }
-    const int M = a.K <= NT ? 1 : 4;
-    void (*kern)(KParams) = nullptr;
-    if (M == 1) kern = vec ? topk_span_kernel<T, 16, 1, true> : topk_span_kernel<T, 16, 1, false>;
-    else kern = vec ? topk_span_kernel<T, 16, 4, true> : topk_span_kernel<T, 16, 4, false>;
-    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem);
-    if (e != cudaSuccess) return e;
-    if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
-    kern<<<grid, NT, plan.smem, a.stream>>>(p);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    count(a);
-    return mark(a, a.ev_end);
+    if (err) *err = "no top-k plan for this call";
+    return cudaErrorInvalidValue;
 }
 
 cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err) {
