@@ -99,6 +99,7 @@ struct LaunchPlan {
     int elems = 32;   // stream path: warp list registers R (0 = wide stream path)
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
     bool cluster = false; // top-k path, small batches: one thread-block cluster per row
+    int cluster_ctas = 8; // CTAs per cluster
     int grid = 0;         // stream kernel grid (CTAs)
     int cand_cap = 0;     // top-k path: candidates each stage-1 item may write
     int gather_cap = 0;   // wide stream path: finish kernel gather capacity (0 = other paths)

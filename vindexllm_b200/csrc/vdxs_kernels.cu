@@ -1321,8 +1321,37 @@ __device__ void finish_select(const KParams& p, int b, uint32_t* ckey, uint32_t*
     uint32_t* si = sk + K;
     const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
     VDXS_T0(t_sel);
-    const SelectOut s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
-    const int nsel = block_emit(SmemPairSrc{ckey, cidx}, n2, s2, sk, si, K, &sh[8], IdentIdx{cidx});
+    SelectOut s2;
+    int nsel;
+    if (n2 <= NT) {
+        // Few candidates: rank select. (key, ~index) composites are distinct, so the
+        // rank of each valid entry is its position in (key desc, index asc) order; key 0
+        // ranks below every valid entry and is never selected.
+        const int tid2 = threadIdx.x;
+        const uint64_t mine = tid2 < n2 ? ((uint64_t)ckey[tid2] << 32) | (uint32_t)~cidx[tid2] : 0ull;
+        const bool valid = tid2 < n2 && ckey[tid2] != 0u;
+        int rank = 0;
+        if (valid)
+            for (int j = 0; j < n2; ++j) rank += (((uint64_t)ckey[j] << 32) | (uint32_t)~cidx[j]) > mine ? 1 : 0;
+        const uint32_t nv = block_sum_u32(valid ? 1u : 0u, sh + 32);
+        if (valid && rank == K - 1) sh[8] = (uint32_t)(mine >> 32);
+        __syncthreads();
+        const uint32_t kth = nv > (uint32_t)K ? sh[8] : 0u;
+        const bool cut = valid && rank >= K && (uint32_t)(mine >> 32) == kth;
+        s2.tie_cut = __syncthreads_or(cut) ? 1 : 0;
+        s2.kth_key = kth;
+        s2.kth_tb = 0xFFFFFFFFu;
+        s2.n_valid = nv;
+        if (valid && rank < K) {
+            sk[rank] = (uint32_t)(mine >> 32);
+            si[rank] = ~(uint32_t)mine;
+        }
+        nsel = (int)min(nv, (uint32_t)K);
+        __syncthreads();
+    } else {
+        s2 = block_select(SmemPairSrc{ckey, cidx}, n2, K, gmax, tbb, hist, sh);
+        nsel = block_emit(SmemPairSrc{ckey, cidx}, n2, s2, sk, si, K, &sh[8], IdentIdx{cidx});
+    }
     VDXS_T1(4, t_sel);
     // The boundary value is the smallest selected key. A boundary tie exists when the
     // merge cut elements of that value, or a stage-1 item cut elements of that value.
@@ -1863,21 +1892,22 @@ __device__ __forceinline__ int warp_compact_selected(uint32_t* k, uint32_t* t, i
 }
 
 // ---------------------------------------------------------------------------------
-// Stream stage 1 (topk_hist_kernel) serves top_k <= kWarpMaxK. Each warp streams
-// kSlice-element TMA slices of its pieces through its own ring of net_ring_slots()
-// slots and keeps the 32*R best (key, index) composites of its stream sorted in
+// Stream stage 1 (topk_hist_kernel) serves top_k <= kWarpMaxK. Each warp streams its
+// pieces through its own ring of net_ring_slots() slots of kSlot elements (one bulk copy
+// each), filters them kSlice elements at a time, and keeps the 32*R best (key, index) composites of its stream sorted in
 // registers; candidates above the row threshold are batched in shared memory and
 // merged into that list with a bitonic network when a warp's region overflows.
 // ---------------------------------------------------------------------------------
 constexpr int kWarpMaxK = 128;
-constexpr int kSlice = 512;     // elements per ring slot (16 per lane)
+constexpr int kSlice = 512;     // elements filtered per step (16 per lane); flat-partition granule
+constexpr int kSlot = 1024;     // elements per ring slot (one bulk copy; two slices)
 
 template <typename T>
-__host__ __device__ constexpr int net_ring_slots() { return sizeof(T) == 4 ? 4 : 8; }
+__host__ __device__ constexpr int net_ring_slots() { return sizeof(T) == 4 ? 2 : 4; }
 // Per-warp area in 32-bit words, rounded to 128 bytes so that every warp's ring slots
 // stay 16-byte aligned (TMA destinations, 128-bit loads).
 __host__ __device__ constexpr int net_area_words(int R, int slots, int esz) {
-    return ((slots * kSlice * esz) / 4 + 2 * slots + 64 * R + kSlice / 32 + 31) & ~31;
+    return ((slots * kSlot * esz) / 4 + 2 * slots + 64 * R + kSlice / 32 + 31) & ~31;
 }
 
 // Merges a warp's candidate batch (bcount entries of buf) into its sorted list, then
@@ -2003,7 +2033,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     const int WW = net_area_words(R, RS, (int)sizeof(T));
     uint32_t* wa = (uint32_t*)region + (size_t)warp * WW;
     T* ring = (T*)wa;
-    uint64_t* full = (uint64_t*)(wa + (RS * kSlice * (int)sizeof(T)) / 4);
+    uint64_t* full = (uint64_t*)(wa + (RS * kSlot * (int)sizeof(T)) / 4);
     uint64_t* buf = full + RS;
     uint32_t* wbm = (uint32_t*)(buf + NB);
     uint32_t* H = (uint32_t*)region + (size_t)NWARPS * WW;
@@ -2049,7 +2079,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             warp_range(pj_prod, lo, hi);
             if (hi > lo) {
                 pleft = hi - lo;
-                pns = (int)((pleft + kSlice - 1) / kSlice);
+                pns = (int)((pleft + kSlot - 1) / kSlot);
                 psrc = (const T*)p.logits + (int64_t)(b_first + pj_prod) * p.stride + lo;
                 pq = 0;
                 return;
@@ -2059,12 +2089,12 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     auto issue = [&]() {
         if (pq >= pns) next_piece();
         if (pj_prod >= npieces) return;
-        const int nn = (int)min((int64_t)kSlice, pleft - (int64_t)pq * kSlice);
+        const int nn = (int)min((int64_t)kSlot, pleft - (int64_t)pq * kSlot);
         const int slot = (int)(pn % RS);
         const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
         if (bytes) {
             mbar_arrive_expect_tx(&full[slot], bytes);
-            tma_load_1d(ring + (size_t)slot * kSlice, psrc + (int64_t)pq * kSlice, bytes, &full[slot]);
+            tma_load_1d(ring + (size_t)slot * kSlot, psrc + (int64_t)pq * kSlot, bytes, &full[slot]);
         } else {
             mbar_arrive(&full[slot]);
         }
@@ -2081,9 +2111,12 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
     }
 
     // Slice loads: 16 values per lane; NaN marks positions past the end.
-    auto load_ring = [&](float (&x)[16], int slot, int n, const T* row, int64_t start) {
+    // Half `half` of ring slot `slot` (n valid elements from row position start); the
+    // bulk copy covered the slot's bytes rounded down to 16, which within a half is the
+    // half's own count rounded the same way (a slice is a multiple of 16 bytes).
+    auto load_ring = [&](float (&x)[16], int slot, int half, int n, const T* row, int64_t start) {
         const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
-        const T* sl = ring + (size_t)slot * kSlice;
+        const T* sl = ring + (size_t)slot * kSlot + (size_t)half * kSlice;
 #pragma unroll
         for (int j = 0; j < 16 / VN; ++j) {
             const int pos = (j * 32 + lane) * VN;
@@ -2160,15 +2193,15 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         // NWARPS * RS slices of the piece. Counted elements are not counted again.
         int ncounted = 0;
         if constexpr (TMA) {
-            ncounted = min(RS, ns);
+            ncounted = min(2 * RS, ns);
             int pjc = pj;
             for (int q = 0; q < ncounted; ++q) {
                 const int64_t start = a0 + (int64_t)q * kSlice;
                 const int n = (int)min((int64_t)kSlice, a1 - start);
-                const uint32_t c = cn + (uint32_t)q;
-                if (!mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
+                const uint32_t c = cn + (uint32_t)(q >> 1);
+                if ((q & 1) == 0 && !mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
                 float x[16];
-                load_ring(x, (int)(c % RS), n, row, start);
+                load_ring(x, (int)(c % RS), q & 1, n, row, start);
                 if (npen > 0) mask_penalised(x, pid, npen, pjc, start, n);
                 count_slice(x);
             }
@@ -2191,10 +2224,10 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             rtau_next = ld_relaxed_u32(rtp);
             float x[16];
             if constexpr (TMA) {
-                const int slot = (int)(cn % RS);
-                if (!mbar_wait_bounded(&full[slot], (cn / RS) & 1u)) timed_out = true;
-                load_ring(x, slot, n, row, start);
-                ++cn;
+                const uint32_t c = cn + (uint32_t)(q >> 1);
+                const int slot = (int)(c % RS);
+                if ((q & 1) == 0 && !mbar_wait_bounded(&full[slot], (c / RS) & 1u)) timed_out = true;
+                load_ring(x, slot, q & 1, n, row, start);
             } else {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
@@ -2221,8 +2254,8 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             const float lmax = max16(x);
             const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
             if constexpr (TMA) {
-                // The slot's values are in registers now: refill it.
-                if (lane == 0) {
+                // After a slot's last half the slot's values are in registers: refill it.
+                if (lane == 0 && ((q & 1) == 1 || q == ns - 1)) {
                     fence_proxy_async_smem();
                     issue();
                 }
@@ -2344,6 +2377,7 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
             // Entries past the K-th are cut when the list is published.
             if (K < NB) max_cut = max(max_cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
         }
+        if constexpr (TMA) cn += (uint32_t)((ns + 1) >> 1);  // slots this piece used
         VDXS_T1(10, t_item);
         if (lane == 0) {
             s_cut[warp] = ovf ? max_cut : 0u;
@@ -2470,7 +2504,7 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
     const int WW = net_area_words(0, RS, (int)sizeof(T));
     uint32_t* wa = (uint32_t*)region + (size_t)warp * WW;
     T* ring = (T*)wa;
-    uint64_t* full = (uint64_t*)(wa + (RS * kSlice * (int)sizeof(T)) / 4);
+    uint64_t* full = (uint64_t*)(wa + (RS * kSlot * (int)sizeof(T)) / 4);
     uint32_t* wbm = (uint32_t*)(full + RS);
     uint32_t* H = (uint32_t*)region + (size_t)NWARPS * WW;
     uint32_t* G = H + kTBins;
@@ -2510,7 +2544,7 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
             warp_range(pj_prod, lo, hi);
             if (hi > lo) {
                 pleft = hi - lo;
-                pns = (int)((pleft + kSlice - 1) / kSlice);
+                pns = (int)((pleft + kSlot - 1) / kSlot);
                 psrc = (const T*)p.logits + (int64_t)(b_first + pj_prod) * p.stride + lo;
                 pq = 0;
                 return;
@@ -2520,12 +2554,12 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
     auto issue = [&]() {
         if (pq >= pns) next_piece();
         if (pj_prod >= npieces) return;
-        const int nn = (int)min((int64_t)kSlice, pleft - (int64_t)pq * kSlice);
+        const int nn = (int)min((int64_t)kSlot, pleft - (int64_t)pq * kSlot);
         const int slot = (int)(pn % RS);
         const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
         if (bytes) {
             mbar_arrive_expect_tx(&full[slot], bytes);
-            tma_load_1d(ring + (size_t)slot * kSlice, psrc + (int64_t)pq * kSlice, bytes, &full[slot]);
+            tma_load_1d(ring + (size_t)slot * kSlot, psrc + (int64_t)pq * kSlot, bytes, &full[slot]);
         } else {
             mbar_arrive(&full[slot]);
         }
@@ -2540,9 +2574,12 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
         }
         __syncwarp();
     }
-    auto load_ring = [&](float (&x)[16], int slot, int n, const T* row, int64_t start) {
+    // Half `half` of ring slot `slot` (n valid elements from row position start); the
+    // bulk copy covered the slot's bytes rounded down to 16, which within a half is the
+    // half's own count rounded the same way (a slice is a multiple of 16 bytes).
+    auto load_ring = [&](float (&x)[16], int slot, int half, int n, const T* row, int64_t start) {
         const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
-        const T* sl = ring + (size_t)slot * kSlice;
+        const T* sl = ring + (size_t)slot * kSlot + (size_t)half * kSlice;
 #pragma unroll
         for (int j = 0; j < 16 / VN; ++j) {
             const int pos = (j * 32 + lane) * VN;
@@ -2608,23 +2645,35 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
         uint32_t rtau_next = ld_relaxed_u32(rtp);
         int ncounted = 0;
         if constexpr (TMA) {
-            // Counting phase: every element of the first slices already in the rings is
-            // counted into the bins (a large K needs more than one lane maximum per lane
-            // to start near the K-th key); the group totals are then summed from the
-            // bins once, and every warp takes the threshold.
-            ncounted = min(RS, ns);
+            // Counting phase: each lane counts the m largest keys of each of the first
+            // slices already in the rings (m grows with K, so the counted set holds
+            // nearly all of those slices' top-K); the group totals are then summed from
+            // the bins once, and every warp takes the threshold.
+            const int mc = K <= 256 ? 1 : (K <= 512 ? 2 : 4);
+            ncounted = min(2 * RS, ns);
             int pjc = pj;
             for (int q = 0; q < ncounted; ++q) {
                 const int64_t start = a0 + (int64_t)q * kSlice;
                 const int n = (int)min((int64_t)kSlice, a1 - start);
-                const uint32_t c = cn + (uint32_t)q;
-                if (!mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
+                const uint32_t c = cn + (uint32_t)(q >> 1);
+                if ((q & 1) == 0 && !mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
                 float x[16];
-                load_ring(x, (int)(c % RS), n, row, start);
+                load_ring(x, (int)(c % RS), q & 1, n, row, start);
                 if (npen > 0) mask_penalised(x, pid, npen, pjc, start, n);
+                uint32_t top[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                    if (x[e] == x[e]) atomicAdd(&H[f2key(x[e]) >> 20], 1u);
+                for (int e = 0; e < 16; ++e) {
+                    uint32_t k = x[e] == x[e] ? f2key(x[e]) : 0u;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const uint32_t hi = max(top[r], k);
+                        k = min(top[r], k);
+                        top[r] = hi;
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                    if (r < mc && top[r]) atomicAdd(&H[top[r] >> 20], 1u);
             }
             __syncthreads();
             {
@@ -2649,10 +2698,10 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
             rtau_next = ld_relaxed_u32(rtp);
             float x[16];
             if constexpr (TMA) {
-                const int slot = (int)(cn % RS);
-                if (!mbar_wait_bounded(&full[slot], (cn / RS) & 1u)) timed_out = true;
-                load_ring(x, slot, n, row, start);
-                ++cn;
+                const uint32_t c = cn + (uint32_t)(q >> 1);
+                const int slot = (int)(c % RS);
+                if ((q & 1) == 0 && !mbar_wait_bounded(&full[slot], (c / RS) & 1u)) timed_out = true;
+                load_ring(x, slot, q & 1, n, row, start);
             } else {
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
@@ -2680,7 +2729,7 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
             const float lmax = max16(x);
             const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
             if constexpr (TMA) {
-                if (lane == 0) {
+                if (lane == 0 && ((q & 1) == 1 || q == ns - 1)) {
                     fence_proxy_async_smem();
                     issue();
                 }
@@ -2747,6 +2796,7 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
             }
             __syncwarp();
         }
+        if constexpr (TMA) cn += (uint32_t)((ns + 1) >> 1);  // slots this piece used
         VDXS_T1(10, t_item);
         __syncthreads();
         if (warp == 0) {
@@ -2779,16 +2829,17 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
 }
 
 // ---------------------------------------------------------------------------------
-// Small batches: one thread-block cluster of kClusterCTAs CTAs per row. Each CTA copies
-// its 1/kClusterCTAs of the row into shared memory (one bulk copy stream, no
+// Small batches: one thread-block cluster of CL CTAs per row. Each CTA copies its 1/CL
+// of the row into shared memory (one bulk copy stream, no
 // multicast), masks the penalised ids, and sends each thread's maximum to the leader
 // CTA through distributed shared memory. The K-th largest of those maxima is a lower
 // bound on the row's K-th key (they are K distinct elements of the row); every CTA then
 // sends the leader its elements at or above it, or, if more than its slot holds, its
 // exact top-K with tie evidence. The leader runs stage 2 on what it gathered.
 // ---------------------------------------------------------------------------------
-constexpr int kClusterCTAs = 8;
+constexpr int kClusterCTAs = 8;     // CTAs per row's cluster (portable size)
 constexpr int kClusterMaxRows = 8;  // batches up to this size take the cluster path
+constexpr int kClusterMaxWords = 8 * NT;  // thread-maxima area (then the warps' send batches)
 
 template <typename T>
 __device__ __forceinline__ T nan_bits();
@@ -2796,6 +2847,42 @@ template <>
 __device__ __forceinline__ float nan_bits<float>() { return __uint_as_float(0x7FC00000u); }
 template <>
 __device__ __forceinline__ uint16_t nan_bits<uint16_t>() { return (uint16_t)0x7FC0u; }
+
+// Warp 0 only: the highest bin g of h[0..256) with at least `need` counts in bins >= g.
+// Writes sh[0] = g (0xFFFFFFFF if the total is below need), sh[1] = count in bins > g.
+__device__ void warp_suffix_find256(const uint32_t* h, uint32_t need, uint32_t* sh) {
+    const int l = threadIdx.x & 31;
+    uint32_t c[8], s = 0u;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        c[u] = h[8 * l + u];
+        s += c[u];
+    }
+    const uint32_t suf = warp_suffix_sum(s);  // counts in bins >= 8l
+    const unsigned m = __ballot_sync(FULL, suf >= need);
+    if (m == 0u) {
+        if (l == 0) sh[0] = 0xFFFFFFFFu;
+        return;
+    }
+    if (l == 31 - __clz((int)m)) {
+        uint32_t above = suf - s;  // counts in bins >= 8(l+1)
+        int g = 8 * l;
+        bool found = false;
+#pragma unroll
+        for (int u = 7; u >= 0; --u) {
+            if (!found) {
+                if (above + c[u] >= need) {
+                    g = 8 * l + u;
+                    found = true;
+                } else {
+                    above += c[u];
+                }
+            }
+        }
+        sh[0] = (uint32_t)g;
+        sh[1] = above;
+    }
+}
 
 template <typename T>
 struct ChunkKeySrc {  // keys of a row chunk in shared memory (NaN: no element), tie-break = position
@@ -2809,8 +2896,8 @@ struct ChunkKeySrc {  // keys of a row chunk in shared memory (NaN: no element),
     __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
 };
 
-template <typename T, bool TMA>
-__global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) row_cluster_kernel(KParams p) {
+template <typename T, bool TMA, int CL>
+__global__ void __launch_bounds__(NT, 1) row_cluster_kernel(KParams p) {
     namespace cg = cooperative_groups;
     cg::cluster_group cl = cg::this_cluster();
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -2828,10 +2915,10 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     const int n = (int)max((int64_t)0, min((int64_t)L, (int64_t)p.V - lo));
     T* xs = (T*)region;
     uint32_t* maxk = (uint32_t*)(region + p.span);  // p.span: bytes of the chunk area
-    const int ncap = kClusterCTAs * cap + p.pen_stride;
-    uint32_t* ckey = maxk + kClusterCTAs * NT;
+    const int ncap = CL * cap + p.pen_stride;
+    uint32_t* ckey = maxk + kClusterMaxWords;
     uint32_t* cidx = ckey + ncap;
-    uint32_t* cuts = cidx + ncap;  // [kClusterCTAs]
+    uint32_t* cuts = cidx + ncap;  // [CL]
     const T* row = (const T*)p.logits + (int64_t)b * p.stride;
 
     // 1. The chunk into shared memory.
@@ -2873,8 +2960,9 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
         }
         __syncthreads();
     }
-    // 3. Bound: this CTA's K-th largest thread maximum (K distinct elements of the row at
-    // or above it), raised into the leader's bound; the leader keeps the largest.
+    // 3. Bound: every thread maximum (CL * NT distinct elements of the row) goes to the
+    // leader, which takes the K-th largest of them to a 16-bit key prefix: a lower bound
+    // on the row's K-th key.
     if (r == 0 && tid == 0) {
         sh[19] = 0u;  // bound
         sh[41] = 0u;  // candidates reserved
@@ -2890,15 +2978,32 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     }
     for (; i < n; i += NT) m0 = fmaxf(m0, to_f(xs[i]));
     const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-    // (key, thread) composites are distinct, so exactly one thread has rank K-1.
-    uint64_t* mk = (uint64_t*)maxk;
-    const uint64_t mine = ((uint64_t)(mx == mx ? f2key(mx) : 0u) << 32) | (uint32_t)tid;
-    mk[tid] = mine;
+    cl.map_shared_rank(maxk, 0)[r * NT + tid] = mx == mx ? f2key(mx) : 0u;
     cl.sync();  // also publishes the leader's zeroed scalars
-    if (K <= NT) {
-        int rank = 0;
-        for (int j = 0; j < NT; ++j) rank += mk[j] > mine ? 1 : 0;
-        if (rank == K - 1 && (uint32_t)(mine >> 32) != 0u) atomicMax(cl.map_shared_rank(&sh[19], 0), (uint32_t)(mine >> 32));
+    if (r == 0 && K <= CL * NT) {
+        // Two 256-bin passes over the top 16 key bits.
+        uint32_t b1 = 0u, need = (uint32_t)K;
+        for (int pass = 0; pass < 2; ++pass) {
+            const int shift = pass == 0 ? 24 : 16;
+            for (int j = tid; j < 256; j += NT) hist[j] = 0u;
+            __syncthreads();
+            for (int j = tid; j < CL * NT; j += NT) {
+                const uint32_t k = maxk[j];
+                if (k != 0u && (pass == 0 || (k >> 24) == b1)) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+            }
+            __syncthreads();
+            if (tid < 32) warp_suffix_find256(hist, need, sh + 16);
+            __syncthreads();
+            const uint32_t g = sh[16];
+            __syncthreads();
+            if (g == 0xFFFFFFFFu) break;  // fewer than K maxima: no bound
+            if (pass == 0) {
+                b1 = g;
+                need -= sh[17];
+            } else if (tid == 0) {
+                sh[19] = (b1 << 24) | (g << 16);
+            }
+        }
     }
     cl.sync();
     VDXS_T1(21, t_c2);
@@ -2910,10 +3015,10 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     uint32_t* lcnt = cl.map_shared_rank(&sh[41], 0);
     uint32_t* lovf = cl.map_shared_rank(&sh[42], 0);
     const uint32_t gbase = (uint32_t)(p.vocab_offset + lo);
-    const uint32_t total_cap = (uint32_t)(kClusterCTAs * cap);
+    const uint32_t total_cap = (uint32_t)(CL * cap);
     // Each warp gathers its candidates locally (its 1 KB of the maxima area, free now)
     // and reserves the leader's slots once per batch of up to kWarpBatch.
-    constexpr int kWarpBatch = (kClusterCTAs * NT * 4) / (NWARPS * 8);  // 128 (key, index) pairs
+    constexpr int kWarpBatch = (kClusterMaxWords * 4) / (NWARPS * 8);  // 128 (key, index) pairs
     uint32_t* wk = maxk + (size_t)(tid >> 5) * (2 * kWarpBatch);
     uint32_t* wi = wk + kWarpBatch;
     int wn = 0;
@@ -2995,12 +3100,12 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     // 5. Leader: stage 2 on the gathered candidates and penalised entries.
     int nc;
     if (overflow) {
-        for (int j = tid; j < kClusterCTAs * cap; j += NT)
+        for (int j = tid; j < CL * cap; j += NT)
             if ((uint32_t)(j % cap) >= sh[48 + j / cap]) ckey[j] = 0u;  // unused slots: no element
-        nc = kClusterCTAs * cap;
+        nc = CL * cap;
     } else {
         nc = (int)sh[41];
-        for (int j = tid; j < kClusterCTAs; j += NT) cuts[j] = 0u;
+        for (int j = tid; j < CL; j += NT) cuts[j] = 0u;
     }
     for (int j = tid; j < npen; j += NT) {
         ckey[nc + j] = f2key(p.pen_vals[(int64_t)b * p.pen_stride + j]);
@@ -3011,7 +3116,7 @@ __global__ void __cluster_dims__(kClusterCTAs, 1, 1) __launch_bounds__(NT, 1) ro
     uint32_t gm = 0u;
     for (int j = tid; j < n2; j += NT) gm = max(gm, ckey[j]);
     gm = block_max_u32(gm, sh + 32);
-    finish_select<T>(p, b, ckey, cidx, n2, gm, kClusterCTAs, [&](int i) -> uint32_t { return cuts[i]; }, region, hist,
+    finish_select<T>(p, b, ckey, cidx, n2, gm, CL, [&](int i) -> uint32_t { return cuts[i]; }, region, hist,
                      sh);
     VDXS_T1(23, t_c4);
 }
@@ -3347,18 +3452,20 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     const size_t esz = a.dtype == VDXS_DTYPE_BF16 ? 2 : 4;
     const bool faithful = a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit;
     if (a.B <= kClusterMaxRows) {
-        // Small batches: one cluster per row when a row's 1/8 fits in shared memory.
-        const int64_t L = ((V + kClusterCTAs - 1) / kClusterCTAs + 15) / 16 * 16;
-        const int cap = std::max(K, 512);
-        size_t xs_area = align16((size_t)L * esz);
-        xs_area = std::max(xs_area, align16((size_t)8 * K + 16));  // finish_select's sk / si
-        if (faithful) xs_area = std::max(xs_area, align16(faithful_bytes(K)));
-        const size_t ncap = (size_t)kClusterCTAs * cap + pen_stride;
-        const int P2 = pow2_at_least(K, 32);
-        const size_t cand_area = std::max((size_t)8 * ncap, (size_t)24 * P2 + 64);  // also stage 2's work
-        const size_t need = kHeadBytes + xs_area + (size_t)4 * kClusterCTAs * NT + cand_area + 4 * kClusterCTAs + 16;
-        if ((int64_t)need + 1024 <= smem_optin && L <= INT32_MAX) {  // 1 KB: the kernel's static shared memory
+        // Small batches: one cluster per row when a row's 1/CL fits in shared memory.
+        for (const int CL : {kClusterCTAs}) {
+            const int64_t L = ((V + CL - 1) / CL + 15) / 16 * 16;
+            const int cap = std::max(K, 512);
+            size_t xs_area = align16((size_t)L * esz);
+            xs_area = std::max(xs_area, align16((size_t)8 * K + 16));  // finish_select's sk / si
+            if (faithful) xs_area = std::max(xs_area, align16(faithful_bytes(K)));
+            const size_t ncap = (size_t)CL * cap + pen_stride;
+            const int P2 = pow2_at_least(K, 32);
+            const size_t cand_area = std::max((size_t)8 * ncap, (size_t)24 * P2 + 64);  // also stage 2's work
+            const size_t need = kHeadBytes + xs_area + (size_t)4 * kClusterMaxWords + cand_area + 4 * CL + 16;
+            if ((int64_t)need + 1024 > smem_optin || L > INT32_MAX) continue;  // 1 KB: the static shared memory
             plan->cluster = true;
+            plan->cluster_ctas = CL;
             plan->stream = false;
             plan->chunk = (int)L;
             plan->span = (int)xs_area;
@@ -3733,12 +3840,24 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
     const size_t esz = sizeof(T);
     const bool vec = ((uintptr_t)a.logits % 16 == 0) && (((size_t)a.stride * esz) % 16 == 0);
     if (plan.cluster) {
-        void (*kc)(KParams) = vec ? row_cluster_kernel<T, true> : row_cluster_kernel<T, false>;
+        const int CL = plan.cluster_ctas;
+        void (*kc)(KParams) = vec ? row_cluster_kernel<T, true, kClusterCTAs> : row_cluster_kernel<T, false, kClusterCTAs>;
         if ((e = cudaFuncSetAttribute(kc, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem)) != cudaSuccess)
             return e;
+        cudaLaunchConfig_t lc = {};
+        lc.gridDim = dim3(CL, a.B);
+        lc.blockDim = dim3(NT);
+        lc.dynamicSmemBytes = plan.smem;
+        lc.stream = a.stream;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = CL;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        lc.attrs = at;
+        lc.numAttrs = 1;
         if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
-        kc<<<dim3(kClusterCTAs, a.B), NT, plan.smem, a.stream>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if ((e = cudaLaunchKernelEx(&lc, kc, p)) != cudaSuccess) return e;
         count(a);
         return mark(a, a.ev_end);
     }
