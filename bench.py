@@ -135,13 +135,15 @@ def workload_config(name, world, spec, tie_mode):
     return cfg
 
 
-def dominant_kernel(cfg, vocab, esz):
+def dominant_kernel(cfg, vocab, esz, batch):
     """Name of the library kernel that streams the logits for this configuration."""
     t = "float" if esz == 4 else "bf16"
+    if batch <= 8 and (cfg.temperature == 0.0 or 0 < cfg.top_k < vocab):
+        return f"vdxs::row_cluster_kernel<{t}> (one 8-CTA cluster per row, batch<=8)"
     if cfg.temperature == 0.0 or 0 < cfg.top_k <= 128:
         return f"vdxs::topk_hist_kernel<{t}> (stage-1 stream top-k, k<=128)"
     if 0 < cfg.top_k < vocab:
-        return f"vdxs::topk_span_kernel<{t}> (span top-k, k>128, finish fused in the last CTA of a row)"
+        return f"vdxs::topk_wide_kernel<{t}> (stage-1 stream top-k, 128<k<=1024)"
     return f"vdxs::full_max_kernel<{t}> + vdxs::full_sum_kernel<{t}> (full softmax)"
 
 
@@ -213,9 +215,15 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     launches0 = ctx.launch_count()
     clocks = ClockSampler(local)
+    # The stage events are recorded on every 4th timed step only: each pair adds two
+    # event records to the step it brackets.
+    staged = [j for j in range(args.steps) if j % 4 == 0]
     with clocks:
         for j in range(args.steps):
-            ctx.set_stage_events(kb[j], ke[j])
+            if j % 4 == 0:
+                ctx.set_stage_events(kb[j], ke[j])
+            elif j % 4 == 1:
+                ctx.set_stage_events(None, None)
             starts[j].record(stream)
             step(args.warmup + j)
             ends[j].record(stream)
@@ -235,7 +243,7 @@ def run_ours(args, rank, world, local):
     value = B / (ms_per_step / 1e3)
     lat = sorted(per_step)
     p99 = lat[min(len(lat) - 1, int(round(0.99 * (len(lat) - 1))))]
-    kt = torch.tensor([statistics.mean(b.elapsed_time(e) for b, e in zip(kb, ke))], dtype=torch.float64, device=dev)
+    kt = torch.tensor([statistics.mean(kb[j].elapsed_time(ke[j]) for j in staged)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(kt, op=dist.ReduceOp.MAX)
     kern_ms = kt.item()
@@ -321,8 +329,8 @@ def run_ours(args, rank, world, local):
             if peak_kind == "measured" else peak_kind,
             "traffic": tr.get("bytes_per_launch") if tr else None,
             "traffic_source": tr.get("source") if tr else None,
-            "kernel": dominant_kernel(cfg, hi - off, esz),
-            "kernel_ms": round(kern_ms, 5), "alg_bytes_per_launch": alg_bytes,
+            "kernel": dominant_kernel(cfg, hi - off, esz, B),
+            "kernel_ms": round(kern_ms, 5), "kernel_ms_steps": len(staged), "alg_bytes_per_launch": alg_bytes,
             "step_frac": round(B * V * esz / (ms_per_step / 1e3) / 1e9 / peak, 4)}
 
     cpu = None
