@@ -938,9 +938,9 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
         __threadfence_block();
         return true;
     };
-    // Slots per lane. Up to four, the owning lane rescans its own slots after an
-    // insertion; beyond that the whole warp rescans them (lane u reads slot owner + 32*u)
-    // and two warp reductions give the owner's (minimum key, lowest slot).
+    // Slots per lane (lane l owns slots l, l + 32, ...). After an insertion the whole warp
+    // rescans the owner's slots (lane u reads slot owner + 32*u) and two warp reductions
+    // give the owner's (minimum key, lowest slot).
     const int RL = (K + 31) / 32;
     // Minimum of the slots this lane owns; the first slot wins ties (strict '<'). Eight
     // slots are loaded at a time so that their latencies overlap.
@@ -1010,62 +1010,65 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
             __syncwarp();
             VDXS_T1(25, t_sw);
             VDXS_T0(t_ss);
-            for (int k = 0; k < nready; ++k) {
-                const int sl = (t + k) % kFaithfulSlots;
-                const int total = s_cnt[sl];
-                const float* cv = rval + sl * kFaithfulSub;
-                const int32_t* ci = ridx + sl * kFaithfulSub;
+            // The ready sub-tiles' candidate lists are replayed as one stream, 32 at a
+            // time: lane k holds the end of sub-tile t + k's list in the stream.
+            const uint32_t cnt_k = lane < nready ? (uint32_t)s_cnt[(t + lane) % kFaithfulSlots] : 0u;
+            uint32_t end_k = cnt_k;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const uint32_t o = __shfl_up_sync(FULL, end_k, d);
+                if (lane >= d) end_k += o;
+            }
+            const int total = (int)__shfl_sync(FULL, end_k, 31);
 #ifdef VDXS_TIMING
-                if (lane == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
+            if (lane == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
 #endif
-                for (int c0 = 0; c0 < total; c0 += 32) {
-                    const int c = c0 + lane;
-                    const bool valid = c < total;
-                    const float v = valid ? cv[c] : 0.0f;
-                    const int32_t gi = valid ? ci[c] : 0;
-                    unsigned pend = __ballot_sync(FULL, valid && v > mv);
-                    while (pend) {
-                        const int l = __ffs(pend) - 1;
-                        if (lane == l) {
-                            sval[ms] = v;
-                            sidx[ms] = gi;
-                        }
-                        __syncwarp();
-#ifdef VDXS_TIMING
-                        if (lane == 0) atomicAdd(&g_phase_count[24], 1ull);
-                        const long long tq0 = clock64();
-#endif
-                        if (RL <= 4) {
-                            if (lane == (ms & 31)) kv = lane_min(bs);
-                        } else {
-                            const int owner = ms & 31, s2 = owner + 32 * lane;
-                            const uint32_t ok = lane < RL && s2 < K ? f2key(sval[s2]) : 0xFFFFFFFFu;
-                            const uint32_t omk = __reduce_min_sync(FULL, ok);
-                            const uint32_t obs = __reduce_min_sync(FULL, ok == omk ? (uint32_t)s2 : 0xFFFFFFFFu);
-                            if (lane == owner) {
-                                kv = omk;
-                                bs = (int)obs;
-                            }
-                        }
-#ifdef VDXS_TIMING
-                        __syncwarp();
-                        const long long tq1 = clock64();
-#endif
-                        const uint32_t mk = __reduce_min_sync(FULL, kv);
-                        ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
-                        mv = key2f(mk);
-#ifdef VDXS_TIMING
-                        if (lane == 0 && threadIdx.x == 0) {
-                            const long long tq2 = clock64();
-                            atomicAdd(&g_phase_cycles[27], (unsigned long long)(tq1 - tq0));
-                            atomicAdd(&g_phase_count[27], 1ull);
-                            atomicAdd(&g_phase_cycles[28], (unsigned long long)(tq2 - tq1));
-                            atomicAdd(&g_phase_count[28], 1ull);
-                        }
-#endif
-                        pend &= ~(1u << l);
-                        pend &= __ballot_sync(FULL, valid && v > mv);
+            for (int c0 = 0; c0 < total; c0 += 32) {
+                const int c = c0 + lane;
+                const bool valid = c < total;
+                // Sub-tile of stream position c: the number of list ends at or below c.
+                int k = 0;
+                uint32_t start = 0u;
+                for (int j = 0; j < nready; ++j) {
+                    const uint32_t e = __shfl_sync(FULL, end_k, j);
+                    if (e <= (uint32_t)c) {
+                        k = j + 1;
+                        start = e;
                     }
+                }
+                float v = 0.0f;
+                int32_t gi = 0;
+                if (valid) {
+                    const int sl = (t + k) % kFaithfulSlots;
+                    v = rval[sl * kFaithfulSub + (c - (int)start)];
+                    gi = ridx[sl * kFaithfulSub + (c - (int)start)];
+                }
+                unsigned pend = __ballot_sync(FULL, valid && v > mv);
+                while (pend) {
+                    const int l = __ffs(pend) - 1;
+                    if (lane == l) {
+                        sval[ms] = v;
+                        sidx[ms] = gi;
+                    }
+                    __syncwarp();
+#ifdef VDXS_TIMING
+                    if (lane == 0) atomicAdd(&g_phase_count[24], 1ull);
+#endif
+                    // The owner's slots are rescanned by the whole warp (lane u reads slot
+                    // owner + 32*u), then the buffer minimum over the lanes' minima.
+                    const int owner = ms & 31, s2 = owner + 32 * lane;
+                    const uint32_t ok = lane < RL && s2 < K ? f2key(sval[s2]) : 0xFFFFFFFFu;
+                    const uint32_t omk = __reduce_min_sync(FULL, ok);
+                    const uint32_t obs = __reduce_min_sync(FULL, ok == omk ? (uint32_t)s2 : 0xFFFFFFFFu);
+                    if (lane == owner) {
+                        kv = omk;
+                        bs = (int)obs;
+                    }
+                    const uint32_t mk = __reduce_min_sync(FULL, kv);
+                    ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
+                    mv = key2f(mk);
+                    pend &= ~(1u << l);
+                    pend &= __ballot_sync(FULL, valid && v > mv);
                 }
             }
             t += nready;
