@@ -312,6 +312,33 @@ def run_ours(args, rank, world, local):
                         "d2h_bytes_per_step": B * 4, "steps": E,
                         "api": "TVdxSampler.Process on device-resident logits (vdxs_sampler_process)"}
 
+    # Device-resident decode loop (vdxs_decode_step): row uniforms from device PRNG states,
+    # sampling, history push and stop check, with no host round trip per token; one
+    # synchronisation after the loop.
+    device_decode = None
+    if world == 1 and not args.no_e2e and not args.profile:
+        from vindexllm_b200.sampler import DeviceDecodeState
+        dcfg = synth.sampler_config(name, seed=7)
+        W = dcfg.repeat_window
+        dds = DeviceDecodeState(B, W, device=local, prng_states=[[7 + r, 11, 13, 17] for r in range(B)])
+        if hist is not None and W > 0:
+            n = min(W, hist.shape[1])
+            dds.hist[:, :n].copy_(hist[:, :n])
+            dds.count.fill_(n)
+            dds.pos.fill_(n % W)
+        E = max(1, min(args.e2e_steps * 10, args.steps))
+        tok2 = torch.empty(B, dtype=torch.int32, device=dev)
+        dds.step(ctx, dcfg, x, tokens=tok2)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(E):
+            dds.step(ctx, dcfg, x, tokens=tok2)
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        device_decode = {"value": round(B * E / el, 1), "unit": "tokens/s", "steps": E,
+                         "api": "vdxs_decode_step (PRNG, history ring and stop check on the device, "
+                                "one synchronisation after the loop)"}
+
     peak, peak_kind = load_peaks()
     # The dominant kernel reads every logit once; its other traffic (candidates out) is
     # below 0.1% of that and is not counted as algorithmic.
@@ -349,6 +376,7 @@ def run_ours(args, rank, world, local):
                 "logits_gbs": round(B * V * esz / (ms_per_step / 1e3) / 1e9, 1),
                 "gpu_launches": launches,
                 "roofline": roof, "cpu_baseline": cpu, "e2e": e2e, "e2e_resident_logits": e2e_resident,
+                "device_decode": device_decode,
                 "clocks": clocks.summary()}
         print(json.dumps(line), flush=True)
     if comm is not None:

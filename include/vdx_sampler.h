@@ -229,6 +229,40 @@ VDXS_API int32_t vdxs_sampler_get_history(const vdxs_sampler* s, int32_t row, in
                                           int32_t capacity, int32_t* count, int32_t* pos);
 
 /* ------------------------------------------------------------------------------
+ * Device-resident decode state: the row PRNGs and history rings that the stateful
+ * sampler keeps on the host (Sampler.pas:42-50, 157-248, 530-549), kept instead in
+ * caller-owned device buffers, so that a decode loop samples without a host round trip
+ * per token. The reference has no such interface (its sampler runs on the host).
+ *   d_prng        [batch][4] uint64 xoshiro256** states, in the layout of
+ *                 vdxs_sampler_get_prng_state (seed them there, or by the reference's
+ *                 SplitMix64 rule, Sampler.pas:224-241, and copy them to the device)
+ *   d_hist        [batch][window] int32 history rings; d_hist_pos and d_hist_count
+ *                 [batch] int32 (zero for an empty ring, as after ResetHistory)
+ * ---------------------------------------------------------------------------- */
+/* NextFloat (Sampler.pas:243-248) of every row on the device: writes d_uniforms[batch]
+ * and advances each row's state by one step, bit-identical to vdxs_sampler_next_float. */
+VDXS_API int32_t vdxs_device_uniforms(uint64_t* d_prng, int32_t batch, float* d_uniforms, void* stream);
+/* AddToHistory (Sampler.pas:530-539) of d_tokens[batch] into the rings (nothing when
+ * window <= 0). When n_stop > 0, rows whose token is one of d_stop_ids[n_stop] get
+ * d_stopped[row] = 1; other rows' flags are left as they are. */
+VDXS_API int32_t vdxs_device_history_push(int32_t* d_hist, int32_t* d_hist_pos, int32_t* d_hist_count,
+                                          int32_t window, const int32_t* d_tokens, int32_t batch,
+                                          const int32_t* d_stop_ids, int32_t n_stop, int32_t* d_stopped,
+                                          void* stream);
+/* One decode step on `stream`, all on the device: the row uniforms from d_prng into
+ * d_uniforms[batch] (unless temperature == 0: Process draws only then, Sampler.pas:448,
+ * 514), vdxs_sample with the rings as the history (window = cfg->repeat_window), then
+ * the tokens pushed into the rings and the stop check. It returns the tokens that
+ * vdxs_sampler_process followed by vdxs_sampler_add_to_history_batch return on the same
+ * host state. Asynchronous: call vdxs_device_status after a run of steps. */
+VDXS_API int32_t vdxs_decode_step(vdxs_context* ctx, const vdxs_config* cfg, const void* d_logits,
+                                  int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,
+                                  uint64_t* d_prng, float* d_uniforms, int32_t* d_hist,
+                                  int32_t* d_hist_pos, int32_t* d_hist_count,
+                                  const int32_t* d_stop_ids, int32_t n_stop, int32_t* d_stopped,
+                                  int32_t* d_out_tokens, void* stream);
+
+/* ------------------------------------------------------------------------------
  * Vocab-sharded sampling over several GPUs (one process or thread per GPU).
  * Each rank holds a contiguous vocab shard [vocab_offset, vocab_offset + vocab_shard)
  * of every row. Each rank selects its local top-k (lowest global index wins ties),

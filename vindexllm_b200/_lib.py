@@ -31,6 +31,9 @@ SIGNATURES = {
                              vp, i32, vp]),
     "vdxs_sample_host": (i32, [vp, P(VdxsConfig), vp, i32, i32, i32, i64, vp, i64, vp, vp, vp, vp]),
     "vdxs_sample_noalloc": (i32, [P(VdxsConfig), i32, vp, i32, i32, i32, i64, vp, i64, vp, vp, vp, vp]),
+    "vdxs_device_uniforms": (i32, [vp, i32, vp, vp]),
+    "vdxs_device_history_push": (i32, [vp, vp, vp, i32, vp, i32, vp, i32, vp, vp]),
+    "vdxs_decode_step": (i32, [vp, P(VdxsConfig), vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, i32, vp, vp, vp]),
     "vdxs_sampler_create": (i32, [vp, i32, P(vp)]),
     "vdxs_sampler_destroy": (i32, [vp]),
     "vdxs_sampler_set_config": (i32, [vp, P(VdxsConfig)]),

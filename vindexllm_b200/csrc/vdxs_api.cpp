@@ -290,6 +290,74 @@ VDXS_API int32_t vdxs_sample(vdxs_context* ctx, const vdxs_config* cfg, const vo
 }
 
 
+// Device-resident decode state (no reference C interface: the reference keeps the PRNG
+// and the ring on the host, Sampler.pas:157-248, 530-549).
+VDXS_API int32_t vdxs_device_uniforms(uint64_t* d_prng, int32_t batch, float* d_uniforms, void* stream) {
+    if (!d_prng || !d_uniforms) return fail(nullptr, VDXS_E_INVALID_ARG, "NULL argument");
+    if (batch < 1 || batch > 65535) return fail(nullptr, VDXS_E_INVALID_ARG, "batch %d out of range [1,65535]", batch);
+    const cudaError_t e = vdxs::launch_device_uniforms(d_prng, batch, d_uniforms, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "uniforms launch");
+    ok(nullptr);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_device_history_push(int32_t* d_hist, int32_t* d_hist_pos, int32_t* d_hist_count,
+                                          int32_t window, const int32_t* d_tokens, int32_t batch,
+                                          const int32_t* d_stop_ids, int32_t n_stop, int32_t* d_stopped,
+                                          void* stream) {
+    if (!d_tokens) return fail(nullptr, VDXS_E_INVALID_ARG, "NULL tokens");
+    if (batch < 1 || batch > 65535) return fail(nullptr, VDXS_E_INVALID_ARG, "batch %d out of range [1,65535]", batch);
+    if (window > 0 && (!d_hist || !d_hist_pos || !d_hist_count))
+        return fail(nullptr, VDXS_E_INVALID_ARG, "history ring buffers are NULL");
+    if (n_stop < 0 || (n_stop > 0 && (!d_stop_ids || !d_stopped)))
+        return fail(nullptr, VDXS_E_INVALID_ARG, "stop list: n_stop %d with NULL buffers", n_stop);
+    const cudaError_t e = vdxs::launch_history_push(d_hist, d_hist_pos, d_hist_count, window > 0 ? window : 0,
+                                                    d_tokens, batch, d_stop_ids, n_stop, d_stopped,
+                                                    (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "history push launch");
+    ok(nullptr);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_decode_step(vdxs_context* ctx, const vdxs_config* cfg, const void* d_logits, int32_t dtype,
+                                  int32_t batch, int32_t vocab, int64_t row_stride, uint64_t* d_prng,
+                                  float* d_uniforms, int32_t* d_hist, int32_t* d_hist_pos, int32_t* d_hist_count,
+                                  const int32_t* d_stop_ids, int32_t n_stop, int32_t* d_stopped,
+                                  int32_t* d_out_tokens, void* stream) {
+    if (!ctx || !cfg) return fail(ctx, VDXS_E_INVALID_ARG, "NULL argument");
+    const bool greedy = cfg->temperature == 0.0f;
+    if (!greedy && (!d_prng || !d_uniforms)) return fail(ctx, VDXS_E_INVALID_ARG, "PRNG state or uniforms are NULL");
+    const int32_t W = cfg->repeat_window > 0 ? cfg->repeat_window : 0;
+    if (W > 0 && (!d_hist || !d_hist_pos || !d_hist_count))
+        return fail(ctx, VDXS_E_INVALID_ARG, "history ring buffers are NULL");
+    if (n_stop < 0 || (n_stop > 0 && (!d_stop_ids || !d_stopped)))
+        return fail(ctx, VDXS_E_INVALID_ARG, "stop list: n_stop %d with NULL buffers", n_stop);
+    if (batch < 1 || batch > 65535) return fail(ctx, VDXS_E_INVALID_ARG, "batch %d out of range [1,65535]", batch);
+    DeviceGuard g(ctx->device);
+    const cudaStream_t st = (cudaStream_t)stream;
+    cudaError_t e;
+    int64_t n = 0;
+    if (!greedy) {
+        if ((e = vdxs::launch_device_uniforms(d_prng, batch, d_uniforms, st)) != cudaSuccess)
+            return cuda_fail(ctx, e, "uniforms launch");
+        ++n;
+    }
+    const bool pen = W > 0 && cfg->repeat_penalty != 1.0f;
+    int32_t rc = vdxs_sample(ctx, cfg, d_logits, dtype, batch, vocab, row_stride, pen ? d_hist : nullptr,
+                             pen ? (int64_t)W : 0, pen ? d_hist_count : nullptr, greedy ? nullptr : d_uniforms,
+                             d_out_tokens, stream);
+    if (rc != VDXS_OK) return rc;
+    if (W > 0 || n_stop > 0) {
+        if ((e = vdxs::launch_history_push(d_hist, d_hist_pos, d_hist_count, W, d_out_tokens, batch, d_stop_ids,
+                                           n_stop, d_stopped, st)) != cudaSuccess)
+            return cuda_fail(ctx, e, "history push launch");
+        ++n;
+    }
+    ctx->launches += n;
+    ok(ctx);
+    return VDXS_OK;
+}
+
 VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg, const void* h_logits, int32_t dtype,
                                   int32_t batch, int32_t vocab, int64_t row_stride, const int32_t* h_history,
                                   int64_t history_stride, const int32_t* h_history_count, const float* h_uniform,

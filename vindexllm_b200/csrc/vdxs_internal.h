@@ -120,6 +120,11 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
                              cudaStream_t stream, std::string* err);
 cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err);
 cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std::string* err);
+// Device-resident decode state (one thread per row).
+cudaError_t launch_device_uniforms(uint64_t* prng, int batch, float* out, cudaStream_t stream);
+cudaError_t launch_history_push(int32_t* hist, int32_t* pos, int32_t* count, int window, const int32_t* tokens,
+                                int batch, const int32_t* stop_ids, int n_stop, int32_t* stopped,
+                                cudaStream_t stream);
 void free_workspace(Workspace& ws);
 // Clears the device error word and the self-resetting counters (after a failed launch).
 cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream);

@@ -3929,6 +3929,65 @@ cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std
     return cudaSuccess;
 }
 
+// ---------------------------------------------------------------------------------
+// Device-resident decode state: per-row xoshiro256** (Sampler.pas:208-222, 243-248) and
+// history ring (Sampler.pas:530-539), one thread per row.
+// ---------------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t rotl64d(uint64_t x, int k) { return (x << k) | (x >> (64 - k)); }
+
+__global__ void device_uniforms_kernel(uint64_t* prng, int batch, float* out) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= batch) return;
+    uint64_t* s = prng + (size_t)4 * r;
+    uint64_t s0 = s[0], s1 = s[1], s2 = s[2], s3 = s[3];
+    const uint64_t result = rotl64d(s1 * 5ull, 7) * 9ull;
+    const uint64_t t = s1 << 17;
+    s2 ^= s0;
+    s3 ^= s1;
+    s1 ^= s2;
+    s0 ^= s3;
+    s2 ^= t;
+    s3 = rotl64d(s3, 45);
+    s[0] = s0;
+    s[1] = s1;
+    s[2] = s2;
+    s[3] = s3;
+    // (result >> 40) / 2^24: a 24-bit integer scaled by a power of two, exact in float.
+    out[r] = (float)(result >> 40) * (1.0f / 16777216.0f);
+}
+
+__global__ void history_push_kernel(int32_t* hist, int32_t* pos, int32_t* count, int window, const int32_t* tokens,
+                                    int batch, const int32_t* stop_ids, int n_stop, int32_t* stopped) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= batch) return;
+    const int32_t tok = tokens[r];
+    if (window > 0) {
+        int p = pos[r] % window;
+        if (p < 0) p += window;  // a position outside the ring never indexes outside it
+        hist[(int64_t)r * window + p] = tok;
+        pos[r] = (p + 1) % window;
+        if (count[r] < window) count[r] = max(count[r], 0) + 1;
+    }
+    if (n_stop > 0) {
+        bool hit = false;
+        for (int j = 0; j < n_stop; ++j) hit |= stop_ids[j] == tok;
+        if (hit) stopped[r] = 1;
+    }
+}
+
+cudaError_t launch_device_uniforms(uint64_t* prng, int batch, float* out, cudaStream_t stream) {
+    device_uniforms_kernel<<<(batch + NT - 1) / NT, NT, 0, stream>>>(prng, batch, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_history_push(int32_t* hist, int32_t* pos, int32_t* count, int window, const int32_t* tokens,
+                                int batch, const int32_t* stop_ids, int n_stop, int32_t* stopped,
+                                cudaStream_t stream) {
+    history_push_kernel<<<(batch + NT - 1) / NT, NT, 0, stream>>>(hist, pos, count, window, tokens, batch, stop_ids,
+                                                                    n_stop, stopped);
+    return cudaGetLastError();
+}
+
 }  // namespace vdxs
 
 #ifdef VDXS_TIMING

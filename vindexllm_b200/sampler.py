@@ -17,8 +17,8 @@ from . import abi
 from ._lib import load, check, VdxsError
 from .abi import VdxsConfig, default_config
 
-__all__ = ["SamplerContext", "TVdxSampler", "ShardComm", "VdxsError", "default_config", "shard_range",
-           "broadcast_unique_id"]
+__all__ = ["SamplerContext", "TVdxSampler", "ShardComm", "DeviceDecodeState", "VdxsError", "default_config",
+           "shard_range", "broadcast_unique_id"]
 
 
 def _stream_ptr(stream):
@@ -229,6 +229,56 @@ class TVdxSampler:
         check(self.lib.vdxs_sampler_get_history(self._h, row, buf, cap, C.byref(cnt), C.byref(pos)),
               self.ctx.handle)
         return list(buf[: cnt.value]), cnt.value, pos.value
+
+
+class DeviceDecodeState:
+    """Row PRNGs and history rings kept on the device (vdxs_device_uniforms,
+    vdxs_device_history_push, vdxs_decode_step), so a decode loop samples without a host
+    round trip per token. The reference keeps both inside TVdxSampler on the host
+    (Sampler.pas:157-248 PRNG, :530-549 ring); ``prng_states`` takes their 4-word states,
+    e.g. from ``TVdxSampler.GetPrngState``."""
+
+    def __init__(self, batch: int, window: int, device: int = 0, prng_states=None):
+        import torch
+        dev = torch.device("cuda", device)
+        self.lib = load()
+        self.batch, self.window = batch, window
+        self.prng = torch.zeros((batch, 4), dtype=torch.int64, device=dev)  # uint64 bit patterns
+        if prng_states is not None:
+            st = np.ascontiguousarray(np.asarray(prng_states, dtype=np.uint64).reshape(batch, 4)).view(np.int64)
+            self.prng.copy_(torch.from_numpy(st))
+        self.uniforms = torch.zeros(batch, dtype=torch.float32, device=dev)
+        self.hist = torch.zeros((batch, max(window, 1)), dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.count = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.stopped = torch.zeros(batch, dtype=torch.int32, device=dev)
+
+    def next_uniforms(self, stream=None):
+        """One NextFloat per row (Sampler.pas:243-248); returns the device tensor."""
+        check(self.lib.vdxs_device_uniforms(_dptr(self.prng), self.batch, _dptr(self.uniforms), _stream_ptr(stream)))
+        return self.uniforms
+
+    def push(self, tokens, stop_ids=None, stream=None):
+        """AddToHistory (Sampler.pas:530-539) of device tokens[batch]; flags stop tokens."""
+        n_stop = 0 if stop_ids is None else int(stop_ids.numel())
+        check(self.lib.vdxs_device_history_push(_dptr(self.hist), _dptr(self.pos), _dptr(self.count), self.window,
+                                                _dptr(tokens), self.batch, _dptr(stop_ids), n_stop,
+                                                _dptr(self.stopped), _stream_ptr(stream)))
+
+    def step(self, ctx: "SamplerContext", cfg: VdxsConfig, logits, stop_ids=None, tokens=None, stream=None):
+        """One device-resident decode step (vdxs_decode_step); returns the device tokens."""
+        import torch
+        assert logits.is_cuda and logits.dim() == 2 and logits.stride(1) == 1
+        B, V = logits.shape
+        assert B == self.batch and cfg.repeat_window == self.window
+        if tokens is None:
+            tokens = torch.empty(B, dtype=torch.int32, device=logits.device)
+        n_stop = 0 if stop_ids is None else int(stop_ids.numel())
+        check(self.lib.vdxs_decode_step(ctx._h, C.byref(cfg), _dptr(logits), _dtype_code(logits), B, V,
+                                        logits.stride(0), _dptr(self.prng), _dptr(self.uniforms), _dptr(self.hist),
+                                        _dptr(self.pos), _dptr(self.count), _dptr(stop_ids), n_stop,
+                                        _dptr(self.stopped), _dptr(tokens), _stream_ptr(stream)), ctx._h)
+        return tokens
 
 
 def shard_range(vocab: int, world: int, rank: int) -> tuple[int, int]:
