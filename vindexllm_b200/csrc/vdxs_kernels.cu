@@ -703,6 +703,10 @@ __global__ void __launch_bounds__(NT) penalty_prep_kernel(const T* logits, int64
         ++off;
     }
     if (tid == 0) pen_cnt[b] = total;
+    // Stage 1 may be launched as a programmatic dependent of this kernel (it waits for
+    // the whole grid before it reads the lists). The trigger comes after this CTA's
+    // work, so no CTA of this grid is left waiting for an SM held by stage 1.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------------
@@ -2112,6 +2116,10 @@ __global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
         }
         __syncwarp();
     }
+    // With a history, this kernel is a programmatic dependent of the penalty prep: the
+    // first slices are in flight; the penalty lists are read only after this wait (a
+    // no-op for an ordinary launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 
     // Slice loads: 16 values per lane; NaN marks positions past the end.
     // Half `half` of ring slot `slot` (n valid elements from row position start); the
@@ -2577,6 +2585,10 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
         }
         __syncwarp();
     }
+    // With a history, this kernel is a programmatic dependent of the penalty prep: the
+    // first slices are in flight; the penalty lists are read only after this wait (a
+    // no-op for an ordinary launch).
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // Half `half` of ring slot `slot` (n valid elements from row position start); the
     // bulk copy covered the slot's bytes rounded down to 16, which within a half is the
     // half's own count rounded the same way (a slice is a multiple of 16 bytes).
@@ -3879,8 +3891,24 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
                                       (int)plan.smem2)) != cudaSuccess)
             return e;
         if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
-        k1<<<plan.grid, NT, plan.smem, a.stream>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        if (a.penalty_on) {
+            // Programmatic dependent of the penalty prep: its launch overlaps the prep's
+            // tail; the kernel waits for the prep grid before it reads the lists.
+            cudaLaunchConfig_t lc1 = {};
+            lc1.gridDim = dim3(plan.grid);
+            lc1.blockDim = dim3(NT);
+            lc1.dynamicSmemBytes = plan.smem;
+            lc1.stream = a.stream;
+            cudaLaunchAttribute at1[1];
+            at1[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at1[0].val.programmaticStreamSerializationAllowed = 1;
+            lc1.attrs = at1;
+            lc1.numAttrs = 1;
+            if ((e = cudaLaunchKernelEx(&lc1, k1, p)) != cudaSuccess) return e;
+        } else {
+            k1<<<plan.grid, NT, plan.smem, a.stream>>>(p);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        }
         if ((e = mark(a, a.ev_end)) != cudaSuccess) return e;
         {
             // Programmatic dependent launch: finish CTAs are scheduled as stage-1 CTAs
