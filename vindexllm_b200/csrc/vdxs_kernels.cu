@@ -2983,16 +2983,24 @@ __global__ void __launch_bounds__(NT, 1) row_cluster_kernel(KParams p) {
         sh[41] = 0u;  // candidates reserved
         sh[42] = 0u;  // overflow
     }
-    float m0 = __uint_as_float(0x7FC00000u), m1 = m0, m2 = m0, m3 = m0;
-    int i = tid;
-    for (; i + 3 * NT < n; i += 4 * NT) {
-        m0 = fmaxf(m0, to_f(xs[i]));
-        m1 = fmaxf(m1, to_f(xs[i + NT]));
-        m2 = fmaxf(m2, to_f(xs[i + 2 * NT]));
-        m3 = fmaxf(m3, to_f(xs[i + 3 * NT]));
+    // Each thread's maximum over its 16-byte groups of the chunk (any partition of the
+    // chunk gives maxima of distinct elements), then the ragged tail.
+    constexpr int GV = (int)(16 / sizeof(T));
+    float m0 = __uint_as_float(0x7FC00000u), m1 = m0;
+    {
+        const int ng4 = n / GV;
+        for (int g = tid; g < ng4; g += NT) {
+            float v[GV];
+            unpack(*reinterpret_cast<const uint4*>(xs + (size_t)g * GV), v, T());
+#pragma unroll
+            for (int e = 0; e < GV; e += 2) {
+                m0 = fmaxf(m0, v[e]);
+                m1 = fmaxf(m1, v[e + 1]);
+            }
+        }
+        for (int i = ng4 * GV + tid; i < n; i += NT) m0 = fmaxf(m0, to_f(xs[i]));
     }
-    for (; i < n; i += NT) m0 = fmaxf(m0, to_f(xs[i]));
-    const float mx = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+    const float mx = fmaxf(m0, m1);
     cl.map_shared_rank(maxk, 0)[r * NT + tid] = mx == mx ? f2key(mx) : 0u;
     cl.sync();  // also publishes the leader's zeroed scalars
     if (r == 0 && K <= CL * NT) {
