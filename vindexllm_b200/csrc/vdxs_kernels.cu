@@ -2845,10 +2845,10 @@ __global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
 
 // ---------------------------------------------------------------------------------
 // Small batches: one thread-block cluster of CL CTAs per row. Each CTA copies its 1/CL
-// of the row into shared memory (one bulk copy stream, no
-// multicast), masks the penalised ids, and sends each thread's maximum to the leader
-// CTA through distributed shared memory. The K-th largest of those maxima is a lower
-// bound on the row's K-th key (they are K distinct elements of the row); every CTA then
+// of the row into its own shared memory (plain bulk copies of this CTA's part), masks
+// the penalised ids, and sends each thread's maximum to the leader CTA through
+// distributed shared memory. The leader takes the K-th largest of those maxima, a lower
+// bound on the row's K-th key (they are distinct elements of the row); every CTA then
 // sends the leader its elements at or above it, or, if more than its slot holds, its
 // exact top-K with tie evidence. The leader runs stage 2 on what it gathered.
 // ---------------------------------------------------------------------------------
