@@ -338,6 +338,22 @@ def run_ours(args, rank, world, local):
         device_decode = {"value": round(B * E / el, 1), "unit": "tokens/s", "steps": E,
                          "api": "vdxs_decode_step (PRNG, history ring and stop check on the device, "
                                 "one synchronisation after the loop)"}
+        # The same step captured once in a CUDA graph and replayed: no per-step launch work
+        # on the host.
+        gds = DeviceDecodeState(B, W, device=local, prng_states=[[7 + r, 11, 13, 17] for r in range(B)])
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            gds.step(ctx, dcfg, x, tokens=tok2)
+        graph.replay()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(E):
+            graph.replay()
+        torch.cuda.synchronize()
+        el = time.perf_counter() - t0
+        del graph
+        device_decode["graph_replay"] = {"value": round(B * E / el, 1), "unit": "tokens/s",
+                                         "us_per_step": round(el / E * 1e6, 2)}
 
     peak, peak_kind = load_peaks()
     # The dominant kernel reads every logit once; its other traffic (candidates out) is

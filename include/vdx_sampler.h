@@ -254,7 +254,9 @@ VDXS_API int32_t vdxs_device_history_push(int32_t* d_hist, int32_t* d_hist_pos, 
  * 514), vdxs_sample with the rings as the history (window = cfg->repeat_window), then
  * the tokens pushed into the rings and the stop check. It returns the tokens that
  * vdxs_sampler_process followed by vdxs_sampler_add_to_history_batch return on the same
- * host state. Asynchronous: call vdxs_device_status after a run of steps. */
+ * host state. Asynchronous: call vdxs_device_status after a run of steps. After one
+ * warm-up call with the same shapes (so the context's workspace no longer grows) the step
+ * can be captured in a CUDA graph and replayed, each replay advancing the device state. */
 VDXS_API int32_t vdxs_decode_step(vdxs_context* ctx, const vdxs_config* cfg, const void* d_logits,
                                   int32_t dtype, int32_t batch, int32_t vocab, int64_t row_stride,
                                   uint64_t* d_prng, float* d_uniforms, int32_t* d_hist,

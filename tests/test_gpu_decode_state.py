@@ -77,3 +77,39 @@ def test_history_push_and_stop_flags(gpu_ctx):
     assert (dev.hist.cpu().numpy() == want).all()
     assert dev.count.cpu().tolist() == [3] * B and dev.pos.cpu().tolist() == [1] * B
     assert dev.stopped.cpu().tolist() == [0, 1, 1, 0, 0]
+
+
+@pytest.mark.parametrize("B", [4, 12])  # cluster path; stream path with the penalty prep
+def test_decode_step_replayed_from_a_cuda_graph(gpu_ctx, B):
+    """A decode step captured once in a CUDA graph (after a warm-up call, so that the
+    context's workspace no longer grows) and replayed four times gives the tokens, rings
+    and PRNG states of four eager steps from the same state."""
+    import torch
+    from vindexllm_b200.sampler import DeviceDecodeState
+    gpu_ctx.set_tie_mode(abi.TIES_FAITHFUL)
+    rng = np.random.default_rng(17)
+    V, W = 40000, 16
+    cfg = default_config(temperature=0.9, top_k=40, top_p=0.9, repeat_penalty=1.2, repeat_window=W)
+    x = _logits(rng, B, V, rng.choice(V, size=5, replace=False))
+    states = [[0x9E3779B97F4A7C15 + r, 0xBF58476D1CE4E5B9, 0x94D049BB133111EB, 7 + 3 * r] for r in range(B)]
+    eager = DeviceDecodeState(B, W, prng_states=states)
+    want = [eager.step(gpu_ctx, cfg, x).cpu().numpy() for _ in range(4)]
+    warm = DeviceDecodeState(B, W, prng_states=states)
+    tok = torch.empty(B, dtype=torch.int32, device="cuda")
+    warm.step(gpu_ctx, cfg, x, tokens=tok)
+    torch.cuda.synchronize()
+    graphed = DeviceDecodeState(B, W, prng_states=states)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        graphed.step(gpu_ctx, cfg, x, tokens=tok)
+    got = []
+    for _ in range(4):
+        g.replay()
+        got.append(tok.cpu().numpy())
+    gpu_ctx.device_status()
+    for a, b in zip(got, want):
+        assert (a == b).all(), f"graph {a} eager {b}"
+    assert (graphed.hist.cpu() == eager.hist.cpu()).all()
+    assert (graphed.prng.cpu() == eager.prng.cpu()).all()
+    assert (graphed.count.cpu() == eager.count.cpu()).all() and (graphed.pos.cpu() == eager.pos.cpu()).all()
+    del g
