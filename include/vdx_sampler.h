@@ -178,13 +178,25 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg,
  * array's device address (once per device, with that device current); make that
  * first call before any stream capture. All calls share the one array and it keeps
  * the last call's contents, so calls that overlap on the GPU (other streams, other
- * host threads) race: serialise them. `tie_mode` is VDXS_TIES_FAITHFUL or
+ * host threads) race: serialise them. `stream` must belong to the current device
+ * (VDXS_E_INVALID_ARG otherwise). `tie_mode` is VDXS_TIES_FAITHFUL or
  * VDXS_TIES_CANONICAL; the other arguments are those of vdxs_sample. */
 VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, const void* d_logits,
                                      int32_t dtype, int32_t batch, int32_t vocab,
                                      int64_t row_stride, const int32_t* d_history,
                                      int64_t history_stride, const int32_t* d_history_count,
                                      const float* d_uniform, int32_t* d_out_tokens, void* stream);
+
+/* Status of the last vdxs_sample_noalloc call on the current device, for callers that
+ * have no context to pass to vdxs_device_status. Waits for `stream` (the stream of that
+ * call, on the current device), then reads the device error word that the call's
+ * kernels set instead of trapping: VDXS_E_TIMEOUT when a bounded wait gave up,
+ * VDXS_E_DEVICE_STATE when an internal selection check failed; the tokens of that call
+ * are then not valid. The word lives in the fixed array and the next
+ * vdxs_sample_noalloc call clears it, so check after each call whose tokens matter.
+ * Allocates nothing (the word is copied into a host variable). No counterpart in the
+ * reference, whose Process runs on the host and cannot fail. */
+VDXS_API int32_t vdxs_noalloc_status(void* stream);
 
 /* ------------------------------------------------------------------------------
  * Stateful mirror of TVdxSampler: one sampler state (config, xoshiro256** PRNG,

@@ -62,6 +62,49 @@ def test_decode_step_matches_stateful_sampler(gpu_ctx, mode, temperature):
     gpu_ctx.set_tie_mode(abi.TIES_FAITHFUL)
 
 
+@pytest.mark.parametrize("temperature", [0.8, 0.0])
+def test_decode_step_matches_oracle_samplers(gpu_ctx, oracle_mod, temperature):
+    """vdxs_decode_step against the CPU restatement of TVdxSampler, one oracle object per
+    row: each step the oracle runs Process (Sampler.pas:265-528, which draws NextFloat
+    from its own PRNG) and AddToHistory (:530-539) on the same logits; tokens must agree
+    at every step, and the rings and PRNG states afterwards."""
+    from vindexllm_b200.sampler import DeviceDecodeState
+    gpu_ctx.set_tie_mode(abi.TIES_FAITHFUL)
+    rng = np.random.default_rng(23)
+    B, V, W = 10, 60000, 24
+    cfg = default_config(temperature=temperature, top_k=32, top_p=0.9, repeat_penalty=1.25, repeat_window=W,
+                         seed=99)
+    states = [[0x243F6A8885A308D3 + 7 * r, 0x13198A2E03707344, 0xA4093822299F31D0 ^ r, 0x082EFA98EC4E6C89]
+              for r in range(B)]
+    orc = []
+    for r in range(B):
+        o = oracle_mod.OracleSampler()
+        o.set_config(cfg)
+        o.set_state(states[r])
+        orc.append(o)
+    dev = DeviceDecodeState(B, W, prng_states=states)
+    hot = rng.choice(V, size=6, replace=False)
+    for step in range(8):
+        x = _logits(rng, B, V, hot)
+        xh = x.cpu().numpy()
+        want = []
+        for r in range(B):
+            t = orc[r].process(np.ascontiguousarray(xh[r]).copy())  # Process mutates its logits
+            orc[r].add_to_history(t)
+            want.append(t)
+        got = dev.step(gpu_ctx, cfg, x).cpu().numpy()
+        assert (got == np.array(want)).all(), f"step {step}: device {got} oracle {want}"
+    gpu_ctx.device_status()
+    hist, pos, cnt = dev.hist.cpu().numpy(), dev.pos.cpu().numpy(), dev.count.cpu().numpy()
+    prng = dev.prng.cpu().numpy().view(np.uint64)
+    for r in range(B):
+        ids, c, p = orc[r].history()
+        assert (c, p) == (int(cnt[r]), int(pos[r]))
+        assert ids[:c] == hist[r, :c].tolist()
+        assert orc[r].get_state() == prng[r].tolist()
+        orc[r].close()
+
+
 def test_history_push_and_stop_flags(gpu_ctx):
     import torch
     from vindexllm_b200.sampler import DeviceDecodeState

@@ -61,6 +61,48 @@ def test_random_small_batches(gpu_ctx, oracle_mod, mode, seed):
 
 
 @pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("seed", range(4))
+def test_random_stream_batches(gpu_ctx, oracle_mod, mode, seed):
+    """Batches above 8 rows (the persistent stream kernel and the finish kernel): odd
+    vocabulary sizes (row tails past the last full 4 KB slot), rows that start off a
+    16-byte boundary (plain-load staging), bf16, top_k from 1 to 1024, penalties with
+    out-of-range ids, quantised rows with many ties."""
+    import torch
+    rng = np.random.default_rng(100 + seed)
+    for trial in range(6):
+        B = int(rng.integers(9, 48))
+        V = int(rng.choice([1500, 4097, 33333, 65536, 100003]))
+        scale = float(rng.choice([0.3, 2.0, 6.0]))
+        x = rng.normal(size=(B, V + 1)) * scale
+        if trial % 3 == 0:
+            x = np.round(x * 2) / 2
+        x = x.astype(np.float32)
+        K = int(rng.choice([1, 2, 40, 64, 128, 200, 512, 1024]))
+        K = min(K, V - 1)
+        cfg = default_config(temperature=float(rng.choice([0.0, 0.7, 1.0, 1.5])), top_k=K,
+                             top_p=float(rng.choice([1.0, 0.95, 0.5])),
+                             min_p=float(rng.choice([0.0, 0.0, 0.05])),
+                             repeat_penalty=float(rng.choice([1.0, 1.3])))
+        W = int(rng.choice([8, 64]))
+        hist = rng.integers(-2, V + 2, size=(B, W)).astype(np.int32)
+        cnt = rng.integers(0, W + 1, size=B).astype(np.int32)
+        u = (rng.integers(0, 1 << 24, size=B) / 16777216.0).astype(np.float32)
+        full = _t(x)
+        off = int(rng.integers(0, 2))  # 1: rows start 4 bytes past a 16-byte boundary
+        view = full[:, off:off + V]
+        xo = x[:, off:off + V].copy()
+        out_k = K if K <= 64 else 0
+        if trial % 2 == 1:
+            xb = view.to(torch.bfloat16).contiguous()
+            g = gpu_run(gpu_ctx, cfg, xb, u, _t(hist), _t(cnt), mode, out_k=out_k)
+            o = oracle_run(oracle_mod, cfg, to_host_bits(xb), u, hist, cnt, mode, out_k=out_k)
+        else:
+            g = gpu_run(gpu_ctx, cfg, view, u, _t(hist), _t(cnt), mode, out_k=out_k)
+            o = oracle_run(oracle_mod, cfg, xo, u, hist, cnt, mode, out_k=out_k)
+        compare(g, o, mode, label=f"seed{seed} trial{trial} B{B} V{V} off{off} bf16{trial % 2} cfg {cfg.as_dict()}")
+
+
+@pytest.mark.parametrize("mode", MODES)
 def test_edge_cases(gpu_ctx, oracle_mod, mode):
     import torch
     cases = []
@@ -92,10 +134,10 @@ def test_edge_cases(gpu_ctx, oracle_mod, mode):
 
 @pytest.mark.parametrize("mode", MODES)
 def test_wide_topk_edge_cases(gpu_ctx, oracle_mod, mode):
-    """top_k above 128 at batches above 8 (the wide stream path). Constant rows make
-    every piece's list outgrow its capacity and one-bin rows overflow the finish gather,
-    so both reach the exact whole-row fallback; ascending rows and tied rows with a
-    repetition penalty take the ordinary gather."""
+    """Batches above 8 (the stream path) with a large and a small top_k. Constant rows
+    make every piece's list outgrow its capacity and one-bin rows overflow the finish
+    gather, so both reach the exact whole-row fallback; ascending rows and tied rows with
+    a repetition penalty take the ordinary gather."""
     rng = np.random.default_rng(23)
     B = 12
     cases = [("constant", np.zeros((B, 262144), np.float32), 200)]
@@ -105,15 +147,16 @@ def test_wide_topk_edge_cases(gpu_ctx, oracle_mod, mode):
     cases.append(("one_bin_shuffled", rng.permuted(d, axis=1), 1024))
     q = (np.round(rng.normal(size=(B, 100000)) * 4) / 4).astype(np.float32)
     cases.append(("quantised", q, 512))
-    for name, x, K in cases:
+    for name, x, K0 in cases:
         hist = rng.integers(0, x.shape[1], size=(B, 64)).astype(np.int32)
         cnt = np.full(B, 64, np.int32)
-        for cfg in [default_config(temperature=1.0, top_k=K, top_p=0.9, repeat_penalty=1.2),
-                    default_config(temperature=0.0, top_k=K)]:
-            u = rng.random(B).astype(np.float32)
-            g = gpu_run(gpu_ctx, cfg, _t(x), u, _t(hist), _t(cnt), mode, out_k=K)
-            o = oracle_run(oracle_mod, cfg, x, u, hist, cnt, mode, out_k=K)
-            compare(g, o, mode, label=f"{name} K{K} {cfg.as_dict()}")
+        for K in (K0, 5):  # the large top_k of the case, and a small one
+            for cfg in [default_config(temperature=1.0, top_k=K, top_p=0.9, repeat_penalty=1.2),
+                        default_config(temperature=0.0, top_k=K)]:
+                u = rng.random(B).astype(np.float32)
+                g = gpu_run(gpu_ctx, cfg, _t(x), u, _t(hist), _t(cnt), mode, out_k=K)
+                o = oracle_run(oracle_mod, cfg, x, u, hist, cnt, mode, out_k=K)
+                compare(g, o, mode, label=f"{name} K{K} {cfg.as_dict()}")
 
 
 @pytest.mark.parametrize("mode", MODES)

@@ -31,6 +31,7 @@ SIGNATURES = {
                              vp, i32, vp]),
     "vdxs_sample_host": (i32, [vp, P(VdxsConfig), vp, i32, i32, i32, i64, vp, i64, vp, vp, vp, vp]),
     "vdxs_sample_noalloc": (i32, [P(VdxsConfig), i32, vp, i32, i32, i32, i64, vp, i64, vp, vp, vp, vp]),
+    "vdxs_noalloc_status": (i32, [vp]),
     "vdxs_device_uniforms": (i32, [vp, i32, vp, vp]),
     "vdxs_device_history_push": (i32, [vp, vp, vp, i32, vp, i32, vp, i32, vp, vp]),
     "vdxs_decode_step": (i32, [vp, P(VdxsConfig), vp, i32, i32, i32, i64, vp, vp, vp, vp, vp, vp, i32, vp, vp, vp]),

@@ -159,6 +159,22 @@ int32_t device_word_status(vdxs_context* ctx, int32_t word, cudaStream_t stream)
                                           "call are not valid", word);
 }
 
+// The allocation-free entry points pick the scratch array of the current device, so a
+// stream created on another device would mix devices: refuse it with a clear error.
+// The legacy and per-thread default streams follow the current device.
+int32_t check_stream_device(cudaStream_t st) {
+    if (st == nullptr || st == cudaStreamLegacy || st == cudaStreamPerThread) return VDXS_OK;
+    int cur = 0, sdev = 0;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDevice");
+    if ((e = cudaStreamGetDevice(st, &sdev)) != cudaSuccess) return cuda_fail(nullptr, e, "cudaStreamGetDevice");
+    if (sdev != cur)
+        return fail(nullptr, VDXS_E_INVALID_ARG,
+                    "the stream belongs to device %d but device %d is current; make the stream's device current", sdev,
+                    cur);
+    return VDXS_OK;
+}
+
 // Fills the diagnostics part of SampleArgs from the context.
 void attach_diagnostics(vdxs_context* ctx, SampleArgs* a) {
     a->ev_begin = ctx->ev_begin;
@@ -476,6 +492,7 @@ VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, c
     int optin = 0;
     cudaError_t e = noalloc_scratch(&scratch, &optin);
     if (e != cudaSuccess) return cuda_fail(nullptr, e, "scratch address lookup");
+    if ((rc = check_stream_device(a.stream)) != VDXS_OK) return rc;
     LaunchPlan plan;
     std::string msg;
     e = a.path == kFull ? plan_full(a, &plan, &msg) : plan_topk(a, optin, &plan, &msg);
@@ -495,6 +512,33 @@ VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, c
     if ((e = launch_sample(a, plan, ws, &msg)) != cudaSuccess) return cuda_fail(nullptr, e, "kernel launch");
     ok(nullptr);
     return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_noalloc_status(void* stream) {
+    void* scratch = nullptr;
+    int optin = 0;
+    cudaError_t e = noalloc_scratch(&scratch, &optin);
+    if (e != cudaSuccess) return cuda_fail(nullptr, e, "scratch address lookup");
+    const cudaStream_t st = (cudaStream_t)stream;
+    int32_t rc = check_stream_device(st);
+    if (rc != VDXS_OK) return rc;
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) return cuda_fail(nullptr, e, "stream synchronize");
+    // The error word is the first field carved out of the array (carve_workspace), so it
+    // sits at offset 0 whatever the last call's shapes were. A synchronous copy into a
+    // host variable: no device allocation.
+    int32_t word = 0;
+    if ((e = cudaMemcpy(&word, (const unsigned char*)scratch + kNoAllocErrOffset, sizeof(int32_t),
+                        cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(nullptr, e, "error word download");
+    if (word == 0) {
+        ok(nullptr);
+        return VDXS_OK;
+    }
+    if (word == 3)
+        return fail(nullptr, VDXS_E_TIMEOUT, "a bounded device wait gave up in the last allocation-free call; "
+                                             "its tokens are not valid");
+    return fail(nullptr, VDXS_E_DEVICE_STATE, "device selection check failed (code %d) in the last allocation-free "
+                                              "call; its tokens are not valid", word);
 }
 
 VDXS_API int32_t vdxs_device_status(vdxs_context* ctx, void* stream) {

@@ -131,6 +131,8 @@ cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream);
 
 // Fixed device scratch used by vdxs_sample_noalloc (no allocation on any call).
 constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+// Byte offset of the device error word inside that array (the first field carved).
+constexpr size_t kNoAllocErrOffset = 0;
 // Device address of the scratch on the current device (resolved once per device) and
 // that device's opt-in shared-memory limit.
 cudaError_t noalloc_scratch(void** ptr, int* smem_optin);

@@ -35,6 +35,7 @@
 #include <climits>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -53,8 +54,8 @@ enum ErrCode : int32_t { kErrNone = 0, kErrSelect = 1, kErrFaithful = 2, kErrTim
 // Phase timing for development builds (-DVDXS_TIMING): thread 0 of each CTA adds the
 // cycles of each phase to a per-phase total. Compiled out of the library otherwise.
 #ifdef VDXS_TIMING
-__device__ unsigned long long g_phase_cycles[32];
-__device__ unsigned long long g_phase_count[32];
+__device__ unsigned long long g_phase_cycles[64];
+__device__ unsigned long long g_phase_count[64];
 #define VDXS_T0(v) long long v = clock64()
 #define VDXS_T1(id, v)                                                          \
     do {                                                                        \
@@ -63,7 +64,12 @@ __device__ unsigned long long g_phase_count[32];
             atomicAdd(&g_phase_count[id], 1ull);                                \
         }                                                                       \
     } while (0)
+// Adds v to counter id from the calling thread (call from one lane per warp).
+#define VDXS_ADD(id, v) atomicAdd(&g_phase_cycles[id], (unsigned long long)(v))
 #else
+#define VDXS_ADD(id, v) \
+    do {                \
+    } while (0)
 #define VDXS_T0(v) \
     do {           \
     } while (0)
@@ -121,6 +127,7 @@ struct KParams {
     int64_t vocab_offset;
     int local_emit;
     uint2* emit_out;  // [B][K+1]
+    int pf;           // stream stage 1: slots prefetched into L2 ahead of each warp's ring
 };
 
 // ---------------------------------------------------------------------------------
@@ -223,6 +230,10 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
+}
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned source) into L2 only.
+__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
@@ -2863,6 +2874,522 @@ __device__ __forceinline__ float nan_bits<float>() { return __uint_as_float(0x7F
 template <>
 __device__ __forceinline__ uint16_t nan_bits<uint16_t>() { return (uint16_t)0x7FC0u; }
 
+// ---------------------------------------------------------------------------------
+// Stream stage 1 (topk_stream_kernel): every top_k of the top-k path, and greedy.
+//
+// One persistent CTA of 16 warps per SM. The rows are cut into 4 KB slots (1024 fp32
+// or 2048 bf16 elements), and the B x slots-per-row slots are split evenly over the
+// grid (flat partition); a CTA's run of slots falls into pieces, maximal runs within one
+// row, and each piece is split evenly over the 16 warps. Each warp streams its slots
+// through its own two-slot ring of bulk copies. Lane l owns the slot's l-th 128-byte
+// group; it reads it as eight 16-byte chunks in a rotated order (conflict-free), and the
+// slot is refilled as soon as the warp holds it in registers. A lane keeps the maxima of
+// its eight chunks, so one compare of the lane maximum decides the whole group, and only
+// chunks whose maximum reaches the threshold are tested element by element.
+//
+// Threshold: one key histogram per CTA (top 12 key bits, plus 64 group counts). Every
+// count is of a distinct element of the piece's row, so the highest bin edge with at
+// least K counts at or above it is a lower bound on the row's K-th key. At the start of
+// a piece every warp counts the maximum (for top_k > 256 the eight chunk maxima) of each
+// lane of its first slot, before anything is filtered; later candidates are counted as
+// they are taken (not those in the threshold's own bin, which cannot raise it). The
+// bound is raised as counts grow and shared per CTA (shared memory) and per row
+// (row_tau, so that every CTA of a row filters against the best bound found).
+//
+// Output: every element of the piece at or above the piece's final bound is in the
+// piece's list (count in chunk_info.x; a count above cand_cap marks the list incomplete
+// and sends the row to the finish kernel's exact fallback). Candidates wait in a
+// per-warp shared region and leave at the piece's end (or when the region fills) if
+// they still reach the bound.
+// ---------------------------------------------------------------------------------
+constexpr int kS1Threads = 512;
+constexpr int kS1Warps = kS1Threads / 32;
+constexpr int kS1SlotBytes = 4096;                    // one bulk copy; a 128-byte group per lane
+constexpr int kS1Ring = 2;                            // ring slots per warp
+constexpr int kS1WCap = 128;                          // region entries per warp
+constexpr int kS1Prefetch = 4;                        // slots prefetched into L2 ahead of the ring
+constexpr int kS1CoopLanes = 8;                       // up to this many hot lanes: warp-cooperative test
+constexpr int kS1HeadWords = 64 + kTBins + kTGroups;  // scalars, key histogram, group counts
+constexpr int kS1WarpBytes = kS1Ring * kS1SlotBytes + 128 + 8 * kS1WCap;
+static_assert((4 * kS1HeadWords) % 128 == 0 && kS1WarpBytes % 128 == 0, "128-byte aligned warp areas");
+
+__host__ __device__ constexpr size_t s1_smem_bytes() {
+    return (size_t)4 * kS1HeadWords + (size_t)kS1Warps * kS1WarpBytes;
+}
+template <typename T>
+__host__ __device__ constexpr int s1_slot_elems() { return kS1SlotBytes / (int)sizeof(T); }
+
+__device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {  // packed bf16 max (NaN ignored)
+    uint32_t d;
+    asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// Element e of a 16-byte chunk (4 fp32 or 8 bf16 values; e is a compile-time constant).
+template <typename T>
+__device__ __forceinline__ float chunk_elem(const uint4& v, int e) {
+    if constexpr (sizeof(T) == 4) {
+        return __uint_as_float(e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w);
+    } else {
+        const uint32_t w = (e >> 1) == 0 ? v.x : (e >> 1) == 1 ? v.y : (e >> 1) == 2 ? v.z : v.w;
+        return (e & 1) ? bf_hi(w) : bf_lo(w);
+    }
+}
+template <typename T>
+__device__ __forceinline__ float chunk_max(const uint4& v) {
+    if constexpr (sizeof(T) == 4) {
+        return fmaxf(fmax3f(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z)), __uint_as_float(v.w));
+    } else {
+        const uint32_t m = bmax2(bmax2(v.x, v.y), bmax2(v.z, v.w));
+        return fmaxf(bf_lo(m), bf_hi(m));
+    }
+}
+
+
+// Development counters of topk_stream_kernel (-DVDXS_TIMING builds only): each warp sums
+// its phase cycles and event counts in registers and adds them once at the end
+// (g_phase_cycles[40 + i]), so the counting barely perturbs the kernel.
+#ifdef VDXS_TIMING
+#define S1_DBG_DECL unsigned long long s1dbg[16] = {0}
+#define S1_ADD(i, v) (s1dbg[i] += (unsigned long long)(v))
+#define S1_T0(v) long long v = clock64()
+#define S1_T1(i, v) (s1dbg[i] += (unsigned long long)(clock64() - v))
+#define S1_FLUSH()                                                               \
+    do {                                                                         \
+        if ((threadIdx.x & 31) == 0)                                             \
+            for (int i_ = 0; i_ < 16; ++i_) atomicAdd(&g_phase_cycles[40 + i_], s1dbg[i_]); \
+    } while (0)
+#else
+#define S1_DBG_DECL \
+    do {            \
+    } while (0)
+#define S1_ADD(i, v) \
+    do {             \
+    } while (0)
+#define S1_T0(v) \
+    do {         \
+    } while (0)
+#define S1_T1(i, v) \
+    do {            \
+    } while (0)
+#define S1_FLUSH() \
+    do {           \
+    } while (0)
+#endif
+
+template <typename T, bool TMA>
+__global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    S1_DBG_DECL;
+    S1_T0(t_all);
+    uint32_t* sh = (uint32_t*)smem_raw;
+    uint32_t* H = sh + 64;
+    uint32_t* Gc = H + kTBins;
+    constexpr int SE = s1_slot_elems<T>();  // elements per slot
+    constexpr int GE = SE / 32;             // elements per lane group
+    constexpr int CE = GE / 8;              // elements per 16-byte chunk
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int sw = lane & 7;
+    const int K = p.K;
+    unsigned char* wa = smem_raw + 4 * kS1HeadWords + (size_t)warp * kS1WarpBytes;
+    unsigned char* ring = wa;
+    uint64_t* full = (uint64_t*)(wa + kS1Ring * kS1SlotBytes);
+    uint32_t* rkey = (uint32_t*)(wa + kS1Ring * kS1SlotBytes + 128);
+    uint32_t* ridx = rkey + kS1WCap;
+    volatile uint32_t* s_T = sh;  // CTA threshold key of the current piece
+    uint32_t* s_cnt = sh + 1;     // entries reserved in the current piece's list
+    const int ng = p.flat_ng;
+    const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
+    const long long g_end = flat_start(p.flat_ngt, gridDim.x, blockIdx.x + 1);
+    const int b_first = (int)(g_begin / ng);
+    const int npieces = g_end > g_begin ? (int)((g_end - 1) / ng) - b_first + 1 : 0;
+    // This warp's slots [q0, q1) of piece j (slot indices within row b_first + j).
+    auto warp_slots = [&](int j, int& q0, int& q1) {
+        const long long rb = (long long)(b_first + j) * ng;
+        const long long glo = max(g_begin, rb) - rb, ghi = min(g_end, rb + ng) - rb;
+        q0 = (int)(glo + (ghi - glo) * warp / kS1Warps);
+        q1 = (int)(glo + (ghi - glo) * (warp + 1) / kS1Warps);
+    };
+    for (int i = tid; i < kTBins + kTGroups; i += kS1Threads) H[i] = 0u;
+    if (tid == 0) {
+        sh[0] = 0u;
+        sh[1] = 0u;
+    }
+    __syncthreads();
+
+    // Producer cursors (lane 0): this warp's slots of its pieces, in consumption order.
+    // The copy cursor fills the ring; the prefetch cursor runs p.pf slots ahead of it and
+    // only asks for the bytes to be brought into L2, so more of the stream is in flight
+    // than the shared-memory ring holds.
+    struct Cursor {
+        int pj = -1, pq = 0, pq_end = 0;
+    };
+    auto advance = [&](Cursor& c) -> bool {  // moves c to its next slot; false when done
+        while (c.pq >= c.pq_end) {
+            if (++c.pj >= npieces) return false;
+            warp_slots(c.pj, c.pq, c.pq_end);
+        }
+        return true;
+    };
+    auto slot_bytes = [&](const Cursor& c) -> uint32_t {  // the slot's bytes, rounded down to 16
+        const int n = (int)min((int64_t)SE, (int64_t)p.V - (int64_t)c.pq * SE);
+        return ((uint32_t)n * (uint32_t)sizeof(T)) & ~15u;
+    };
+    auto slot_src = [&](const Cursor& c) -> const T* {
+        return (const T*)p.logits + (int64_t)(b_first + c.pj) * p.stride + (int64_t)c.pq * SE;
+    };
+    Cursor cc_copy, cc_pf;
+    uint32_t pn = 0;
+    auto prefetch_next = [&]() {
+        if (!advance(cc_pf)) return;
+        const uint32_t bytes = slot_bytes(cc_pf);
+        if (bytes) l2_prefetch_bulk(slot_src(cc_pf), bytes);
+        ++cc_pf.pq;
+    };
+    auto issue = [&]() {
+        if (!advance(cc_copy)) return;
+        const int s = (int)(pn % kS1Ring);
+        const uint32_t bytes = slot_bytes(cc_copy);
+        if (bytes) {
+            mbar_arrive_expect_tx(&full[s], bytes);
+            tma_load_1d(ring + s * kS1SlotBytes, slot_src(cc_copy), bytes, &full[s]);
+        } else {
+            mbar_arrive(&full[s]);
+        }
+        ++pn;
+        ++cc_copy.pq;
+    };
+    if constexpr (TMA) {
+        if (lane == 0) {
+            for (int s = 0; s < kS1Ring; ++s) mbar_init(&full[s], 1);
+            fence_mbar_init();
+            // The prefetch cursor starts p.pf slots past the ring's first fill.
+            for (int s = 0; s < kS1Ring; ++s) {
+                if (!advance(cc_pf)) break;
+                ++cc_pf.pq;
+            }
+            for (int s = 0; s < p.pf; ++s) prefetch_next();
+            for (int s = 0; s < kS1Ring; ++s) issue();
+        }
+        __syncwarp();
+    }
+    // With a history, this kernel is a programmatic dependent of the penalty prep: the
+    // first slots are in flight; the penalty lists are read only after this wait.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+
+    uint32_t cn = 0;  // slots consumed by this warp (ring position and phase)
+    bool timed_out = false;
+    for (int j = 0; j < npieces; ++j) {
+        const int b = b_first + j;
+        const T* row = (const T*)p.logits + (int64_t)b * p.stride;
+        const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+        const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+        int q0, q1;
+        warp_slots(j, q0, q1);
+        int pjp = npen > 0 ? lower_bound_i32(pid, npen, (int64_t)q0 * SE) : 0;
+        uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
+        uint32_t rtau = ld_relaxed_u32(rtp);
+        uint32_t rtau_next = rtau;
+        uint32_t wcnt = 0u, since = 0u;
+        const int item = (int)blockIdx.x * p.flat_pmax + j;
+        uint2* out = p.cand + (size_t)item * p.cand_cap;
+        const uint32_t cap = (uint32_t)p.cand_cap;
+        const uint32_t gbase0 = (uint32_t)p.vocab_offset;
+
+        // Slot q of the row: waits for its bulk copy (or copies it with plain loads), fills
+        // the row tail, masks the penalised ids, and loads the lane's group into registers.
+        // The slot stays staged until release().
+        auto stage = [&](int q, uint4 (&v)[8]) -> const unsigned char* {
+            S1_T0(t_st);
+            const int64_t start = (int64_t)q * SE;
+            const int n = (int)min((int64_t)SE, (int64_t)p.V - start);
+            unsigned char* slotp = ring + (cn % kS1Ring) * kS1SlotBytes;
+            T* sl = (T*)slotp;
+            if constexpr (TMA) {
+                if (!mbar_wait_bounded(&full[cn % kS1Ring], (cn / kS1Ring) & 1u)) timed_out = true;
+                const int n_tma = (int)((((uint32_t)n * (uint32_t)sizeof(T)) & ~15u) / sizeof(T));
+                // Row tail: the elements past the copy's 16-byte multiple are read directly;
+                // positions past the row hold NaN (no element).
+                for (int i = n_tma + lane; i < SE; i += 32) sl[i] = i < n ? row[start + i] : nan_bits<T>();
+            } else {
+                for (int i = lane; i < SE; i += 32) sl[i] = i < n ? row[start + i] : nan_bits<T>();
+            }
+            if (npen > 0) {
+                // Penalised ids leave stage 1 (they re-enter with their penalised values in
+                // the finish kernel).
+                for (;;) {
+                    const int jj = pjp + lane;
+                    const bool in = jj < npen && pid[jj] < start + n;
+                    if (in) sl[pid[jj] - start] = nan_bits<T>();
+                    const unsigned m = __ballot_sync(FULL, in);
+                    pjp += __popc(m);
+                    if (m != FULL) break;
+                }
+            }
+            __syncwarp();
+            const unsigned char* g = slotp + lane * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(g + ((c ^ sw) << 4));
+            S1_T1(0, t_st);
+            return slotp;
+        };
+        // Hands the staged slot back to the producer: its next bulk copy (and the L2
+        // prefetch further ahead) are issued behind the warp's reads of it.
+        auto release = [&]() {
+            __syncwarp();
+            if constexpr (TMA) {
+                if (lane == 0) {
+                    fence_proxy_async_smem();
+                    issue();
+                    prefetch_next();
+                }
+            }
+            ++cn;
+        };
+        // Writes the region entries at or above tmin to the piece's list; empties the region.
+        auto flush_region = [&](uint32_t tmin) {
+            S1_ADD(10, 1);
+            for (uint32_t i0 = 0; i0 < wcnt; i0 += 32) {
+                const uint32_t i = i0 + lane;
+                uint32_t k = 0u, ix = 0u;
+                bool keep = false;
+                if (i < wcnt) {
+                    k = rkey[i];
+                    ix = ridx[i];
+                    keep = k >= tmin;
+                }
+                const unsigned m = __ballot_sync(FULL, keep);
+                if (m) {
+                    uint32_t base = 0u;
+                    if (lane == 0) base = atomicAdd(s_cnt, (uint32_t)__popc(m));
+                    base = __shfl_sync(FULL, base, 0);
+                    const uint32_t pos = base + __popc(m & lanemask_lt());
+                    if (keep && pos < cap) out[pos] = make_uint2(k, ix);
+                }
+            }
+            __syncwarp();
+            wcnt = 0u;
+        };
+        auto raise = [&]() {
+            __syncwarp();
+            S1_ADD(9, 1);
+            const uint32_t t = hist_threshold(H, Gc, K);
+            if (lane == 0 && t > *s_T) {
+                atomicMax((uint32_t*)s_T, t);
+                if (t > rtau) atomicMax(rtp, t);
+            }
+        };
+        // Appends one candidate (key k, index ix) at region position pos and, when
+        // counting, counts it in the histogram unless it lies in the bound's own bin
+        // (such counts cannot raise the bound).
+        auto take = [&](uint32_t pos, uint32_t k, uint32_t ix, bool counting, uint32_t tbin, uint32_t& counted) {
+            rkey[pos] = k;
+            ridx[pos] = ix;
+            if (counting && (k >> 20) > tbin) {
+                atomicAdd(&H[k >> 20], 1u);
+                atomicAdd(&Gc[k >> 26], 1u);
+                ++counted;
+            }
+        };
+        // Filters one staged slot against the current bound. Few hot lanes: the warp
+        // tests each hot lane's group together, one element (fp32) or one pair (bf16) per
+        // lane, from shared memory. Many: each lane extracts its own candidates from its
+        // registers, testing only the chunks whose maximum reaches the bound.
+        auto filter = [&](const unsigned char* slotp, const uint4 (&v)[8], const float (&xq)[8], float lmax, int q,
+                          bool counting) {
+            S1_ADD(5, 1);
+            const uint32_t tg = max((uint32_t)*s_T, rtau);
+            const float thr = key_threshold(tg);
+            const bool hot = lmax >= thr;
+            unsigned hb = __ballot_sync(FULL, hot);
+            if (hb == 0u) return;
+            S1_T0(t_hot);
+            S1_ADD(6, 1);
+            S1_ADD(7, __popc(hb));
+            const uint32_t tbin = tg >> 20;
+            const uint32_t gslot = gbase0 + (uint32_t)q * SE;
+            uint32_t counted = 0u;
+            if (__popc(hb) <= kS1CoopLanes) {
+                while (hb) {
+                    const int h = __ffs((int)hb) - 1;
+                    hb &= hb - 1u;
+                    if (wcnt + 2u * 32u > (uint32_t)kS1WCap) flush_region(tg);
+                    if constexpr (sizeof(T) == 4) {
+                        const float xv = reinterpret_cast<const float*>(slotp)[h * 32 + lane];
+                        const bool pass = xv >= thr;
+                        const unsigned m = __ballot_sync(FULL, pass);
+                        if (pass)
+                            take(wcnt + __popc(m & lanemask_lt()), f2key(xv), gslot + (uint32_t)(h * 32 + lane),
+                                 counting, tbin, counted);
+                        wcnt += (uint32_t)__popc(m);
+                        S1_ADD(8, __popc(m));
+                    } else {
+                        const uint32_t w = reinterpret_cast<const uint32_t*>(slotp)[h * 32 + lane];
+                        const float a = bf_lo(w), b = bf_hi(w);
+                        const bool pa = a >= thr, pb = b >= thr;
+                        const unsigned ma = __ballot_sync(FULL, pa), mb = __ballot_sync(FULL, pb);
+                        const uint32_t pos = wcnt + __popc(ma & lanemask_lt()) + __popc(mb & lanemask_lt());
+                        const uint32_t ix = gslot + (uint32_t)(h * 64 + 2 * lane);
+                        if (pa) take(pos, f2key(a), ix, counting, tbin, counted);
+                        if (pb) take(pos + (pa ? 1u : 0u), f2key(b), ix + 1u, counting, tbin, counted);
+                        wcnt += (uint32_t)(__popc(ma) + __popc(mb));
+                        S1_ADD(8, __popc(ma) + __popc(mb));
+                    }
+                }
+            } else {
+                uint64_t pm = 0ull;  // this lane's elements at or above the bound
+                if (hot) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        if (xq[c] >= thr) {
+                            uint32_t cm = 0u;
+#pragma unroll
+                            for (int e = 0; e < CE; ++e) cm |= (chunk_elem<T>(v[c], e) >= thr ? 1u : 0u) << e;
+                            pm |= (uint64_t)cm << (c * CE);
+                        }
+                    }
+                }
+                const uint32_t cnt = (uint32_t)__popcll(pm);
+                uint32_t incl = cnt;
+#pragma unroll
+                for (int d = 1; d < 32; d <<= 1) {
+                    const uint32_t o = __shfl_up_sync(FULL, incl, d);
+                    if (lane >= d) incl += o;
+                }
+                const uint32_t total = __shfl_sync(FULL, incl, 31);
+                if (wcnt + total > (uint32_t)kS1WCap && wcnt > 0u) flush_region(tg);
+                const bool direct = total > (uint32_t)kS1WCap;  // more than a region: straight to the list
+                if (direct) S1_ADD(12, 1);
+                uint32_t pos;
+                if (direct) {
+                    uint32_t base = 0u;
+                    if (lane == 0) base = atomicAdd(s_cnt, total);
+                    pos = __shfl_sync(FULL, base, 0) + incl - cnt;
+                } else {
+                    pos = wcnt + incl - cnt;
+                }
+                const uint32_t gb = gslot + (uint32_t)lane * GE;
+                if (cnt) {
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint32_t cm = (uint32_t)(pm >> (c * CE)) & ((1u << CE) - 1u);
+                        if (cm) {
+#pragma unroll
+                            for (int e = 0; e < CE; ++e) {
+                                if ((cm >> e) & 1u) {
+                                    const uint32_t k = f2key(chunk_elem<T>(v[c], e));
+                                    const uint32_t ix = gb + (uint32_t)((c ^ sw) * CE + e);
+                                    if (direct) {
+                                        if (pos < cap) out[pos] = make_uint2(k, ix);
+                                        if (counting && (k >> 20) > tbin) {
+                                            atomicAdd(&H[k >> 20], 1u);
+                                            atomicAdd(&Gc[k >> 26], 1u);
+                                            ++counted;
+                                        }
+                                    } else {
+                                        take(pos, k, ix, counting, tbin, counted);
+                                    }
+                                    ++pos;
+                                }
+                            }
+                        }
+                    }
+                }
+                if (!direct) wcnt += total;
+                S1_ADD(8, total);
+            }
+            since += __reduce_add_sync(FULL, counted);
+            if (since >= 8u) {
+                since = 0u;
+                raise();
+            }
+            S1_T1(1, t_hot);
+        };
+        auto maxima = [&](const uint4 (&v)[8], float (&xq)[8]) -> float {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) xq[c] = chunk_max<T>(v[c]);
+            return fmaxf(fmax3f(fmax3f(xq[0], xq[1], xq[2]), fmax3f(xq[3], xq[4], xq[5]), xq[6]), xq[7]);
+        };
+
+        // Counting: each warp's first slot of the piece (already in flight) is counted
+        // before anything is filtered, so the bound starts near the K-th key of the
+        // CTA's first slots.
+        uint4 v[8];
+        float xq[8];
+        float lmax = __uint_as_float(0x7FC00000u);
+        const unsigned char* slotp = nullptr;
+        S1_T0(t_cnt);
+        if (q0 < q1) {
+            slotp = stage(q0, v);
+            lmax = maxima(v, xq);
+            if (K > 256) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    if (xq[c] == xq[c]) {
+                        const uint32_t k = f2key(xq[c]);
+                        atomicAdd(&H[k >> 20], 1u);
+                        atomicAdd(&Gc[k >> 26], 1u);
+                    }
+                }
+            } else if (lmax == lmax) {
+                const uint32_t k = f2key(lmax);
+                atomicAdd(&H[k >> 20], 1u);
+                atomicAdd(&Gc[k >> 26], 1u);
+            }
+        }
+        __syncthreads();
+        raise();
+        S1_T1(3, t_cnt);
+        if (q0 < q1) {
+            filter(slotp, v, xq, lmax, q0, false);  // its maxima are counted already
+            release();
+            for (int q = q0 + 1; q < q1; ++q) {
+                rtau = rtau_next;  // the row bound is fetched one slot ahead
+                rtau_next = ld_relaxed_u32(rtp);
+                slotp = stage(q, v);
+                lmax = maxima(v, xq);
+                filter(slotp, v, xq, lmax, q, true);
+                release();
+            }
+        }
+        // Piece end: the final bound from the complete histogram; every region entry at
+        // or above it leaves.
+        S1_T0(t_pe);
+        __syncthreads();
+        if (warp == 0) {
+            const uint32_t t = hist_threshold(H, Gc, K);
+            if (lane == 0) sh[2] = max(max((uint32_t)*s_T, t), ld_relaxed_u32(rtp));
+        }
+        __syncthreads();
+        const uint32_t tfin = sh[2];
+        flush_region(tfin);
+        __syncthreads();
+        if (tid == 0) {
+            S1_ADD(11, *s_cnt);
+            p.chunk_info[item] = make_uint2(*s_cnt, 0u);
+            p.item_tau[item] = tfin;
+            if (tfin > ld_relaxed_u32(rtp)) atomicMax(rtp, tfin);
+            sh[0] = 0u;
+            sh[1] = 0u;
+        }
+        for (int i = tid; i < kTBins + kTGroups; i += kS1Threads) H[i] = 0u;
+        __syncthreads();
+        S1_T1(2, t_pe);
+    }
+    if (__any_sync(FULL, timed_out) && lane == 0) atomicExch(p.err, kErrTimeout);
+    if constexpr (TMA) {
+        __syncwarp();
+        if (lane == 0)
+            for (int s = 0; s < kS1Ring; ++s) mbar_inval(&full[s]);
+    }
+    S1_T1(4, t_all);
+    S1_FLUSH();
+    // This CTA is done: the finish kernel may start launching (it waits for the grid).
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Warp 0 only: the highest bin g of h[0..256) with at least `need` counts in bins >= g.
 // Writes sh[0] = g (0xFFFFFFFF if the total is below need), sh[1] = count in bins > g.
 __device__ void warp_suffix_find256(const uint32_t* h, uint32_t need, uint32_t* sh) {
@@ -3500,32 +4027,31 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
             return cudaSuccess;
         }
     }
-    if (K <= kWarpMaxK) {
-        // Stream path: persistent stage 1 (two CTAs per SM) + one finish CTA per row.
-        int dev = 0, sms = 148, per_sm = 0;
+    if (K <= kMaxTopK) {
+        // Stream path: persistent stage 1 (one 16-warp CTA per SM) + one finish CTA per row.
+        int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-        const int R = K <= 32 ? 1 : (K <= 64 ? 2 : 4);
-        const int rs = esz == 4 ? net_ring_slots<float>() : net_ring_slots<uint16_t>();
-        const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(R, rs, (int)esz) + (size_t)4 * hist_area_words();
-        const int ctas_per_sm = per_sm >= 2 * (int)(align16(s1) + 1024) ? 2 : 1;
-        // Flat partition: granules of kSlice elements, evenly over at most one wave of
-        // CTAs, at least kMinGranules per CTA so small batches keep pieces worth a CTA.
-        constexpr long long kMinGranules = 16;
-        const int ng = (int)((V + kSlice - 1) / kSlice);
+        const int SE = esz == 4 ? s1_slot_elems<float>() : s1_slot_elems<uint16_t>();
+        const int ng = (int)((V + SE - 1) / SE);
         const long long ngt = (long long)a.B * ng;
-        const int grid = (int)std::max<long long>(1, std::min<long long>((long long)sms * ctas_per_sm, ngt / kMinGranules));
+        // Flat partition of the B x ng slots over at most one CTA per SM, at least one slot
+        // per warp.
+        const int grid = (int)std::max<long long>(1, std::min<long long>((long long)sms, ngt / kS1Warps));
         const long long gmax_cta = (ngt + grid - 1) / grid, gmin_cta = std::max<long long>(1, ngt / grid);
-        const int pmax = (int)((gmax_cta - 1) / ng + 2);                 // pieces per CTA
-        const int ipr = (int)((ng + gmin_cta - 1) / gmin_cta + 1);       // pieces per row
-        // Each piece writes its candidates at or above the final threshold (usually its
-        // share of the row's top-K plus the boundary bin); more than this takes an exact
-        // top-K in the piece.
-        const int cc = (int)std::max<int64_t>(K, std::min<int64_t>(4 * K, 8192 / ipr));
-        size_t s2 = std::max(stage2_bytes(K, (size_t)ipr * cc + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
+        const int pmax = (int)((gmax_cta - 1) / ng + 2);            // pieces per CTA
+        const int ipr = (int)((ng + gmin_cta - 1) / gmin_cta + 1);  // pieces per row
+        // A piece's list holds its elements at or above the piece's final bound: for small
+        // top_k about the row's share above the bound's bin edge; for large top_k also the
+        // candidates taken while the bound was still rising. A longer list is incomplete
+        // and its row takes the finish kernel's exact fallback.
+        const int cc = K <= 128 ? (int)std::max<int64_t>(std::max(256, 2 * K), std::min<int64_t>(8 * K, 16384 / ipr))
+                                : (int)std::min<int64_t>(std::max<int64_t>(16LL * K, 8192), (int64_t)ng * SE);
+        const int gather = std::max(8192, K + pen_stride);
+        size_t s2 = std::max(stage2_bytes(K, gather + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
         s2 += kHeadBytes;
-        if ((int64_t)s1 > smem_optin || (int64_t)s2 > smem_optin) {
+        const size_t s1 = s1_smem_bytes();
+        if ((int64_t)s1 > smem_optin || (int64_t)align16(s2) > smem_optin) {
             if (err) *err = "shared-memory plan exceeds the device limit";
             return cudaErrorInvalidValue;
         }
@@ -3533,61 +4059,18 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         plan->nchunks = ipr;
         plan->nspans = ipr;
         plan->span = 1;
-        plan->elems = R;
+        plan->elems = 0;
         plan->stream = true;
         plan->cand_cap = cc;
+        plan->gather_cap = gather;
         plan->grid = grid;
         plan->flat_ng = ng;
         plan->flat_ngt = ngt;
         plan->flat_pmax = pmax;
         plan->items = (long long)grid * pmax;
-        plan->smem = align16(s1);
+        plan->smem = s1;
         plan->smem2 = align16(s2);
         return cudaSuccess;
-    }
-    if (K <= kMaxTopK) {
-        // Wide stream path: the same persistent stage 1 without per-warp lists; pieces
-        // append raw candidate lists that the finish kernel gathers at the row's bound.
-        int dev = 0, sms = 148, per_sm = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
-        const int rs = esz == 4 ? net_ring_slots<float>() : net_ring_slots<uint16_t>();
-        const size_t s1 = kHeadBytes + (size_t)NWARPS * 4 * net_area_words(0, rs, (int)esz) +
-                          (size_t)4 * (kTBins + kTGroups);
-        const int ctas_per_sm = per_sm >= 2 * (int)(align16(s1) + 1024) ? 2 : 1;
-        constexpr long long kMinGranules = 16;
-        const int ng = (int)((V + kSlice - 1) / kSlice);
-        const long long ngt = (long long)a.B * ng;
-        const int grid = (int)std::max<long long>(1, std::min<long long>((long long)sms * ctas_per_sm, ngt / kMinGranules));
-        const long long gmax_cta = (ngt + grid - 1) / grid, gmin_cta = std::max<long long>(1, ngt / grid);
-        const int pmax = (int)((gmax_cta - 1) / ng + 2);
-        const int ipr = (int)((ng + gmin_cta - 1) / gmin_cta + 1);
-        // Raw list of a piece: its elements that met the running threshold (about
-        // K * (1 + ln(piece / K)) plus the boundary bin); a longer list is incomplete and
-        // the row takes the finish kernel's exact fallback.
-        const int cc = (int)std::min<int64_t>(std::max<int64_t>(16LL * K, 8192), (int64_t)ng * kSlice);
-        const int gather = std::max(8192, K + pen_stride);
-        size_t s2 = std::max(stage2_bytes(K, gather + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
-        s2 += kHeadBytes;
-        if ((int64_t)align16(s1) <= smem_optin && (int64_t)align16(s2) <= smem_optin) {
-            plan->chunk = 0;
-            plan->nchunks = ipr;
-            plan->nspans = ipr;
-            plan->span = 1;
-            plan->elems = 0;
-            plan->stream = true;
-            plan->cand_cap = cc;
-            plan->gather_cap = gather;
-            plan->grid = grid;
-            plan->flat_ng = ng;
-            plan->flat_ngt = ngt;
-            plan->flat_pmax = pmax;
-            plan->items = (long long)grid * pmax;
-            plan->smem = align16(s1);
-            plan->smem2 = align16(s2);
-            return cudaSuccess;
-        }
     }
     if (err) *err = "top_k too large for the shared-memory plan (top_k=" + std::to_string(K) + ")";
     return cudaErrorInvalidValue;
@@ -3818,6 +4301,10 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.vocab_offset = a.vocab_offset;
     p.local_emit = a.local_emit ? 1 : 0;
     p.emit_out = ws.shard_send;
+    p.pf = kS1Prefetch;
+#ifdef VDXS_TIMING
+    if (const char* e = getenv("VDXS_PF")) p.pf = atoi(e);
+#endif
     return p;
 }
 
@@ -3885,14 +4372,7 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         return mark(a, a.ev_end);
     }
     if (plan.stream) {
-        void (*k1)(KParams) = nullptr;
-        const int R = plan.elems;
-#define VDXS_HIST(R_) k1 = vec ? topk_hist_kernel<T, true, R_> : topk_hist_kernel<T, false, R_>
-        if (R == 0) k1 = vec ? topk_wide_kernel<T, true> : topk_wide_kernel<T, false>;
-        else if (R == 1) VDXS_HIST(1);
-        else if (R == 2) VDXS_HIST(2);
-        else VDXS_HIST(4);
-#undef VDXS_HIST
+        void (*k1)(KParams) = vec ? topk_stream_kernel<T, true> : topk_stream_kernel<T, false>;
         if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem)) != cudaSuccess)
             return e;
         if ((e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -3904,7 +4384,7 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
             // tail; the kernel waits for the prep grid before it reads the lists.
             cudaLaunchConfig_t lc1 = {};
             lc1.gridDim = dim3(plan.grid);
-            lc1.blockDim = dim3(NT);
+            lc1.blockDim = dim3(kS1Threads);
             lc1.dynamicSmemBytes = plan.smem;
             lc1.stream = a.stream;
             cudaLaunchAttribute at1[1];
@@ -3914,7 +4394,7 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
             lc1.numAttrs = 1;
             if ((e = cudaLaunchKernelEx(&lc1, k1, p)) != cudaSuccess) return e;
         } else {
-            k1<<<plan.grid, NT, plan.smem, a.stream>>>(p);
+            k1<<<plan.grid, kS1Threads, plan.smem, a.stream>>>(p);
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         if ((e = mark(a, a.ev_end)) != cudaSuccess) return e;
@@ -4040,10 +4520,10 @@ extern "C" __attribute__((visibility("default"))) int vdxs_debug_network_selftes
 extern "C" __attribute__((visibility("default"))) int vdxs_debug_phase_times(unsigned long long* cycles,
                                                                                 unsigned long long* counts,
                                                                                 int reset) {
-    cudaMemcpyFromSymbol(cycles, vdxs::g_phase_cycles, sizeof(unsigned long long) * 32);
-    cudaMemcpyFromSymbol(counts, vdxs::g_phase_count, sizeof(unsigned long long) * 32);
+    cudaMemcpyFromSymbol(cycles, vdxs::g_phase_cycles, sizeof(unsigned long long) * 64);
+    cudaMemcpyFromSymbol(counts, vdxs::g_phase_count, sizeof(unsigned long long) * 64);
     if (reset) {
-        unsigned long long z[32] = {0};
+        unsigned long long z[64] = {0};
         cudaMemcpyToSymbol(vdxs::g_phase_cycles, z, sizeof(z));
         cudaMemcpyToSymbol(vdxs::g_phase_count, z, sizeof(z));
     }
