@@ -170,7 +170,7 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg,
  * workspace lazily, Sampler.pas:250-263).
  *
  * Runs on the calling thread's current CUDA device and takes no context: its
- * workspace is a fixed 4 MiB device array built into the library, which every GPU
+ * workspace is a fixed 32 MiB device array built into the library, which every GPU
  * that loads the library holds until the process exits. Calls whose workspace would
  * exceed it return VDXS_E_UNSUPPORTED (batch 512 at vocab 262144 with top_k 64 fits;
  * batch 1024 with top_k 1024 does not). The call never allocates: no cudaMalloc,

@@ -505,10 +505,7 @@ VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, c
                     "(use vdxs_sample with a context)",
                     need, kNoAllocScratchBytes);
     // The array keeps the previous call's contents: reset what must start at zero.
-    if ((e = cudaMemsetAsync(ws.err, 0, sizeof(int32_t), a.stream)) != cudaSuccess ||
-        (e = cudaMemsetAsync(ws.row_counter, 0, sizeof(uint32_t) * batch, a.stream)) != cudaSuccess ||
-        (e = cudaMemsetAsync(ws.row_tau, 0, sizeof(uint32_t) * kTauStride * batch, a.stream)) != cudaSuccess)
-        return cuda_fail(nullptr, e, "scratch reset");
+    if ((e = reset_device_state(ws, a.stream)) != cudaSuccess) return cuda_fail(nullptr, e, "scratch reset");
     if ((e = launch_sample(a, plan, ws, &msg)) != cudaSuccess) return cuda_fail(nullptr, e, "kernel launch");
     ok(nullptr);
     return VDXS_OK;

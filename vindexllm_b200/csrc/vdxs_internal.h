@@ -21,12 +21,13 @@ enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
 // Device workspace owned by a context (TVdxSampler.EnsureWorkspace analogue,
 // Sampler.pas:250-263). Grown on demand; never shrunk until the context dies.
 struct Workspace {
-    uint2* cand = nullptr;          // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
+    uint2* cand = nullptr;          // stage-1 (key, index) candidates: [rows * cand_cap] (stream path)
     size_t cand_cap = 0;            // elements
-    uint2* chunk_info = nullptr;    // [items] (candidate count, largest key cut by an exact decision)
-    size_t chunk_info_cap = 0;
-    uint32_t* item_tau = nullptr;   // [items] each item's lower bound on its row's K-th key
-    size_t item_tau_cap = 0;
+    uint32_t* rhist = nullptr;      // [rows * kRowHistWords] stream path key histograms, self-resetting
+    size_t rhist_cap = 0;
+    uint32_t* row_cnt = nullptr;    // [rows] stream path list counts, self-resetting
+    size_t row_cnt_cap = 0;
+    unsigned long long* unit_next = nullptr;  // [2] stream path slot claims and finished warps, self-resetting
     uint32_t* row_counter = nullptr;  // [rows] completion counters, self-resetting
     size_t row_counter_cap = 0;
     uint32_t* row_tau = nullptr;      // [rows * kTauStride] stream path K-th key bounds, self-resetting
@@ -101,12 +102,11 @@ struct LaunchPlan {
     bool cluster = false; // top-k path, small batches: one thread-block cluster per row
     int cluster_ctas = 8; // CTAs per cluster
     int grid = 0;         // stream kernel grid (CTAs)
-    int cand_cap = 0;     // top-k path: candidates each stage-1 item may write
-    int gather_cap = 0;   // wide stream path: finish kernel gather capacity (0 = other paths)
-    long long items = 0;  // top-k path: stage-1 item slots (candidate lists)
-    int flat_ng = 0;      // stream path: granules per row of the flat partition (0 = spans)
-    int flat_pmax = 0;    // stream path: pieces per CTA
-    long long flat_ngt = 0;
+    int cand_cap = 0;     // top-k path: candidates each stage-1 list may hold (stream path: per row)
+    int gather_cap = 0;   // stream path: finish kernel gather capacity
+    long long items = 0;  // top-k path: stage-1 candidate lists
+    int slots = 0;        // stream path: 4 KB slots per row
+    int unit_slots = 0;   // stream path: slots per claimed unit
     size_t smem = 0;
     size_t smem2 = 0;     // finish kernel shared memory
 };
@@ -130,7 +130,7 @@ void free_workspace(Workspace& ws);
 cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream);
 
 // Fixed device scratch used by vdxs_sample_noalloc (no allocation on any call).
-constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+constexpr size_t kNoAllocScratchBytes = (size_t)32 << 20;
 // Byte offset of the device error word inside that array (the first field carved).
 constexpr size_t kNoAllocErrOffset = 0;
 // Device address of the scratch on the current device (resolved once per device) and

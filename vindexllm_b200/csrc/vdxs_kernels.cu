@@ -94,18 +94,15 @@ struct KParams {
     const int32_t* pen_cnt;
     int pen_stride;
     // workspace
-    uint2* cand;        // [rows * nchunks * cand_cap] stage-1 (key, index) candidates
-    int cand_cap;       // candidates each stage-1 item may write
-    int gather_cap;     // finish kernel: fixed gather capacity (0 = nsp * cand_cap)
-    uint2* chunk_info;  // [items] (candidate count, largest key dropped by an exact cut)
-    uint32_t* item_tau; // [items] the item's lower bound on its row's K-th key (0 = none)
-    // Flat partition of the stream path (flat_ng > 0): the B x ng granules of kSlice
-    // elements are split evenly over flat_grid CTAs; CTA c writes its pieces (maximal
-    // runs within one row) to items c * flat_pmax + j.
+    uint2* cand;        // stage-1 (key, index) candidates (stream path: [B][cand_cap], one list per row)
+    int cand_cap;       // candidates a list may hold
+    int gather_cap;     // finish kernel: fixed gather capacity
+    // Stream path: rows of flat_ng 4 KB slots, claimed in units of unit_slots slots.
     int flat_ng;
-    int flat_grid;
-    int flat_pmax;
-    long long flat_ngt;
+    int unit_slots;
+    uint32_t* rhist;      // [B][kRowHistWords] per-row key histograms (reset by finish)
+    uint32_t* row_cnt;    // [B] list counts (reset by finish)
+    unsigned long long* unit_next;  // [2] slot claims and finished warps (reset by the last warp)
     uint32_t* row_counter;
     uint32_t* row_tau;  // stream path: per-row lower bound on the K-th key (reset by finish)
     int32_t* err;
@@ -127,20 +124,11 @@ struct KParams {
     int64_t vocab_offset;
     int local_emit;
     uint2* emit_out;  // [B][K+1]
-    int pf;           // stream stage 1: slots prefetched into L2 ahead of each warp's ring
 };
 
 // ---------------------------------------------------------------------------------
 // Keys and loads
 // ---------------------------------------------------------------------------------
-// First granule of CTA c in the flat partition, and the CTA that holds granule g.
-__host__ __device__ __forceinline__ long long flat_start(long long ngt, int grid, int c) {
-    return (long long)c * ngt / grid;
-}
-__host__ __device__ __forceinline__ int flat_owner(long long ngt, int grid, long long g) {
-    return (int)(((g + 1) * (long long)grid - 1) / ngt);
-}
-
 __device__ __forceinline__ uint32_t f2key(float f) {
     uint32_t u = __float_as_uint(f);
     if (u == 0x80000000u) u = 0u;  // -0.0 compares equal to +0.0
@@ -231,10 +219,6 @@ __device__ __forceinline__ void tma_load_1d(void* dst, const void* src, uint32_t
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
 }
-// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned source) into L2 only.
-__device__ __forceinline__ void l2_prefetch_bulk(const void* src, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -253,6 +237,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const unsigned long long* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ uint64_t global_ns() {
@@ -1479,31 +1468,19 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     uint32_t* sk = (uint32_t*)region;
     uint32_t* si = sk + K;
     uint32_t* ckey = si + K;
-    // Stage-1 items of this row: the pieces of the CTAs that own the row's granules in
-    // the flat partition.
-    const long long g0 = (long long)b * p.flat_ng;
-    const int c_lo = flat_owner(p.flat_ngt, p.flat_grid, g0);
-    const int nsp = flat_owner(p.flat_ngt, p.flat_grid, g0 + p.flat_ng - 1) - c_lo + 1;
-    auto item_of = [&](int i) -> int64_t {
-        const int c = c_lo + i;
-        const int jj = b - (int)(flat_start(p.flat_ngt, p.flat_grid, c) / p.flat_ng);
-        return (int64_t)c * p.flat_pmax + jj;
-    };
-    const int cc = p.cand_cap;
-    // Every item's bound is a lower bound on the row's K-th key, so is their maximum:
-    // candidates and penalised entries below it can be neither selected nor tied at the
-    // boundary, and are not gathered.
-    uint32_t tb = 0u;
-    for (int i = tid; i < nsp; i += NT) tb = max(tb, __ldcg(&p.item_tau[item_of(i)]));
-    tb = block_max_u32(tb, sh + 32);
-    // Capacity of the gathered arrays. The wide stream path gathers into a fixed
-    // capacity; an incomplete item list (count > cand_cap) or a gather that does not fit
-    // sends the row to the exact fallback below.
-    const bool wide = p.gather_cap > 0;
-    const int gcap = wide ? p.gather_cap + npen : nsp * cc + npen;
+    const uint32_t cc = (uint32_t)p.cand_cap;
+    // The row's bound: the largest bound any stage-1 warp published, a lower bound on the
+    // row's K-th key; the row's list holds every element at or above it. Candidates and
+    // penalised entries below it can be neither selected nor tied at the boundary, and
+    // are not gathered.
+    const uint32_t tb = __ldcg(&p.row_tau[(size_t)b * kTauStride]);
+    const uint32_t craw = __ldcg(&p.row_cnt[b]);
+    // A list that outgrew its capacity (count > cand_cap) is incomplete, and a gather that
+    // does not fit the shared arrays: both send the row to the exact fallback below.
+    const bool incomplete = craw > cc;
+    const int gcap = p.gather_cap + npen;
     uint32_t* cidx = ckey + gcap;
     uint32_t lm = 0u;
-    bool incomplete = false;
     VDXS_T0(t_gather);
     {
         const int lane = tid & 31;
@@ -1524,37 +1501,19 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
                 lm = max(lm, k);
             }
         };
-        if (wide) {
-            // Long raw lists: the whole CTA walks each list, four loads in flight per thread.
-            for (int it = 0; it < nsp; ++it) {
-                const int64_t ii = item_of(it);
-                const uint32_t craw = __ldcg(&p.chunk_info[ii].x);
-                incomplete |= craw > (uint32_t)cc;
-                const int c = (int)min(craw, (uint32_t)cc);
-                const uint2* src = p.cand + ii * cc;
-                for (int j0 = 0; j0 < c; j0 += 4 * NT) {
-                    uint2 e[4];
+        if (!incomplete) {
+            // The whole CTA walks the list, four loads in flight per thread.
+            const int c = (int)craw;
+            const uint2* src = p.cand + (size_t)b * cc;
+            for (int j0 = 0; j0 < c; j0 += 4 * NT) {
+                uint2 e[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int j = j0 + u * NT + tid;
-                        e[u] = j < c ? __ldcg(src + j) : make_uint2(0u, 0u);
-                    }
+                for (int u = 0; u < 4; ++u) {
+                    const int j = j0 + u * NT + tid;
+                    e[u] = j < c ? __ldcg(src + j) : make_uint2(0u, 0u);
+                }
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) put(j0 + u * NT + tid < c && e[u].x >= tb, e[u].x, e[u].y);
-                }
-            }
-        } else {
-            // Short lists: warp w takes items w, w+8, ...
-            for (int it = tid >> 5; it < nsp; it += NWARPS) {
-                const int64_t ii = item_of(it);
-                const int c = (int)min(__ldcg(&p.chunk_info[ii].x), (uint32_t)cc);
-                const uint2* src = p.cand + ii * cc;
-                for (int j0 = 0; j0 < c; j0 += 32) {
-                    const int j = j0 + lane;
-                    uint2 e = make_uint2(0u, 0u);
-                    if (j < c) e = __ldcg(src + j);
-                    put(j < c && e.x >= tb, e.x, e.y);
-                }
+                for (int u = 0; u < 4; ++u) put(j0 + u * NT + tid < c && e[u].x >= tb, e[u].x, e[u].y);
             }
         }
         for (int j0 = 0; j0 < npen; j0 += NT) {
@@ -1567,7 +1526,7 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     }
     VDXS_T1(29, t_gather);
     const int n2 = (int)sh[40];
-    if (__syncthreads_or(incomplete) || n2 > gcap) {
+    if (incomplete || n2 > gcap) {
 #ifdef VDXS_TIMING
         if (tid == 0) atomicAdd(&g_phase_count[30], 1ull);
 #endif
@@ -1575,8 +1534,7 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
         return;
     }
     const uint32_t gmax = block_max_u32(lm, sh + 32);
-    finish_select<T>(p, b, ckey, cidx, n2, gmax, nsp,
-                     [&](int i) -> uint32_t { return __ldcg(&p.chunk_info[item_of(i)].y); }, region, hist, sh);
+    finish_select<T>(p, b, ckey, cidx, n2, gmax, 0, [&](int) -> uint32_t { return 0u; }, region, hist, sh);
 }
 
 // ---------------------------------------------------------------------------------
@@ -1910,48 +1868,6 @@ __device__ __forceinline__ int warp_compact_selected(uint32_t* k, uint32_t* t, i
 }
 
 // ---------------------------------------------------------------------------------
-// Stream stage 1 (topk_hist_kernel) serves top_k <= kWarpMaxK. Each warp streams its
-// pieces through its own ring of net_ring_slots() slots of kSlot elements (one bulk copy
-// each), filters them kSlice elements at a time, and keeps the 32*R best (key, index) composites of its stream sorted in
-// registers; candidates above the row threshold are batched in shared memory and
-// merged into that list with a bitonic network when a warp's region overflows.
-// ---------------------------------------------------------------------------------
-constexpr int kWarpMaxK = 128;
-constexpr int kSlice = 512;     // elements filtered per step (16 per lane); flat-partition granule
-constexpr int kSlot = 1024;     // elements per ring slot (one bulk copy; two slices)
-
-template <typename T>
-__host__ __device__ constexpr int net_ring_slots() { return sizeof(T) == 4 ? 2 : 4; }
-// Per-warp area in 32-bit words, rounded to 128 bytes so that every warp's ring slots
-// stay 16-byte aligned (TMA destinations, 128-bit loads).
-__host__ __device__ constexpr int net_area_words(int R, int slots, int esz) {
-    return ((slots * kSlot * esz) / 4 + 2 * slots + 64 * R + kSlice / 32 + 31) & ~31;
-}
-
-// Merges a warp's candidate batch (bcount entries of buf) into its sorted list, then
-// refreshes its K-th key `tau` and the largest dropped key `max_cut`.
-template <int R>
-__device__ __forceinline__ void net_merge_batch(uint64_t (&lst)[R], const uint64_t* buf, int& bcount, int K,
-                                                uint32_t& tau, uint32_t& max_cut) {
-    const int lane = threadIdx.x & 31;
-    VDXS_T0(t_mg);
-    uint64_t bv[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) {
-        const int i = r * 32 + lane;
-        bv[r] = i < bcount ? buf[i] : 0ull;
-    }
-    warp_sort_desc<R>(bv);
-    const uint64_t dropped = warp_merge_desc<R>(lst, bv);
-    max_cut = max(max_cut, (uint32_t)(dropped >> 32));
-    bcount = 0;
-    const uint64_t kth = warp_elem<R>(lst, K - 1);
-    tau = max(tau, (uint32_t)(kth >> 32));
-    __syncwarp();
-    VDXS_T1(11, t_mg);
-}
-
-// ---------------------------------------------------------------------------------
 // Threshold histogram of the stream kernel. Bins are the top 12 bits of the key (sign,
 // exponent and 3 mantissa bits); groups are the top 6 bits (64 bins each). Every count
 // is of distinct elements of one row, so any bin edge with at least K counted elements
@@ -1959,9 +1875,6 @@ __device__ __forceinline__ void net_merge_batch(uint64_t (&lst)[R], const uint64
 // ---------------------------------------------------------------------------------
 constexpr int kTBins = 4096;
 constexpr int kTGroups = 64;
-constexpr int kCandTotal = 2304;  // CTA candidate entries, the warp-list spill area included
-
-__host__ __device__ constexpr int hist_area_words() { return kTBins + kTGroups + 2 * kCandTotal; }
 
 __device__ __forceinline__ void lds_v2_volatile(const uint32_t* a, uint32_t& x, uint32_t& y) {
     asm volatile("ld.volatile.shared.v2.u32 {%0, %1}, [%2];" : "=r"(x), "=r"(y) : "r"(smem_u32(a)));
@@ -2022,838 +1935,6 @@ __device__ __forceinline__ float max16(const float (&x)[16]) {
     return fmaxf(fmax3f(a, b, c), fmax3f(d, e, x[15]));
 }
 
-// Stream stage 1 for top_k <= 128. Persistent CTAs (two per SM), 8 warps each. Work
-// item = (row, piece); warp w streams the contiguous sub-range [w*SW, (w+1)*SW) of the
-// piece through its own ring of TMA bulk copies (plain loads when the rows are not
-// 16-byte aligned). Elements at or above the CTA threshold are appended to a shared
-// candidate buffer and counted in the threshold histogram; the threshold is then
-// raised to the histogram's K-th edge and published per row, so every CTA of the row
-// filters against the best bound found so far. The first slice of each warp is counted
-// whole, which starts the threshold near the K-th key of the CTA's first 4096 elements.
-// At the end of an item the candidates at or above the final threshold are written out
-// unsorted (the finish kernel selects); only when more remain than the output holds is
-// an exact top-K taken here. If the buffer fills (e.g. many equal keys), a warp keeps
-// the rest of its candidates in an exact register list (bitonic networks, composite
-// (key, index) order), which also records any key it drops for the tie flags.
-template <typename T, bool TMA, int R>
-__global__ void __launch_bounds__(NT, 2) topk_hist_kernel(KParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint32_t* hist = (uint32_t*)smem_raw;
-    uint32_t* sh = hist + kHistWords;
-    unsigned char* region = smem_raw + kHeadBytes;
-    constexpr int RS = net_ring_slots<T>();
-    constexpr int VN = TMA ? (int)(16 / sizeof(T)) : 1;
-    constexpr int NB = 32 * R;  // list and batch length
-    constexpr int CAP = kCandTotal - NWARPS * NB;
-    constexpr int WCAP = CAP / NWARPS;  // candidate slots of each warp's region
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = p.K;
-    const int WW = net_area_words(R, RS, (int)sizeof(T));
-    uint32_t* wa = (uint32_t*)region + (size_t)warp * WW;
-    T* ring = (T*)wa;
-    uint64_t* full = (uint64_t*)(wa + (RS * kSlot * (int)sizeof(T)) / 4);
-    uint64_t* buf = full + RS;
-    uint32_t* wbm = (uint32_t*)(buf + NB);
-    uint32_t* H = (uint32_t*)region + (size_t)NWARPS * WW;
-    uint32_t* G = H + kTBins;
-    uint32_t* ckey = G + kTGroups;
-    uint32_t* cidx = ckey + kCandTotal;
-    volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current piece
-    uint32_t* s_ovf = sh + 22;         // some warp spilled to its list
-    uint32_t* s_out = sh + 23;         // output counter
-    uint32_t* s_cut = sh + 24;         // [NWARPS] largest key each warp list dropped
-    uint32_t* s_wcnt = sh + 48;        // [NWARPS] candidates in each warp's region
-    const float NANF = __uint_as_float(0x7FC00000u);
-    const int ng = p.flat_ng;
-    const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
-    const long long g_end = flat_start(p.flat_ngt, gridDim.x, blockIdx.x + 1);
-    const int b_first = (int)(g_begin / ng);
-    const int npieces = g_end > g_begin ? (int)((g_end - 1) / ng) - b_first + 1 : 0;
-    // This warp's element range of piece j (row b_first + j).
-    auto warp_range = [&](int j, int64_t& lo, int64_t& hi) {
-        const long long rb = (long long)(b_first + j) * ng;
-        const long long glo = max(g_begin, rb) - rb, ghi = min(g_end, rb + ng) - rb;
-        const long long w0 = glo + (ghi - glo) * warp / NWARPS, w1 = glo + (ghi - glo) * (warp + 1) / NWARPS;
-        lo = w0 * kSlice;
-        hi = min(w1 * kSlice, (long long)p.V);
-    };
-    for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
-    if (tid == 0) {
-        sh[20] = 0u;
-        sh[21] = 0u;
-        sh[22] = 0u;
-    }
-    __syncthreads();
-
-    // Producer cursor (lane 0): the warp's slices of its pieces, in consumption order.
-    int pj_prod = -1, pq = 0, pns = 0;
-    int64_t pleft = 0;
-    const T* psrc = nullptr;
-    uint32_t pn = 0;
-    auto next_piece = [&]() {
-        for (;;) {
-            if (++pj_prod >= npieces) return;
-            int64_t lo, hi;
-            warp_range(pj_prod, lo, hi);
-            if (hi > lo) {
-                pleft = hi - lo;
-                pns = (int)((pleft + kSlot - 1) / kSlot);
-                psrc = (const T*)p.logits + (int64_t)(b_first + pj_prod) * p.stride + lo;
-                pq = 0;
-                return;
-            }
-        }
-    };
-    auto issue = [&]() {
-        if (pq >= pns) next_piece();
-        if (pj_prod >= npieces) return;
-        const int nn = (int)min((int64_t)kSlot, pleft - (int64_t)pq * kSlot);
-        const int slot = (int)(pn % RS);
-        const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
-        if (bytes) {
-            mbar_arrive_expect_tx(&full[slot], bytes);
-            tma_load_1d(ring + (size_t)slot * kSlot, psrc + (int64_t)pq * kSlot, bytes, &full[slot]);
-        } else {
-            mbar_arrive(&full[slot]);
-        }
-        ++pn;
-        ++pq;
-    };
-    if constexpr (TMA) {
-        if (lane == 0) {
-            for (int s = 0; s < RS; ++s) mbar_init(&full[s], 1);
-            fence_mbar_init();
-            for (int s = 0; s < RS; ++s) issue();
-        }
-        __syncwarp();
-    }
-    // With a history, this kernel is a programmatic dependent of the penalty prep: the
-    // first slices are in flight; the penalty lists are read only after this wait (a
-    // no-op for an ordinary launch).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-
-    // Slice loads: 16 values per lane; NaN marks positions past the end.
-    // Half `half` of ring slot `slot` (n valid elements from row position start); the
-    // bulk copy covered the slot's bytes rounded down to 16, which within a half is the
-    // half's own count rounded the same way (a slice is a multiple of 16 bytes).
-    auto load_ring = [&](float (&x)[16], int slot, int half, int n, const T* row, int64_t start) {
-        const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
-        const T* sl = ring + (size_t)slot * kSlot + (size_t)half * kSlice;
-#pragma unroll
-        for (int j = 0; j < 16 / VN; ++j) {
-            const int pos = (j * 32 + lane) * VN;
-            if (pos + VN <= n_tma) {
-                unpack(*reinterpret_cast<const uint4*>(sl + pos), &x[j * VN], T());
-            } else {
-#pragma unroll
-                for (int e = 0; e < VN; ++e) {
-                    const int i = pos + e;
-                    x[j * VN + e] = i < n ? (i < n_tma ? to_f(sl[i]) : ld_elem(row, start + i)) : NANF;
-                }
-            }
-        }
-    };
-    // Penalised history ids are excluded from stage 1 (they re-enter in stage 2).
-    auto mask_penalised = [&](float (&x)[16], const int32_t* pid, int npen, int& pj, int64_t start, int n) {
-        if (lane < kSlice / 32) wbm[lane] = 0u;
-        __syncwarp();
-        for (;;) {
-            const int j = pj + lane;
-            const bool in = j < npen && pid[j] < start + n;
-            if (in) {
-                const int d = (int)(pid[j] - start);
-                atomicOr(&wbm[d >> 5], 1u << (d & 31));
-            }
-            const unsigned m = __ballot_sync(FULL, in);
-            pj += __popc(m);
-            if (m != FULL) break;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-            if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
-        }
-        __syncwarp();
-    };
-    // Counts each lane's maximum of a slice: distinct elements, so any count is still a
-    // valid basis for the threshold, at one atomic pair per lane instead of sixteen.
-    auto count_slice = [&](const float (&x)[16]) {
-        const float m = max16(x);
-        if (m == m) {
-            const uint32_t k = f2key(m);
-            atomicAdd(&H[k >> 20], 1u);
-            atomicAdd(&G[k >> 26], 1u);
-        }
-    };
-
-    uint32_t cn = 0;
-    bool timed_out = false;
-    for (int j = 0; j < npieces; ++j) {
-        const int b = b_first + j;
-        const T* row = (const T*)p.logits + (int64_t)b * p.stride;
-        const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
-        const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-        int64_t a0, a1;
-        warp_range(j, a0, a1);
-        const int ns = a1 > a0 ? (int)((a1 - a0 + kSlice - 1) / kSlice) : 0;
-        uint64_t lst[R];
-#pragma unroll
-        for (int r = 0; r < R; ++r) lst[r] = 0ull;
-        int bcount = 0, pj = 0;
-        uint32_t tau = 0u, max_cut = 0u;
-        bool ovf = false;  // warp-uniform: candidates go to the exact list from now on
-        uint32_t since = 0u;  // candidates counted since the threshold was last raised
-        uint32_t wcnt = 0u;   // candidates in this warp's region of the buffer
-        uint32_t* rkey = ckey + warp * WCAP;
-        uint32_t* ridx = cidx + warp * WCAP;
-        if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
-        uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
-        uint32_t rtau_next = ld_relaxed_u32(rtp);
-        // Counting phase: the first slices already in the ring are counted whole before
-        // any is filtered, so the threshold starts near the K-th key of the CTA's first
-        // NWARPS * RS slices of the piece. Counted elements are not counted again.
-        int ncounted = 0;
-        if constexpr (TMA) {
-            ncounted = min(2 * RS, ns);
-            int pjc = pj;
-            for (int q = 0; q < ncounted; ++q) {
-                const int64_t start = a0 + (int64_t)q * kSlice;
-                const int n = (int)min((int64_t)kSlice, a1 - start);
-                const uint32_t c = cn + (uint32_t)(q >> 1);
-                if ((q & 1) == 0 && !mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
-                float x[16];
-                load_ring(x, (int)(c % RS), q & 1, n, row, start);
-                if (npen > 0) mask_penalised(x, pid, npen, pjc, start, n);
-                count_slice(x);
-            }
-        }
-        if (ncounted > 0) {
-            __syncwarp();
-            const uint32_t t = hist_threshold(H, G, K);
-            if (lane == 0 && t > *s_T) {
-                atomicMax((uint32_t*)s_T, t);
-                if (t > rtau_next) atomicMax(rtp, t);
-            }
-        }
-        VDXS_T0(t_item);
-
-        for (int q = 0; q < ns; ++q) {
-            const int64_t start = a0 + (int64_t)q * kSlice;
-            const int n = (int)min((int64_t)kSlice, a1 - start);
-            // The row bound is fetched one slice ahead so its L2 latency is hidden.
-            const uint32_t rtau = rtau_next;
-            rtau_next = ld_relaxed_u32(rtp);
-            float x[16];
-            if constexpr (TMA) {
-                const uint32_t c = cn + (uint32_t)(q >> 1);
-                const int slot = (int)(c % RS);
-                if ((q & 1) == 0 && !mbar_wait_bounded(&full[slot], (c / RS) & 1u)) timed_out = true;
-                load_ring(x, slot, q & 1, n, row, start);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int pos = e * 32 + lane;
-                    x[e] = pos < n ? ld_elem(row, start + pos) : NANF;
-                }
-            }
-            if (npen > 0) mask_penalised(x, pid, npen, pj, start, n);
-            bool counted = q < ncounted;
-            if (!TMA && q == 0) {
-                // Plain-load path: count the first slice, then take its threshold.
-                count_slice(x);
-                __syncwarp();
-                const uint32_t t = hist_threshold(H, G, K);
-                if (lane == 0 && t > *s_T) {
-                    atomicMax((uint32_t*)s_T, t);
-                    if (t > rtau) atomicMax(rtp, t);
-                }
-                counted = true;
-            }
-            // Threshold: the CTA's, the row's and (after a spill) the warp list's K-th key.
-            const uint32_t tg = max(max(*s_T, rtau), tau);
-            float thr = key_threshold(tg);
-            const float lmax = max16(x);
-            const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
-            if constexpr (TMA) {
-                // After a slot's last half the slot's values are in registers: refill it.
-                if (lane == 0 && ((q & 1) == 1 || q == ns - 1)) {
-                    fence_proxy_async_smem();
-                    issue();
-                }
-            }
-            if (lanes == 0u) continue;
-            const uint32_t gb = (uint32_t)(p.vocab_offset + start);
-            bool added = false;
-            if (!ovf) {
-                uint32_t pm = 0u;
-#pragma unroll
-                for (int e = 0; e < 16; ++e) pm |= (x[e] >= thr ? 1u : 0u) << e;
-                const uint32_t cnt = (uint32_t)__popc(pm);
-                if (!__any_sync(FULL, cnt > 1u)) {
-                    // Common case: at most one candidate per lane, which is then the lane
-                    // maximum; one ballot gives the slots.
-                    const uint32_t total = (uint32_t)__popc(lanes);
-                    if (wcnt + total > (uint32_t)WCAP) {
-                        ovf = true;
-                        if (lane == 0) atomicExch(s_ovf, 1u);
-                    } else {
-                        if (cnt) {
-                            const int e = __ffs((int)pm) - 1;
-                            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                            const uint32_t k = f2key(lmax);
-                            const uint32_t slot = wcnt + __popc(lanes & lanemask_lt());
-                            rkey[slot] = k;
-                            ridx[slot] = gb + (uint32_t)pos;
-                            if (!counted) {
-                                atomicAdd(&H[k >> 20], 1u);
-                                atomicAdd(&G[k >> 26], 1u);
-                            }
-                        }
-                        wcnt += total;
-                        added = true;
-                        since += total;
-                    }
-                } else {
-                // General case: a per-lane pass mask, one warp scan, then predicated stores.
-                uint32_t incl = cnt;
-#pragma unroll
-                for (int d = 1; d < 32; d <<= 1) {
-                    const uint32_t o = __shfl_up_sync(FULL, incl, d);
-                    if (lane >= d) incl += o;
-                }
-                const uint32_t total = __shfl_sync(FULL, incl, 31);
-                if (wcnt + total > (uint32_t)WCAP) {
-                    // Region full: spill the whole slice to the exact list.
-                    ovf = true;
-                    if (lane == 0) atomicExch(s_ovf, 1u);
-                } else {
-                    uint32_t slot = wcnt + incl - cnt;
-                    wcnt += total;
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        if ((pm >> e) & 1u) {
-                            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                            const uint32_t k = f2key(x[e]);
-                            rkey[slot] = k;
-                            ridx[slot] = gb + (uint32_t)pos;
-                            ++slot;
-                            if (!counted) {
-                                atomicAdd(&H[k >> 20], 1u);
-                                atomicAdd(&G[k >> 26], 1u);
-                            }
-                        }
-                    }
-                    added = true;
-                    since += total;
-                }
-                }
-            }
-            int e0 = 0;
-            if (ovf) {
-                // Exact list: append from element e0 on; merge when the batch would
-                // overflow, then tighten the threshold and resume.
-                for (;;) {
-                    int stop = 16;
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                        const bool pass = e >= e0 && x[e] >= thr;
-                        const unsigned m = __ballot_sync(FULL, pass);
-                        if (m == 0u) continue;
-                        if (bcount + __popc(m) > NB) {
-                            stop = e;
-                            break;
-                        }
-                        if (pass) buf[bcount + __popc(m & lanemask_lt())] = comp_key(f2key(x[e]), gb + (uint32_t)pos);
-                        bcount += __popc(m);
-                    }
-                    if (stop == 16) break;
-                    __syncwarp();
-                    net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
-                    const uint32_t kk = (uint32_t)(warp_elem<R>(lst, K - 1) >> 32);
-                    if (kk) {
-                        thr = fmaxf(thr, key_threshold(kk));
-                        if (lane == 0) {
-                            atomicMax((uint32_t*)s_T, kk);
-                            atomicMax(rtp, kk);
-                        }
-                    }
-                    e0 = stop;
-                }
-            }
-            if (added && !counted && since >= 8u) {
-                // Raise the threshold once a few new candidates have been counted.
-                since = 0u;
-                __syncwarp();
-                const uint32_t t = hist_threshold(H, G, K);
-                if (lane == 0 && t > *s_T) {
-                    atomicMax((uint32_t*)s_T, t);
-                    if (t > rtau) atomicMax(rtp, t);
-                }
-            }
-            __syncwarp();
-        }
-        if (ovf) {
-            if (bcount > 0) net_merge_batch<R>(lst, buf, bcount, K, tau, max_cut);
-            // Entries past the K-th are cut when the list is published.
-            if (K < NB) max_cut = max(max_cut, (uint32_t)(warp_elem<R>(lst, K) >> 32));
-        }
-        if constexpr (TMA) cn += (uint32_t)((ns + 1) >> 1);  // slots this piece used
-        VDXS_T1(10, t_item);
-        if (lane == 0) {
-            s_cut[warp] = ovf ? max_cut : 0u;
-            s_wcnt[warp] = wcnt;
-        }
-        __syncthreads();
-        VDXS_T0(t_cm);
-        if (warp == 0) {
-            // Final threshold of the piece from the complete histogram.
-            const uint32_t t = hist_threshold(H, G, K);
-            if (lane == 0) {
-                sh[19] = max(max((uint32_t)*s_T, t), ld_relaxed_u32(rtp));
-                *s_out = 0u;
-            }
-        }
-        __syncthreads();
-        // Every candidate at or above the final threshold leaves; anything below it is
-        // below the row's K-th key, so it cannot be selected or tie at the boundary.
-        const uint32_t tfin = sh[19];
-        const bool any_ovf = *s_ovf != 0u;
-        const int item = (int)blockIdx.x * p.flat_pmax + j;
-        uint2* out = p.cand + (size_t)item * p.cand_cap;
-        bool done = false;
-        if (!any_ovf) {
-            for (int i0 = 0; i0 < CAP; i0 += NT) {
-                const int i = i0 + tid;
-                uint32_t k = 0u;
-                bool sel = false;
-                if (i < CAP && (uint32_t)(i % WCAP) < s_wcnt[i / WCAP]) {
-                    k = ckey[i];
-                    sel = k >= tfin;
-                }
-                const unsigned m = __ballot_sync(FULL, sel);
-                if (m) {
-                    uint32_t base = 0u;
-                    if (lane == 0) base = atomicAdd(s_out, (uint32_t)__popc(m));
-                    base = __shfl_sync(FULL, base, 0);
-                    const uint32_t slot = base + __popc(m & lanemask_lt());
-                    if (sel && slot < (uint32_t)p.cand_cap) out[slot] = make_uint2(k, cidx[i]);
-                }
-            }
-            __syncthreads();
-            const uint32_t total = *s_out;
-            if (total <= (uint32_t)p.cand_cap) {
-                if (tid == 0) {
-                    p.chunk_info[item] = make_uint2(total, 0u);
-                    p.item_tau[item] = tfin;
-                }
-                done = true;
-            }
-        }
-        if (!done) {
-            // Exact top-K of the buffer (and of the warp lists after a spill). Unused
-            // region slots are blanked (key 0 is never selected).
-            for (int i = tid; i < CAP; i += NT)
-                if ((uint32_t)(i % WCAP) >= s_wcnt[i / WCAP]) ckey[i] = 0u;
-            int nin = CAP;
-            if (any_ovf) {
-#pragma unroll
-                for (int r = 0; r < R; ++r) {
-                    const int i = CAP + warp * NB + r * 32 + lane;
-                    const uint64_t v = lst[r];
-                    ckey[i] = v ? (uint32_t)(v >> 32) : 0u;
-                    cidx[i] = ~(uint32_t)v;
-                }
-                nin = CAP + NWARPS * NB;
-            }
-            __syncthreads();
-            uint32_t km = 0u;
-            for (int i = tid; i < nin; i += NT) km = max(km, ckey[i]);
-            km = block_max_u32(km, sh + 32);
-            const int tbb = bits_for((uint32_t)(p.vocab_offset + p.V - 1));
-            const SelectOut so = block_select(SmemPairSrc{ckey, cidx}, nin, K, km, tbb, hist, sh);
-            uint32_t* ok = H;
-            uint32_t* oi = H + K;
-            const int m_out = block_emit(SmemPairSrc{ckey, cidx}, nin, so, ok, oi, K, &sh[8], IdentIdx{cidx});
-            for (int i = tid; i < m_out; i += NT) out[i] = make_uint2(ok[i], oi[i]);
-            if (tid == 0) {
-                uint32_t cut = so.tie_cut ? so.kth_key : 0u;
-                for (int w = 0; w < NWARPS; ++w) cut = max(cut, s_cut[w]);
-                p.chunk_info[item] = make_uint2((uint32_t)m_out, cut);
-                p.item_tau[item] = tfin;
-            }
-        }
-        __syncthreads();
-        for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
-        if (tid == 0) {
-            sh[20] = 0u;
-            sh[22] = 0u;
-        }
-        __syncthreads();
-        VDXS_T1(13, t_cm);
-    }
-    if (__any_sync(FULL, timed_out) && lane == 0) atomicExch(p.err, kErrTimeout);
-    if constexpr (TMA) {
-        __syncwarp();
-        if (lane == 0)
-            for (int s = 0; s < RS; ++s) mbar_inval(&full[s]);
-    }
-    // This CTA is done: the finish kernel may start launching (it waits for the grid).
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// ---------------------------------------------------------------------------------
-// Stream stage 1 for kWarpMaxK < top_k <= kMaxTopK. Same flat partition, per-warp TMA
-// rings and threshold histogram as topk_hist_kernel, but a warp appends the elements
-// of a slice that reach the threshold straight to its piece's candidate list in global
-// memory (one shared-memory reservation per warp and slice), and nothing is selected
-// here: every element at or above the piece's final threshold is in the list, so no
-// key at or above the row's K-th key is ever dropped. The finish kernel gathers the
-// entries at or above the row's best bound and selects; a list that outgrows its
-// capacity (count > cand_cap) sends the row to the finish kernel's exact fallback.
-// ---------------------------------------------------------------------------------
-template <typename T, bool TMA>
-__global__ void __launch_bounds__(NT, 2) topk_wide_kernel(KParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint32_t* hist = (uint32_t*)smem_raw;
-    uint32_t* sh = hist + kHistWords;
-    unsigned char* region = smem_raw + kHeadBytes;
-    constexpr int RS = net_ring_slots<T>();
-    constexpr int VN = TMA ? (int)(16 / sizeof(T)) : 1;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = p.K;
-    const int WW = net_area_words(0, RS, (int)sizeof(T));
-    uint32_t* wa = (uint32_t*)region + (size_t)warp * WW;
-    T* ring = (T*)wa;
-    uint64_t* full = (uint64_t*)(wa + (RS * kSlot * (int)sizeof(T)) / 4);
-    uint32_t* wbm = (uint32_t*)(full + RS);
-    uint32_t* H = (uint32_t*)region + (size_t)NWARPS * WW;
-    uint32_t* G = H + kTBins;
-    volatile uint32_t* s_T = sh + 20;  // CTA threshold key of the current piece
-    uint32_t* s_out = sh + 23;         // entries appended to the current piece's list
-    const float NANF = __uint_as_float(0x7FC00000u);
-    const uint32_t cap = (uint32_t)p.cand_cap;
-    // The threshold is re-derived from the histogram after this many new candidates.
-    const uint32_t raise_every = (uint32_t)max(8, K / 32);
-    const int ng = p.flat_ng;
-    const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
-    const long long g_end = flat_start(p.flat_ngt, gridDim.x, blockIdx.x + 1);
-    const int b_first = (int)(g_begin / ng);
-    const int npieces = g_end > g_begin ? (int)((g_end - 1) / ng) - b_first + 1 : 0;
-    auto warp_range = [&](int j, int64_t& lo, int64_t& hi) {
-        const long long rb = (long long)(b_first + j) * ng;
-        const long long glo = max(g_begin, rb) - rb, ghi = min(g_end, rb + ng) - rb;
-        const long long w0 = glo + (ghi - glo) * warp / NWARPS, w1 = glo + (ghi - glo) * (warp + 1) / NWARPS;
-        lo = w0 * kSlice;
-        hi = min(w1 * kSlice, (long long)p.V);
-    };
-    for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
-    if (tid == 0) {
-        sh[20] = 0u;
-        sh[23] = 0u;
-    }
-    __syncthreads();
-
-    int pj_prod = -1, pq = 0, pns = 0;
-    int64_t pleft = 0;
-    const T* psrc = nullptr;
-    uint32_t pn = 0;
-    auto next_piece = [&]() {
-        for (;;) {
-            if (++pj_prod >= npieces) return;
-            int64_t lo, hi;
-            warp_range(pj_prod, lo, hi);
-            if (hi > lo) {
-                pleft = hi - lo;
-                pns = (int)((pleft + kSlot - 1) / kSlot);
-                psrc = (const T*)p.logits + (int64_t)(b_first + pj_prod) * p.stride + lo;
-                pq = 0;
-                return;
-            }
-        }
-    };
-    auto issue = [&]() {
-        if (pq >= pns) next_piece();
-        if (pj_prod >= npieces) return;
-        const int nn = (int)min((int64_t)kSlot, pleft - (int64_t)pq * kSlot);
-        const int slot = (int)(pn % RS);
-        const uint32_t bytes = (uint32_t)((size_t)nn * sizeof(T)) & ~15u;
-        if (bytes) {
-            mbar_arrive_expect_tx(&full[slot], bytes);
-            tma_load_1d(ring + (size_t)slot * kSlot, psrc + (int64_t)pq * kSlot, bytes, &full[slot]);
-        } else {
-            mbar_arrive(&full[slot]);
-        }
-        ++pn;
-        ++pq;
-    };
-    if constexpr (TMA) {
-        if (lane == 0) {
-            for (int s = 0; s < RS; ++s) mbar_init(&full[s], 1);
-            fence_mbar_init();
-            for (int s = 0; s < RS; ++s) issue();
-        }
-        __syncwarp();
-    }
-    // With a history, this kernel is a programmatic dependent of the penalty prep: the
-    // first slices are in flight; the penalty lists are read only after this wait (a
-    // no-op for an ordinary launch).
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    // Half `half` of ring slot `slot` (n valid elements from row position start); the
-    // bulk copy covered the slot's bytes rounded down to 16, which within a half is the
-    // half's own count rounded the same way (a slice is a multiple of 16 bytes).
-    auto load_ring = [&](float (&x)[16], int slot, int half, int n, const T* row, int64_t start) {
-        const int n_tma = (int)((((size_t)n * sizeof(T)) & ~(size_t)15) / sizeof(T));
-        const T* sl = ring + (size_t)slot * kSlot + (size_t)half * kSlice;
-#pragma unroll
-        for (int j = 0; j < 16 / VN; ++j) {
-            const int pos = (j * 32 + lane) * VN;
-            if (pos + VN <= n_tma) {
-                unpack(*reinterpret_cast<const uint4*>(sl + pos), &x[j * VN], T());
-            } else {
-#pragma unroll
-                for (int e = 0; e < VN; ++e) {
-                    const int i = pos + e;
-                    x[j * VN + e] = i < n ? (i < n_tma ? to_f(sl[i]) : ld_elem(row, start + i)) : NANF;
-                }
-            }
-        }
-    };
-    // Penalised history ids are excluded from stage 1 (they re-enter in stage 2).
-    auto mask_penalised = [&](float (&x)[16], const int32_t* pid, int npen, int& pj, int64_t start, int n) {
-        if (lane < kSlice / 32) wbm[lane] = 0u;
-        __syncwarp();
-        for (;;) {
-            const int j = pj + lane;
-            const bool in = j < npen && pid[j] < start + n;
-            if (in) {
-                const int d = (int)(pid[j] - start);
-                atomicOr(&wbm[d >> 5], 1u << (d & 31));
-            }
-            const unsigned m = __ballot_sync(FULL, in);
-            pj += __popc(m);
-            if (m != FULL) break;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-            const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-            if ((wbm[pos >> 5] >> (pos & 31)) & 1u) x[e] = NANF;
-        }
-        __syncwarp();
-    };
-    auto count_slice = [&](const float (&x)[16]) {
-        const float m = max16(x);
-        if (m == m) {
-            const uint32_t k = f2key(m);
-            atomicAdd(&H[k >> 20], 1u);
-            atomicAdd(&G[k >> 26], 1u);
-        }
-    };
-
-    uint32_t cn = 0;
-    bool timed_out = false;
-    for (int j = 0; j < npieces; ++j) {
-        const int b = b_first + j;
-        const T* row = (const T*)p.logits + (int64_t)b * p.stride;
-        const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
-        const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-        const int item = (int)blockIdx.x * p.flat_pmax + j;
-        uint2* out = p.cand + (size_t)item * p.cand_cap;
-        int64_t a0, a1;
-        warp_range(j, a0, a1);
-        const int ns = a1 > a0 ? (int)((a1 - a0 + kSlice - 1) / kSlice) : 0;
-        int pj = 0;
-        uint32_t since = 0u;
-        if (npen > 0) pj = lower_bound_i32(pid, npen, a0);
-        uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
-        uint32_t rtau_next = ld_relaxed_u32(rtp);
-        int ncounted = 0;
-        if constexpr (TMA) {
-            // Counting phase: each lane counts the m largest keys of each of the first
-            // slices already in the rings (m grows with K, so the counted set holds
-            // nearly all of those slices' top-K); the group totals are then summed from
-            // the bins once, and every warp takes the threshold.
-            const int mc = K <= 256 ? 1 : (K <= 512 ? 2 : 4);
-            ncounted = min(2 * RS, ns);
-            int pjc = pj;
-            for (int q = 0; q < ncounted; ++q) {
-                const int64_t start = a0 + (int64_t)q * kSlice;
-                const int n = (int)min((int64_t)kSlice, a1 - start);
-                const uint32_t c = cn + (uint32_t)(q >> 1);
-                if ((q & 1) == 0 && !mbar_wait_bounded(&full[c % RS], (c / RS) & 1u)) timed_out = true;
-                float x[16];
-                load_ring(x, (int)(c % RS), q & 1, n, row, start);
-                if (npen > 0) mask_penalised(x, pid, npen, pjc, start, n);
-                uint32_t top[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    uint32_t k = x[e] == x[e] ? f2key(x[e]) : 0u;
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const uint32_t hi = max(top[r], k);
-                        k = min(top[r], k);
-                        top[r] = hi;
-                    }
-                }
-#pragma unroll
-                for (int r = 0; r < 4; ++r)
-                    if (r < mc && top[r]) atomicAdd(&H[top[r] >> 20], 1u);
-            }
-            __syncthreads();
-            {
-                constexpr int BPT = kTBins / NT;  // bins summed per thread, within one group
-                uint32_t sum = 0u;
-#pragma unroll
-                for (int i = 0; i < BPT; ++i) sum += H[tid * BPT + i];
-                if (sum) atomicAdd(&G[(tid * BPT) >> 6], sum);
-            }
-            __syncthreads();
-            const uint32_t t = hist_threshold(H, G, K);
-            if (lane == 0 && t > *s_T) {
-                atomicMax((uint32_t*)s_T, t);
-                if (t > rtau_next) atomicMax(rtp, t);
-            }
-        }
-        VDXS_T0(t_item);
-        for (int q = 0; q < ns; ++q) {
-            const int64_t start = a0 + (int64_t)q * kSlice;
-            const int n = (int)min((int64_t)kSlice, a1 - start);
-            const uint32_t rtau = rtau_next;
-            rtau_next = ld_relaxed_u32(rtp);
-            float x[16];
-            if constexpr (TMA) {
-                const uint32_t c = cn + (uint32_t)(q >> 1);
-                const int slot = (int)(c % RS);
-                if ((q & 1) == 0 && !mbar_wait_bounded(&full[slot], (c / RS) & 1u)) timed_out = true;
-                load_ring(x, slot, q & 1, n, row, start);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const int pos = e * 32 + lane;
-                    x[e] = pos < n ? ld_elem(row, start + pos) : NANF;
-                }
-            }
-            if (npen > 0) mask_penalised(x, pid, npen, pj, start, n);
-            bool counted = q < ncounted;
-            if (!TMA && q == 0) {
-                count_slice(x);
-                __syncwarp();
-                const uint32_t t = hist_threshold(H, G, K);
-                if (lane == 0 && t > *s_T) {
-                    atomicMax((uint32_t*)s_T, t);
-                    if (t > rtau) atomicMax(rtp, t);
-                }
-                counted = true;
-            }
-            const uint32_t tkey = max((uint32_t)*s_T, rtau);
-            const float thr = key_threshold(tkey);
-            // A candidate in the threshold's own bin cannot raise the threshold (that
-            // needs K counts at a higher edge), so only candidates above it are counted.
-            const uint32_t tbin = tkey >> 20;
-            const float lmax = max16(x);
-            const unsigned lanes = __ballot_sync(FULL, lmax >= thr);
-            if constexpr (TMA) {
-                if (lane == 0 && ((q & 1) == 1 || q == ns - 1)) {
-                    fence_proxy_async_smem();
-                    issue();
-                }
-            }
-            if (lanes == 0u) continue;
-            const uint32_t gb = (uint32_t)(p.vocab_offset + start);
-            uint32_t pm = 0u;
-#pragma unroll
-            for (int e = 0; e < 16; ++e) pm |= (x[e] >= thr ? 1u : 0u) << e;
-            const uint32_t cnt = (uint32_t)__popc(pm);
-            uint32_t total;
-            if (!__any_sync(FULL, cnt > 1u)) {
-                // At most one candidate per lane (the lane maximum): contiguous slots.
-                total = (uint32_t)__popc(lanes);
-                uint32_t base = 0u;
-                if (lane == 0) base = atomicAdd(s_out, total);
-                base = __shfl_sync(FULL, base, 0);
-                if (cnt) {
-                    const int e = __ffs((int)pm) - 1;
-                    const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                    const uint32_t k = f2key(lmax);
-                    const uint32_t slot = base + __popc(lanes & lanemask_lt());
-                    if (slot < cap) out[slot] = make_uint2(k, gb + (uint32_t)pos);
-                    if (!counted && (k >> 20) > tbin) {
-                        atomicAdd(&H[k >> 20], 1u);
-                        atomicAdd(&G[k >> 26], 1u);
-                    }
-                }
-            } else {
-                uint32_t incl = cnt;
-#pragma unroll
-                for (int d = 1; d < 32; d <<= 1) {
-                    const uint32_t o = __shfl_up_sync(FULL, incl, d);
-                    if (lane >= d) incl += o;
-                }
-                total = __shfl_sync(FULL, incl, 31);
-                uint32_t base = 0u;
-                if (lane == 0) base = atomicAdd(s_out, total);
-                base = __shfl_sync(FULL, base, 0);
-                uint32_t slot = base + incl - cnt;
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    if ((pm >> e) & 1u) {
-                        const int pos = TMA ? ((e / VN) * 32 + lane) * VN + (e % VN) : e * 32 + lane;
-                        const uint32_t k = f2key(x[e]);
-                        if (slot < cap) out[slot] = make_uint2(k, gb + (uint32_t)pos);
-                        ++slot;
-                        if (!counted && (k >> 20) > tbin) {
-                            atomicAdd(&H[k >> 20], 1u);
-                            atomicAdd(&G[k >> 26], 1u);
-                        }
-                    }
-                }
-            }
-            since += total;
-            if (!counted && since >= raise_every) {
-                since = 0u;
-                __syncwarp();
-                const uint32_t t = hist_threshold(H, G, K);
-                if (lane == 0 && t > *s_T) {
-                    atomicMax((uint32_t*)s_T, t);
-                    if (t > rtau) atomicMax(rtp, t);
-                }
-            }
-            __syncwarp();
-        }
-        if constexpr (TMA) cn += (uint32_t)((ns + 1) >> 1);  // slots this piece used
-        VDXS_T1(10, t_item);
-        __syncthreads();
-        if (warp == 0) {
-            // Final threshold of the piece from the complete histogram.
-            const uint32_t t = hist_threshold(H, G, K);
-            if (lane == 0) {
-                const uint32_t tfin = max(max((uint32_t)*s_T, t), ld_relaxed_u32(rtp));
-                p.chunk_info[item] = make_uint2(*s_out, 0u);  // count > cand_cap: list incomplete
-                p.item_tau[item] = tfin;
-#ifdef VDXS_TIMING
-                atomicAdd(&g_phase_count[31], (unsigned long long)*s_out);
-#endif
-            }
-        }
-        __syncthreads();
-        for (int i = tid; i < kTBins + kTGroups; i += NT) H[i] = 0u;
-        if (tid == 0) {
-            sh[20] = 0u;
-            sh[23] = 0u;
-        }
-        __syncthreads();
-    }
-    if (__any_sync(FULL, timed_out) && lane == 0) atomicExch(p.err, kErrTimeout);
-    if constexpr (TMA) {
-        __syncwarp();
-        if (lane == 0)
-            for (int s = 0; s < RS; ++s) mbar_inval(&full[s]);
-    }
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
 // ---------------------------------------------------------------------------------
 // Small batches: one thread-block cluster of CL CTAs per row. Each CTA copies its 1/CL
 // of the row into its own shared memory (plain bulk copies of this CTA's part), masks
@@ -2877,45 +1958,49 @@ __device__ __forceinline__ uint16_t nan_bits<uint16_t>() { return (uint16_t)0x7F
 // ---------------------------------------------------------------------------------
 // Stream stage 1 (topk_stream_kernel): every top_k of the top-k path, and greedy.
 //
-// One persistent CTA of 16 warps per SM. The rows are cut into 4 KB slots (1024 fp32
-// or 2048 bf16 elements), and the B x slots-per-row slots are split evenly over the
-// grid (flat partition); a CTA's run of slots falls into pieces, maximal runs within one
-// row, and each piece is split evenly over the 16 warps. Each warp streams its slots
-// through its own two-slot ring of bulk copies. Lane l owns the slot's l-th 128-byte
-// group; it reads it as eight 16-byte chunks in a rotated order (conflict-free), and the
-// slot is refilled as soon as the warp holds it in registers. A lane keeps the maxima of
-// its eight chunks, so one compare of the lane maximum decides the whole group, and only
-// chunks whose maximum reaches the threshold are tested element by element.
+// Work: each row is cut into 4 KB slots (1024 fp32 or 2048 bf16 elements) and its slots
+// into units of p.unit_slots consecutive slots. Warps claim units one at a time from a
+// global counter, in column-major order (unit u is row u % B, segment u / B): every
+// row's first segments are streamed first, so later segments start from a bound that
+// earlier segments of the same row have already raised, and no SM waits on a static
+// share of the work. There is no CTA-wide synchronisation: every warp runs on its own.
 //
-// Threshold: one key histogram per CTA (top 12 key bits, plus 64 group counts). Every
-// count is of a distinct element of the piece's row, so the highest bin edge with at
-// least K counts at or above it is a lower bound on the row's K-th key. At the start of
-// a piece every warp counts the maximum (for top_k > 256 the eight chunk maxima) of each
-// lane of its first slot, before anything is filtered; later candidates are counted as
-// they are taken (not those in the threshold's own bin, which cannot raise it). The
-// bound is raised as counts grow and shared per CTA (shared memory) and per row
-// (row_tau, so that every CTA of a row filters against the best bound found).
+// Loading: each warp streams its slots through its own two-slot ring of bulk copies.
+// Lane l owns the slot's l-th 128-byte group and reads it as eight 16-byte chunks in a
+// rotated order (conflict-free); it keeps the maxima of its chunks, so one compare of the
+// lane maximum decides the whole group. Few hot lanes: the warp tests each hot group
+// together from shared memory. Many: each lane extracts its own candidates from its
+// registers, testing only chunks whose maximum reaches the bound.
 //
-// Output: every element of the piece at or above the piece's final bound is in the
-// piece's list (count in chunk_info.x; a count above cand_cap marks the list incomplete
-// and sends the row to the finish kernel's exact fallback). Candidates wait in a
-// per-warp shared region and leave at the piece's end (or when the region fills) if
-// they still reach the bound.
+// Bound: one key histogram per row in global memory (top 12 key bits, and 64 group
+// counts), counted with fire-and-forget atomics by every warp working on the row. Every
+// count is of a distinct element of the row, so the highest bin edge with at least K
+// counts at or above it is a lower bound on the row's K-th key. Candidates are counted
+// as they are taken (not those in the bound's own bin, which cannot raise it), and the
+// first slot of each unit is filtered against the K-th largest of its chunk maxima as
+// well (top_k <= 256). A warp raises the row bound (row_tau, atomicMax) from the
+// histogram asynchronously: the two dependent reads overlap the next two slots.
+//
+// Output: one list per row. Candidates wait in a per-warp shared region and are written
+// out when it fills and at the end of each unit if they still reach the bound then. The
+// final row bound is the largest bound any warp published, and every element at or
+// above it is in the list (an element at or above it was at or above every bound it was
+// tested or flushed against). row_cnt counts the list; a count above cand_cap marks it
+// incomplete and sends the row to the finish kernel's exact fallback. The finish kernel
+// resets the row's histogram, count and bound, and the claim counter, for the next call.
 // ---------------------------------------------------------------------------------
 constexpr int kS1Threads = 512;
 constexpr int kS1Warps = kS1Threads / 32;
 constexpr int kS1SlotBytes = 4096;                    // one bulk copy; a 128-byte group per lane
 constexpr int kS1Ring = 2;                            // ring slots per warp
 constexpr int kS1WCap = 128;                          // region entries per warp
-constexpr int kS1Prefetch = 4;                        // slots prefetched into L2 ahead of the ring
 constexpr int kS1CoopLanes = 8;                       // up to this many hot lanes: warp-cooperative test
-constexpr int kS1HeadWords = 64 + kTBins + kTGroups;  // scalars, key histogram, group counts
-constexpr int kS1WarpBytes = kS1Ring * kS1SlotBytes + 128 + 8 * kS1WCap;
-static_assert((4 * kS1HeadWords) % 128 == 0 && kS1WarpBytes % 128 == 0, "128-byte aligned warp areas");
+constexpr int kS1RaiseEvery = 4;                      // counted candidates between bound raises
+constexpr int kRowHistWords = kTBins + kTGroups;      // per-row histogram in global memory
+constexpr int kS1WarpBytes = kS1Ring * kS1SlotBytes + 64 + 8 * kS1WCap + 4 * 256;
+static_assert(kS1WarpBytes % 16 == 0, "16-byte aligned warp areas");
 
-__host__ __device__ constexpr size_t s1_smem_bytes() {
-    return (size_t)4 * kS1HeadWords + (size_t)kS1Warps * kS1WarpBytes;
-}
+__host__ __device__ constexpr size_t s1_smem_bytes() { return (size_t)kS1Warps * kS1WarpBytes; }
 template <typename T>
 __host__ __device__ constexpr int s1_slot_elems() { return kS1SlotBytes / (int)sizeof(T); }
 
@@ -2926,6 +2011,14 @@ __device__ __forceinline__ uint32_t bmax2(uint32_t a, uint32_t b) {  // packed b
 }
 __device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+__device__ __forceinline__ void red_add_u32(uint32_t* a, uint32_t v) {
+    asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint2 ld_relaxed_v2(const uint32_t* p) {
+    uint2 v;
+    asm volatile("ld.relaxed.gpu.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
 
 // Element e of a 16-byte chunk (4 fp32 or 8 bf16 values; e is a compile-time constant).
 template <typename T>
@@ -2947,6 +2040,50 @@ __device__ __forceinline__ float chunk_max(const uint4& v) {
     }
 }
 
+// One warp: a lower bound on the K-th largest of 8 keys per lane (key 0 = no element),
+// with the low 16 bits cleared: two radix passes of 8 bits over a 256-word warp-private
+// histogram. Returns 0 when fewer than K keys are valid.
+__device__ uint32_t warp_kth_of_keys8(const uint32_t (&k)[8], int K, uint32_t* wh) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0u, need = (uint32_t)K;
+#pragma unroll
+    for (int pass = 0; pass < 2; ++pass) {
+        const int shift = 24 - 8 * pass;
+        reinterpret_cast<uint4*>(wh)[2 * lane] = make_uint4(0u, 0u, 0u, 0u);
+        reinterpret_cast<uint4*>(wh)[2 * lane + 1] = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (k[j] != 0u && (pass == 0 || (k[j] >> 24) == (prefix >> 24))) atomicAdd(&wh[(k[j] >> shift) & 255u], 1u);
+        __syncwarp();
+        const uint4 a = reinterpret_cast<const uint4*>(wh)[2 * lane];
+        const uint4 c = reinterpret_cast<const uint4*>(wh)[2 * lane + 1];
+        const uint32_t cnt[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+        const uint32_t mine = a.x + a.y + a.z + a.w + c.x + c.y + c.z + c.w;
+        const uint32_t suf = warp_suffix_sum(mine);  // counts in bins >= 8 * lane
+        const unsigned m = __ballot_sync(FULL, suf >= need);
+        __syncwarp();
+        if (m == 0u) return pass == 0 ? 0u : prefix;
+        const int l0 = 31 - __clz((int)m);  // lane holding the bin that reaches `need`
+        uint32_t above = __shfl_sync(FULL, suf - mine, l0);  // counts in bins >= 8 * (l0 + 1)
+        int bin = 8 * l0;
+        if (lane == l0) {
+            uint32_t s = above;
+            int j = 7;
+            for (; j > 0; --j) {
+                if (s + cnt[j] >= need) break;
+                s += cnt[j];
+            }
+            bin += j;
+            above = s;
+        }
+        bin = __shfl_sync(FULL, bin, l0);
+        above = __shfl_sync(FULL, above, l0);
+        prefix |= (uint32_t)bin << shift;
+        need -= above;
+    }
+    return prefix;
+}
 
 // Development counters of topk_stream_kernel (-DVDXS_TIMING builds only): each warp sums
 // its phase cycles and event counts in registers and adds them once at the end
@@ -2984,233 +2121,348 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     S1_DBG_DECL;
     S1_T0(t_all);
-    uint32_t* sh = (uint32_t*)smem_raw;
-    uint32_t* H = sh + 64;
-    uint32_t* Gc = H + kTBins;
     constexpr int SE = s1_slot_elems<T>();  // elements per slot
     constexpr int GE = SE / 32;             // elements per lane group
     constexpr int CE = GE / 8;              // elements per 16-byte chunk
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sw = lane & 7;
     const int K = p.K;
-    unsigned char* wa = smem_raw + 4 * kS1HeadWords + (size_t)warp * kS1WarpBytes;
+    unsigned char* wa = smem_raw + (size_t)warp * kS1WarpBytes;
     unsigned char* ring = wa;
     uint64_t* full = (uint64_t*)(wa + kS1Ring * kS1SlotBytes);
-    uint32_t* rkey = (uint32_t*)(wa + kS1Ring * kS1SlotBytes + 128);
+    int32_t* wq = (int32_t*)(full + kS1Ring);  // [kS1Ring][2]: (row, slot) staged in each ring slot
+    uint32_t* rkey = (uint32_t*)(wa + kS1Ring * kS1SlotBytes + 64);
     uint32_t* ridx = rkey + kS1WCap;
-    volatile uint32_t* s_T = sh;  // CTA threshold key of the current piece
-    uint32_t* s_cnt = sh + 1;     // entries reserved in the current piece's list
-    const int ng = p.flat_ng;
-    const long long g_begin = flat_start(p.flat_ngt, gridDim.x, blockIdx.x);
-    const long long g_end = flat_start(p.flat_ngt, gridDim.x, blockIdx.x + 1);
-    const int b_first = (int)(g_begin / ng);
-    const int npieces = g_end > g_begin ? (int)((g_end - 1) / ng) - b_first + 1 : 0;
-    // This warp's slots [q0, q1) of piece j (slot indices within row b_first + j).
-    auto warp_slots = [&](int j, int& q0, int& q1) {
-        const long long rb = (long long)(b_first + j) * ng;
-        const long long glo = max(g_begin, rb) - rb, ghi = min(g_end, rb + ng) - rb;
-        q0 = (int)(glo + (ghi - glo) * warp / kS1Warps);
-        q1 = (int)(glo + (ghi - glo) * (warp + 1) / kS1Warps);
-    };
-    for (int i = tid; i < kTBins + kTGroups; i += kS1Threads) H[i] = 0u;
-    if (tid == 0) {
-        sh[0] = 0u;
-        sh[1] = 0u;
-    }
-    __syncthreads();
+    uint32_t* wh = ridx + kS1WCap;  // 256-word warp histogram (first-slot bound)
+    const int ng = p.flat_ng;       // slots per row
+    const int U = p.unit_slots;     // slots per row segment
+    const int nseg = (ng + U - 1) / U;
+    // Slot enumeration, column-major over row segments: position g is segment
+    // g / (B * U), row (g / U) % B, slot (g / (B * U)) * U + g % U of that row (positions past
+    // the row's last slot are skipped).
+    const long long ne = (long long)p.B * nseg * U;
+    const long long nwarps = (long long)gridDim.x * kS1Warps;
 
-    // Producer cursors (lane 0): this warp's slots of its pieces, in consumption order.
-    // The copy cursor fills the ring; the prefetch cursor runs p.pf slots ahead of it and
-    // only asks for the bytes to be brought into L2, so more of the stream is in flight
-    // than the shared-memory ring holds.
-    struct Cursor {
-        int pj = -1, pq = 0, pq_end = 0;
+    // Producer (lane 0): claims runs of positions and issues the ring's bulk copies in order.
+    // Runs are U positions long until the remaining work nears two runs per warp, then
+    // shrink to one slot, so that warps run out of work together.
+    long long cg = 0, ce = 0;  // the producer's claimed run [cg, ce)
+    long long ng0 = 0, nc = 0;  // the next run, claimed one run ahead: start (atomic result) and length
+    bool have_next = false;
+    uint32_t pn = 0;            // copies issued
+    bool pr_done = false;
+    auto claim_next = [&](long long left_est) {
+        nc = max(1LL, min((long long)U, left_est / (2 * nwarps)));
+        ng0 = (long long)atomicAdd((unsigned long long*)p.unit_next, (unsigned long long)nc);
+        have_next = true;
     };
-    auto advance = [&](Cursor& c) -> bool {  // moves c to its next slot; false when done
-        while (c.pq >= c.pq_end) {
-            if (++c.pj >= npieces) return false;
-            warp_slots(c.pj, c.pq, c.pq_end);
-        }
-        return true;
-    };
-    auto slot_bytes = [&](const Cursor& c) -> uint32_t {  // the slot's bytes, rounded down to 16
-        const int n = (int)min((int64_t)SE, (int64_t)p.V - (int64_t)c.pq * SE);
-        return ((uint32_t)n * (uint32_t)sizeof(T)) & ~15u;
-    };
-    auto slot_src = [&](const Cursor& c) -> const T* {
-        return (const T*)p.logits + (int64_t)(b_first + c.pj) * p.stride + (int64_t)c.pq * SE;
-    };
-    Cursor cc_copy, cc_pf;
-    uint32_t pn = 0;
-    auto prefetch_next = [&]() {
-        if (!advance(cc_pf)) return;
-        const uint32_t bytes = slot_bytes(cc_pf);
-        if (bytes) l2_prefetch_bulk(slot_src(cc_pf), bytes);
-        ++cc_pf.pq;
-    };
+    // Position of cg within the enumeration: segment, row and slot offset, advanced
+    // incrementally (one division per run).
+    int cseg = 0, crow = 0, ct = 0;
     auto issue = [&]() {
-        if (!advance(cc_copy)) return;
-        const int s = (int)(pn % kS1Ring);
-        const uint32_t bytes = slot_bytes(cc_copy);
-        if (bytes) {
-            mbar_arrive_expect_tx(&full[s], bytes);
-            tma_load_1d(ring + s * kS1SlotBytes, slot_src(cc_copy), bytes, &full[s]);
-        } else {
-            mbar_arrive(&full[s]);
-        }
-        ++pn;
-        ++cc_copy.pq;
-    };
-    if constexpr (TMA) {
-        if (lane == 0) {
-            for (int s = 0; s < kS1Ring; ++s) mbar_init(&full[s], 1);
-            fence_mbar_init();
-            // The prefetch cursor starts p.pf slots past the ring's first fill.
-            for (int s = 0; s < kS1Ring; ++s) {
-                if (!advance(cc_pf)) break;
-                ++cc_pf.pq;
+        int pr_row = -1, pr_q = 0;
+        while (!pr_done) {
+            if (cg >= ce) {
+                if (!have_next) claim_next(ne);
+                // Move to the run claimed ahead (its atomic result is first needed here),
+                // and claim the one after it.
+                cg = ng0;
+                ce = min(ng0 + nc, ne);
+                have_next = false;
+                if (cg >= ne) {
+                    pr_done = true;
+                    break;
+                }
+                claim_next(ne - ce);
+                const long long su = cg / U;
+                ct = (int)(cg - su * U);
+                cseg = (int)(su / p.B);
+                crow = (int)(su - (long long)cseg * p.B);
             }
-            for (int s = 0; s < p.pf; ++s) prefetch_next();
-            for (int s = 0; s < kS1Ring; ++s) issue();
-        }
-        __syncwarp();
-    }
-    // With a history, this kernel is a programmatic dependent of the penalty prep: the
-    // first slots are in flight; the penalty lists are read only after this wait.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-
-    uint32_t cn = 0;  // slots consumed by this warp (ring position and phase)
-    bool timed_out = false;
-    for (int j = 0; j < npieces; ++j) {
-        const int b = b_first + j;
-        const T* row = (const T*)p.logits + (int64_t)b * p.stride;
-        const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
-        const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-        int q0, q1;
-        warp_slots(j, q0, q1);
-        int pjp = npen > 0 ? lower_bound_i32(pid, npen, (int64_t)q0 * SE) : 0;
-        uint32_t* rtp = p.row_tau + (size_t)b * kTauStride;
-        uint32_t rtau = ld_relaxed_u32(rtp);
-        uint32_t rtau_next = rtau;
-        uint32_t wcnt = 0u, since = 0u;
-        const int item = (int)blockIdx.x * p.flat_pmax + j;
-        uint2* out = p.cand + (size_t)item * p.cand_cap;
-        const uint32_t cap = (uint32_t)p.cand_cap;
-        const uint32_t gbase0 = (uint32_t)p.vocab_offset;
-
-        // Slot q of the row: waits for its bulk copy (or copies it with plain loads), fills
-        // the row tail, masks the penalised ids, and loads the lane's group into registers.
-        // The slot stays staged until release().
-        auto stage = [&](int q, uint4 (&v)[8]) -> const unsigned char* {
-            S1_T0(t_st);
-            const int64_t start = (int64_t)q * SE;
-            const int n = (int)min((int64_t)SE, (int64_t)p.V - start);
-            unsigned char* slotp = ring + (cn % kS1Ring) * kS1SlotBytes;
-            T* sl = (T*)slotp;
-            if constexpr (TMA) {
-                if (!mbar_wait_bounded(&full[cn % kS1Ring], (cn / kS1Ring) & 1u)) timed_out = true;
-                const int n_tma = (int)((((uint32_t)n * (uint32_t)sizeof(T)) & ~15u) / sizeof(T));
-                // Row tail: the elements past the copy's 16-byte multiple are read directly;
-                // positions past the row hold NaN (no element).
-                for (int i = n_tma + lane; i < SE; i += 32) sl[i] = i < n ? row[start + i] : nan_bits<T>();
-            } else {
-                for (int i = lane; i < SE; i += 32) sl[i] = i < n ? row[start + i] : nan_bits<T>();
-            }
-            if (npen > 0) {
-                // Penalised ids leave stage 1 (they re-enter with their penalised values in
-                // the finish kernel).
-                for (;;) {
-                    const int jj = pjp + lane;
-                    const bool in = jj < npen && pid[jj] < start + n;
-                    if (in) sl[pid[jj] - start] = nan_bits<T>();
-                    const unsigned m = __ballot_sync(FULL, in);
-                    pjp += __popc(m);
-                    if (m != FULL) break;
+            const int q = cseg * U + ct;
+            const int r = crow;
+            ++cg;
+            if (++ct == U) {
+                ct = 0;
+                if (++crow == p.B) {
+                    crow = 0;
+                    ++cseg;
                 }
             }
-            __syncwarp();
+            if (q < ng) {
+                pr_row = r;
+                pr_q = q;
+                break;
+            }
+        }
+        const int s = (int)(pn % kS1Ring);
+        if (pr_done) {
+            wq[2 * s] = -1;  // no more work
+            mbar_arrive(&full[s]);
+        } else {
+            const int64_t e0 = (int64_t)pr_q * SE;
+            const int n = (int)min((int64_t)SE, (int64_t)p.V - e0);
+            const uint32_t bytes = ((uint32_t)n * (uint32_t)sizeof(T)) & ~15u;
+            wq[2 * s] = pr_row;
+            wq[2 * s + 1] = pr_q;
+            if (TMA && bytes) {
+                mbar_arrive_expect_tx(&full[s], bytes);
+                tma_load_1d(ring + s * kS1SlotBytes, (const T*)p.logits + (int64_t)pr_row * p.stride + e0, bytes,
+                            &full[s]);
+            } else {
+                mbar_arrive(&full[s]);
+            }
+        }
+        ++pn;
+    };
+    if (lane == 0) {
+        for (int s = 0; s < kS1Ring; ++s) mbar_init(&full[s], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    // With a history, this kernel is a programmatic dependent of the penalty prep; the
+    // penalty lists are read only after this wait (a no-op for an ordinary launch). The
+    // claim counter is reset by the previous call's finish kernel, so claims come after.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (lane == 0)
+        for (int s = 0; s < kS1Ring; ++s) issue();
+    __syncwarp();
+
+    uint32_t cn = 0;  // slots consumed (ring position and phase)
+    bool timed_out = false;
+    // Current row of the consumer (-1: none yet).
+    int row = -1;
+    const T* rowp = nullptr;
+    int npen = 0, pjp = 0;
+    const int32_t* pid = nullptr;
+    uint32_t* rtp = nullptr;
+    uint32_t* rh = nullptr;  // the row's histogram
+    uint2* out = nullptr;
+    uint32_t* rcnt = nullptr;
+    const uint32_t cap = (uint32_t)p.cand_cap;
+    uint32_t rtau = 0u, rtau_next = 0u, lbound = 0u, wcnt = 0u, since = 0u;
+    // Asynchronous bound raise: 0 idle, 1 group counts in flight, 2 bin counts in flight.
+    // The raise keeps its row's pointers, so it completes after the warp moves on.
+    int rs_state = 0;
+    uint2 rs_g = make_uint2(0u, 0u), rs_h = make_uint2(0u, 0u);
+    int rs_grp = 0;
+    uint32_t rs_above = 0u;
+    const uint32_t* rs_rh = nullptr;
+    uint32_t* rs_rtp = nullptr;
+
+    // Writes the region entries at or above tmin to the row's list; empties the region.
+    auto flush_region = [&](uint32_t tmin) {
+        S1_ADD(10, 1);
+        for (uint32_t i0 = 0; i0 < wcnt; i0 += 32) {
+            const uint32_t i = i0 + lane;
+            uint32_t k = 0u, ix = 0u;
+            bool keep = false;
+            if (i < wcnt) {
+                k = rkey[i];
+                ix = ridx[i];
+                keep = k >= tmin;
+            }
+            const unsigned m = __ballot_sync(FULL, keep);
+            if (m) {
+                uint32_t base = 0u;
+                if (lane == 0) base = atomicAdd(rcnt, (uint32_t)__popc(m));
+                base = __shfl_sync(FULL, base, 0);
+                const uint32_t pos = base + __popc(m & lanemask_lt());
+                if (keep && pos < cap) out[pos] = make_uint2(k, ix);
+            }
+        }
+        __syncwarp();
+        wcnt = 0u;
+    };
+    auto cur_bound = [&]() -> uint32_t { return max(rtau, lbound); };
+    // Advances the asynchronous raise by one step (called once per slot).
+    auto raise_step = [&]() {
+        if (rs_state == 1) {
+            const uint32_t s = warp_suffix_sum(rs_g.x + rs_g.y);  // counts in groups >= 2 * lane
+            const unsigned m0 = __ballot_sync(FULL, s >= (uint32_t)K);
+            if (m0 == 0u) {
+                rs_state = 0;
+                return;
+            }
+            const unsigned m1 = __ballot_sync(FULL, s - rs_g.x >= (uint32_t)K);
+            const int l0 = 31 - __clz((int)m0);
+            const int hi = (int)((m1 >> l0) & 1u);
+            rs_grp = 2 * l0 + hi;
+            const uint32_t s_l0 = __shfl_sync(FULL, s, l0);
+            const uint32_t g0_l0 = __shfl_sync(FULL, rs_g.x, l0);
+            const uint32_t s_next = __shfl_sync(FULL, s, (l0 + 1) & 31);
+            rs_above = hi ? (l0 < 31 ? s_next : 0u) : s_l0 - g0_l0;  // counts in groups > grp
+            rs_h = ld_relaxed_v2(rs_rh + rs_grp * 64 + 2 * lane);
+            rs_state = 2;
+        } else if (rs_state == 2) {
+            const uint32_t t = warp_suffix_sum(rs_h.x + rs_h.y) + rs_above;
+            const unsigned n0 = __ballot_sync(FULL, t >= (uint32_t)K);
+            uint32_t edge = (uint32_t)rs_grp << 26;  // the group qualified, its bins not yet
+            if (n0 != 0u) {
+                const unsigned n1 = __ballot_sync(FULL, t - rs_h.x >= (uint32_t)K);
+                const int j0 = 31 - __clz((int)n0);
+                edge = (uint32_t)(rs_grp * 64 + 2 * j0 + (int)((n1 >> j0) & 1u)) << 20;
+            }
+            if (rs_rtp == rtp) {
+                if (edge > rtau) {
+                    rtau = edge;
+                    if (lane == 0) atomicMax(rtp, edge);
+                }
+            } else if (lane == 0) {
+                atomicMax(rs_rtp, edge);
+            }
+            rs_state = 0;
+        }
+    };
+    auto raise_start = [&]() {
+        if (rs_state == 0) {
+            S1_ADD(9, 1);
+            rs_rh = rh;
+            rs_rtp = rtp;
+            rs_g = ld_relaxed_v2(rh + kTBins + 2 * lane);
+            rs_state = 1;
+        }
+    };
+    // Leaves the current row: the region entries at or above the warp's bound are written
+    // to the list and the bound is published.
+    auto leave_row = [&]() {
+        if (row < 0) return;
+        const uint32_t tb = cur_bound();
+        flush_region(tb);
+        if (lane == 0 && tb > rtau) atomicMax(rtp, tb);
+        row = -1;
+    };
+    auto enter_row = [&](int b) {
+        row = b;
+        rowp = (const T*)p.logits + (int64_t)b * p.stride;
+        npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+        pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
+        pjp = 0;
+        rtp = p.row_tau + (size_t)b * kTauStride;
+        rh = p.rhist + (size_t)b * kRowHistWords;
+        out = p.cand + (size_t)b * cap;
+        rcnt = p.row_cnt + b;
+        rtau = ld_relaxed_u32(rtp);
+        rtau_next = rtau;
+        lbound = 0u;
+        since = 0u;
+    };
+
+    int last_q = -2;
+    for (;;) {
+        // ---- stage the next slot of this warp's claimed sequence ----
+        S1_T0(t_st);
+        const int s = (int)(cn % kS1Ring);
+        unsigned char* slotp = ring + s * kS1SlotBytes;
+        T* sl = (T*)slotp;
+        if (!mbar_wait_bounded(&full[s], (cn / kS1Ring) & 1u)) {
+            timed_out = true;
+            break;
+        }
+        const int b = wq[2 * s], q = wq[2 * s + 1];
+        if (b < 0) break;  // no more units
+        const bool first = b != row || q != last_q + 1;  // first slot of a claimed unit
+        if (b != row) {
+            S1_T0(t_sw);
+            leave_row();
+            enter_row(b);
+            S1_T1(15, t_sw);
+        }
+        last_q = q;
+        const int64_t start = (int64_t)q * SE;
+        const int n = (int)min((int64_t)SE, (int64_t)p.V - start);
+        {
+            const int n_tma = TMA ? (int)((((uint32_t)n * (uint32_t)sizeof(T)) & ~15u) / sizeof(T)) : 0;
+            // Elements the bulk copy did not bring (row tail, or every element without bulk
+            // copies) are read directly; positions past the row hold NaN (no element).
+            for (int i = n_tma + lane; i < SE; i += 32) sl[i] = i < n ? rowp[start + i] : nan_bits<T>();
+        }
+        if (npen > 0) {
+            // Penalised ids leave stage 1 (they re-enter with their penalised values in the
+            // finish kernel). The ids are sorted and this warp's slots of a row ascend.
+            for (;;) {
+                const int jj = pjp + lane;
+                const bool below = jj < npen && pid[jj] < start;
+                const unsigned m = __ballot_sync(FULL, below);
+                pjp += __popc(m);
+                if (m != FULL) break;
+            }
+            for (;;) {
+                const int jj = pjp + lane;
+                const bool in = jj < npen && pid[jj] < start + n;
+                if (in) sl[pid[jj] - start] = nan_bits<T>();
+                const unsigned m = __ballot_sync(FULL, in);
+                pjp += __popc(m);
+                if (m != FULL) break;
+            }
+        }
+        __syncwarp();
+        uint4 v[8];
+        {
             const unsigned char* g = slotp + lane * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(g + ((c ^ sw) << 4));
-            S1_T1(0, t_st);
-            return slotp;
-        };
-        // Hands the staged slot back to the producer: its next bulk copy (and the L2
-        // prefetch further ahead) are issued behind the warp's reads of it.
-        auto release = [&]() {
-            __syncwarp();
-            if constexpr (TMA) {
-                if (lane == 0) {
-                    fence_proxy_async_smem();
-                    issue();
-                    prefetch_next();
-                }
-            }
-            ++cn;
-        };
-        // Writes the region entries at or above tmin to the piece's list; empties the region.
-        auto flush_region = [&](uint32_t tmin) {
-            S1_ADD(10, 1);
-            for (uint32_t i0 = 0; i0 < wcnt; i0 += 32) {
-                const uint32_t i = i0 + lane;
-                uint32_t k = 0u, ix = 0u;
-                bool keep = false;
-                if (i < wcnt) {
-                    k = rkey[i];
-                    ix = ridx[i];
-                    keep = k >= tmin;
-                }
-                const unsigned m = __ballot_sync(FULL, keep);
-                if (m) {
-                    uint32_t base = 0u;
-                    if (lane == 0) base = atomicAdd(s_cnt, (uint32_t)__popc(m));
-                    base = __shfl_sync(FULL, base, 0);
-                    const uint32_t pos = base + __popc(m & lanemask_lt());
-                    if (keep && pos < cap) out[pos] = make_uint2(k, ix);
-                }
-            }
-            __syncwarp();
-            wcnt = 0u;
-        };
-        auto raise = [&]() {
-            __syncwarp();
-            S1_ADD(9, 1);
-            const uint32_t t = hist_threshold(H, Gc, K);
-            if (lane == 0 && t > *s_T) {
-                atomicMax((uint32_t*)s_T, t);
-                if (t > rtau) atomicMax(rtp, t);
-            }
-        };
-        // Appends one candidate (key k, index ix) at region position pos and, when
-        // counting, counts it in the histogram unless it lies in the bound's own bin
-        // (such counts cannot raise the bound).
-        auto take = [&](uint32_t pos, uint32_t k, uint32_t ix, bool counting, uint32_t tbin, uint32_t& counted) {
-            rkey[pos] = k;
-            ridx[pos] = ix;
-            if (counting && (k >> 20) > tbin) {
-                atomicAdd(&H[k >> 20], 1u);
-                atomicAdd(&Gc[k >> 26], 1u);
-                ++counted;
-            }
-        };
-        // Filters one staged slot against the current bound. Few hot lanes: the warp
-        // tests each hot lane's group together, one element (fp32) or one pair (bf16) per
-        // lane, from shared memory. Many: each lane extracts its own candidates from its
-        // registers, testing only the chunks whose maximum reaches the bound.
-        auto filter = [&](const unsigned char* slotp, const uint4 (&v)[8], const float (&xq)[8], float lmax, int q,
-                          bool counting) {
-            S1_ADD(5, 1);
-            const uint32_t tg = max((uint32_t)*s_T, rtau);
-            const float thr = key_threshold(tg);
-            const bool hot = lmax >= thr;
-            unsigned hb = __ballot_sync(FULL, hot);
-            if (hb == 0u) return;
+        }
+        S1_T1(0, t_st);
+        S1_T0(t_rs);
+        rtau = max(rtau, rtau_next);  // the row bound is fetched one slot ahead
+        rtau_next = ld_relaxed_u32(rtp);
+        raise_step();
+        S1_T1(14, t_rs);
+        float xq[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) xq[c] = chunk_max<T>(v[c]);
+        const float lmax = fmaxf(fmax3f(fmax3f(xq[0], xq[1], xq[2]), fmax3f(xq[3], xq[4], xq[5]), xq[6]), xq[7]);
+        if (first && K <= 256 && __popc(__ballot_sync(FULL, lmax >= key_threshold(cur_bound()))) > kS1CoopLanes) {
+            // The row's bound would let many lanes through: add the K-th largest chunk
+            // maximum of this slot (distinct elements of the row) as a bound.
+            S1_T0(t_cnt);
+            uint32_t kk[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) kk[c] = xq[c] == xq[c] ? f2key(xq[c]) : 0u;
+            lbound = max(lbound, warp_kth_of_keys8(kk, K, wh));  // stays a bound of this row
+            S1_T1(3, t_cnt);
+        }
+
+        // ---- filter the slot against the bound ----
+        S1_ADD(5, 1);
+        const uint32_t tg = cur_bound();
+        const float thr = key_threshold(tg);
+        const bool hot = lmax >= thr;
+        unsigned hb = __ballot_sync(FULL, hot);
+        if (hb != 0u) {
             S1_T0(t_hot);
             S1_ADD(6, 1);
             S1_ADD(7, __popc(hb));
             const uint32_t tbin = tg >> 20;
-            const uint32_t gslot = gbase0 + (uint32_t)q * SE;
+            const uint32_t gslot = (uint32_t)p.vocab_offset + (uint32_t)start;
             uint32_t counted = 0u;
+            // Appends a candidate at region position pos and counts it in the row
+            // histogram unless it lies in the bound's own bin.
+            auto take = [&](uint32_t pos, uint32_t k, uint32_t ix) {
+                rkey[pos] = k;
+                ridx[pos] = ix;
+                if ((k >> 20) > tbin) {
+                    red_add_u32(rh + (k >> 20), 1u);
+                    red_add_u32(rh + kTBins + (k >> 26), 1u);
+                    ++counted;
+                }
+            };
+            // The same count for a warp-uniform step: lanes with equal bins add together.
+            auto count_step = [&](bool valid, uint32_t k) {
+                const bool cnt_it = valid && (k >> 20) > tbin;
+                const unsigned cm = __ballot_sync(FULL, cnt_it);
+                if (cm == 0u) return;
+                const unsigned same = __match_any_sync(FULL, cnt_it ? (k >> 20) : 0xFFFFFFFFu);
+                if (cnt_it && (__ffs((int)same) - 1) == lane) red_add_u32(rh + (k >> 20), (uint32_t)__popc(same));
+                const unsigned sameg = __match_any_sync(FULL, cnt_it ? (k >> 26) : 0xFFFFFFFFu);
+                if (cnt_it && (__ffs((int)sameg) - 1) == lane) red_add_u32(rh + kTBins + (k >> 26), (uint32_t)__popc(sameg));
+                counted += (uint32_t)(cnt_it ? 1 : 0);
+            };
+            auto put = [&](uint32_t pos, uint32_t k, uint32_t ix) {
+                rkey[pos] = k;
+                ridx[pos] = ix;
+            };
             if (__popc(hb) <= kS1CoopLanes) {
                 while (hb) {
                     const int h = __ffs((int)hb) - 1;
@@ -3220,26 +2472,31 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
                         const float xv = reinterpret_cast<const float*>(slotp)[h * 32 + lane];
                         const bool pass = xv >= thr;
                         const unsigned m = __ballot_sync(FULL, pass);
-                        if (pass)
-                            take(wcnt + __popc(m & lanemask_lt()), f2key(xv), gslot + (uint32_t)(h * 32 + lane),
-                                 counting, tbin, counted);
+                        const uint32_t k = f2key(xv);
+                        if (pass) put(wcnt + __popc(m & lanemask_lt()), k, gslot + (uint32_t)(h * 32 + lane));
+                        count_step(pass, k);
                         wcnt += (uint32_t)__popc(m);
                         S1_ADD(8, __popc(m));
                     } else {
                         const uint32_t w = reinterpret_cast<const uint32_t*>(slotp)[h * 32 + lane];
-                        const float a = bf_lo(w), b = bf_hi(w);
-                        const bool pa = a >= thr, pb = b >= thr;
+                        const float a = bf_lo(w), bb = bf_hi(w);
+                        const bool pa = a >= thr, pb = bb >= thr;
                         const unsigned ma = __ballot_sync(FULL, pa), mb = __ballot_sync(FULL, pb);
                         const uint32_t pos = wcnt + __popc(ma & lanemask_lt()) + __popc(mb & lanemask_lt());
                         const uint32_t ix = gslot + (uint32_t)(h * 64 + 2 * lane);
-                        if (pa) take(pos, f2key(a), ix, counting, tbin, counted);
-                        if (pb) take(pos + (pa ? 1u : 0u), f2key(b), ix + 1u, counting, tbin, counted);
+                        const uint32_t ka = f2key(a), kb = f2key(bb);
+                        if (pa) put(pos, ka, ix);
+                        if (pb) put(pos + (pa ? 1u : 0u), kb, ix + 1u);
+                        count_step(pa, ka);
+                        count_step(pb, kb);
                         wcnt += (uint32_t)(__popc(ma) + __popc(mb));
                         S1_ADD(8, __popc(ma) + __popc(mb));
                     }
                 }
             } else {
-                uint64_t pm = 0ull;  // this lane's elements at or above the bound
+                // Bit i of pm: element i of this lane's group reaches the bound (only chunks
+                // whose maximum reaches it are tested).
+                uint64_t pm = 0ull;
                 if (hot) {
 #pragma unroll
                     for (int c = 0; c < 8; ++c) {
@@ -3247,7 +2504,7 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
                             uint32_t cm = 0u;
 #pragma unroll
                             for (int e = 0; e < CE; ++e) cm |= (chunk_elem<T>(v[c], e) >= thr ? 1u : 0u) << e;
-                            pm |= (uint64_t)cm << (c * CE);
+                            pm |= (uint64_t)cm << ((c ^ sw) * CE);
                         }
                     }
                 }
@@ -3265,124 +2522,68 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
                 uint32_t pos;
                 if (direct) {
                     uint32_t base = 0u;
-                    if (lane == 0) base = atomicAdd(s_cnt, total);
+                    if (lane == 0) base = atomicAdd(rcnt, total);
                     pos = __shfl_sync(FULL, base, 0) + incl - cnt;
                 } else {
                     pos = wcnt + incl - cnt;
                 }
+                // Each lane writes its own candidates, re-read from the staged slot.
+                const T* grp = reinterpret_cast<const T*>(slotp) + lane * GE;
                 const uint32_t gb = gslot + (uint32_t)lane * GE;
-                if (cnt) {
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) {
-                        const uint32_t cm = (uint32_t)(pm >> (c * CE)) & ((1u << CE) - 1u);
-                        if (cm) {
-#pragma unroll
-                            for (int e = 0; e < CE; ++e) {
-                                if ((cm >> e) & 1u) {
-                                    const uint32_t k = f2key(chunk_elem<T>(v[c], e));
-                                    const uint32_t ix = gb + (uint32_t)((c ^ sw) * CE + e);
-                                    if (direct) {
-                                        if (pos < cap) out[pos] = make_uint2(k, ix);
-                                        if (counting && (k >> 20) > tbin) {
-                                            atomicAdd(&H[k >> 20], 1u);
-                                            atomicAdd(&Gc[k >> 26], 1u);
-                                            ++counted;
-                                        }
-                                    } else {
-                                        take(pos, k, ix, counting, tbin, counted);
-                                    }
-                                    ++pos;
-                                }
-                            }
+                while (pm) {
+                    const int i = __ffsll((long long)pm) - 1;
+                    pm &= pm - 1ull;
+                    const uint32_t k = f2key(to_f(grp[i]));
+                    const uint32_t ix = gb + (uint32_t)i;
+                    if (direct) {
+                        if (pos < cap) out[pos] = make_uint2(k, ix);
+                        if ((k >> 20) > tbin) {
+                            red_add_u32(rh + (k >> 20), 1u);
+                            red_add_u32(rh + kTBins + (k >> 26), 1u);
+                            ++counted;
                         }
+                    } else {
+                        take(pos, k, ix);
                     }
+                    ++pos;
                 }
                 if (!direct) wcnt += total;
                 S1_ADD(8, total);
             }
             since += __reduce_add_sync(FULL, counted);
-            if (since >= 8u) {
+            if (since >= (uint32_t)kS1RaiseEvery) {
                 since = 0u;
-                raise();
+                raise_start();
             }
             S1_T1(1, t_hot);
-        };
-        auto maxima = [&](const uint4 (&v)[8], float (&xq)[8]) -> float {
-#pragma unroll
-            for (int c = 0; c < 8; ++c) xq[c] = chunk_max<T>(v[c]);
-            return fmaxf(fmax3f(fmax3f(xq[0], xq[1], xq[2]), fmax3f(xq[3], xq[4], xq[5]), xq[6]), xq[7]);
-        };
+        }
 
-        // Counting: each warp's first slot of the piece (already in flight) is counted
-        // before anything is filtered, so the bound starts near the K-th key of the
-        // CTA's first slots.
-        uint4 v[8];
-        float xq[8];
-        float lmax = __uint_as_float(0x7FC00000u);
-        const unsigned char* slotp = nullptr;
-        S1_T0(t_cnt);
-        if (q0 < q1) {
-            slotp = stage(q0, v);
-            lmax = maxima(v, xq);
-            if (K > 256) {
-#pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    if (xq[c] == xq[c]) {
-                        const uint32_t k = f2key(xq[c]);
-                        atomicAdd(&H[k >> 20], 1u);
-                        atomicAdd(&Gc[k >> 26], 1u);
-                    }
-                }
-            } else if (lmax == lmax) {
-                const uint32_t k = f2key(lmax);
-                atomicAdd(&H[k >> 20], 1u);
-                atomicAdd(&Gc[k >> 26], 1u);
-            }
-        }
-        __syncthreads();
-        raise();
-        S1_T1(3, t_cnt);
-        if (q0 < q1) {
-            filter(slotp, v, xq, lmax, q0, false);  // its maxima are counted already
-            release();
-            for (int q = q0 + 1; q < q1; ++q) {
-                rtau = rtau_next;  // the row bound is fetched one slot ahead
-                rtau_next = ld_relaxed_u32(rtp);
-                slotp = stage(q, v);
-                lmax = maxima(v, xq);
-                filter(slotp, v, xq, lmax, q, true);
-                release();
-            }
-        }
-        // Piece end: the final bound from the complete histogram; every region entry at
-        // or above it leaves.
-        S1_T0(t_pe);
-        __syncthreads();
-        if (warp == 0) {
-            const uint32_t t = hist_threshold(H, Gc, K);
-            if (lane == 0) sh[2] = max(max((uint32_t)*s_T, t), ld_relaxed_u32(rtp));
-        }
-        __syncthreads();
-        const uint32_t tfin = sh[2];
-        flush_region(tfin);
-        __syncthreads();
-        if (tid == 0) {
-            S1_ADD(11, *s_cnt);
-            p.chunk_info[item] = make_uint2(*s_cnt, 0u);
-            p.item_tau[item] = tfin;
-            if (tfin > ld_relaxed_u32(rtp)) atomicMax(rtp, tfin);
-            sh[0] = 0u;
-            sh[1] = 0u;
-        }
-        for (int i = tid; i < kTBins + kTGroups; i += kS1Threads) H[i] = 0u;
-        __syncthreads();
-        S1_T1(2, t_pe);
-    }
-    if (__any_sync(FULL, timed_out) && lane == 0) atomicExch(p.err, kErrTimeout);
-    if constexpr (TMA) {
+        // ---- release the slot: its next bulk copy goes behind the warp's reads ----
+        S1_T0(t_rel);
         __syncwarp();
-        if (lane == 0)
-            for (int s = 0; s < kS1Ring; ++s) mbar_inval(&full[s]);
+        if (lane == 0) {
+            fence_proxy_async_smem();
+            issue();
+        }
+        ++cn;
+        S1_T1(13, t_rel);
+    }
+    leave_row();
+    const bool any_timeout = __any_sync(FULL, timed_out);
+    if (any_timeout && lane == 0) atomicExch(p.err, kErrTimeout);
+    __syncwarp();
+    // Every copy this warp issued has been consumed (the positions after the end-of-work
+    // marker hold markers too, which complete on arrival), so the barriers are idle.
+    if (!any_timeout && lane == 0)
+        for (int s2 = 0; s2 < kS1Ring; ++s2) mbar_inval(&full[s2]);
+    // The last warp of the grid to finish resets the claim counter for the next call:
+    // all claims of this call precede every warp's fence and finish count.
+    if (lane == 0) {
+        __threadfence();
+        if (atomicAdd(&p.unit_next[1], 1ull) == (unsigned long long)gridDim.x * kS1Warps - 1ull) {
+            atomicExch(&p.unit_next[0], 0ull);
+            atomicExch(&p.unit_next[1], 0ull);
+        }
     }
     S1_T1(4, t_all);
     S1_FLUSH();
@@ -3682,8 +2883,15 @@ __global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
     // and its writes are visible (a no-op for an ordinary launch).
     asm volatile("griddepcontrol.wait;" ::: "memory");
     VDXS_T0(t_fin);
-    finish_row<T>(p, blockIdx.x, region, hist, sh);
-    if (threadIdx.x == 0 && p.row_tau) p.row_tau[(size_t)blockIdx.x * kTauStride] = 0u;  // ready for the next launch
+    const int b = blockIdx.x;
+    finish_row<T>(p, b, region, hist, sh);
+    // The row's stage-1 state is ready for the next call: bound, list count, histogram.
+    if (threadIdx.x == 0) {
+        p.row_tau[(size_t)b * kTauStride] = 0u;
+        p.row_cnt[b] = 0u;
+    }
+    uint4* rh4 = reinterpret_cast<uint4*>(p.rhist + (size_t)b * kRowHistWords);
+    for (int i = threadIdx.x; i < kRowHistWords / 4; i += NT) rh4[i] = make_uint4(0u, 0u, 0u, 0u);
     VDXS_T1(5, t_fin);
 }
 
@@ -4028,26 +3236,27 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         }
     }
     if (K <= kMaxTopK) {
-        // Stream path: persistent stage 1 (one 16-warp CTA per SM) + one finish CTA per row.
+        // Stream path: stage 1 on one 16-warp CTA per SM (warps claim row units) + one
+        // finish CTA per row.
         int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         const int SE = esz == 4 ? s1_slot_elems<float>() : s1_slot_elems<uint16_t>();
         const int ng = (int)((V + SE - 1) / SE);
-        const long long ngt = (long long)a.B * ng;
-        // Flat partition of the B x ng slots over at most one CTA per SM, at least one slot
-        // per warp.
-        const int grid = (int)std::max<long long>(1, std::min<long long>((long long)sms, ngt / kS1Warps));
-        const long long gmax_cta = (ngt + grid - 1) / grid, gmin_cta = std::max<long long>(1, ngt / grid);
-        const int pmax = (int)((gmax_cta - 1) / ng + 2);            // pieces per CTA
-        const int ipr = (int)((ng + gmin_cta - 1) / gmin_cta + 1);  // pieces per row
-        // A piece's list holds its elements at or above the piece's final bound: for small
-        // top_k about the row's share above the bound's bin edge; for large top_k also the
-        // candidates taken while the bound was still rising. A longer list is incomplete
-        // and its row takes the finish kernel's exact fallback.
-        const int cc = K <= 128 ? (int)std::max<int64_t>(std::max(256, 2 * K), std::min<int64_t>(8 * K, 16384 / ipr))
-                                : (int)std::min<int64_t>(std::max<int64_t>(16LL * K, 8192), (int64_t)ng * SE);
-        const int gather = std::max(8192, K + pen_stride);
+        // Row segments of 16 slots (64 KB fp32); the kernel claims them in runs that shrink
+        // near the end of the work.
+        const int U = std::min(ng, 16);
+        const long long units = (long long)a.B * ((ng + U - 1) / U);
+        if (units >= (1LL << 31)) {
+            if (err) *err = "batch x vocab too large for the stream path";
+            return cudaErrorInvalidValue;
+        }
+        // A row's list holds every element at or above the row's final bound, plus
+        // candidates taken while the bounds were still rising (about K times the log of
+        // the row's units for random orders, more for rows with many ties at the bound).
+        // A longer list is incomplete and its row takes the finish kernel's exact fallback.
+        const int cc = (int)std::min<int64_t>(std::max<int64_t>(32LL * K, 4096), (int64_t)ng * SE);
+        const int gather = std::max(K <= 128 ? 4096 : 8192, K + pen_stride);
         size_t s2 = std::max(stage2_bytes(K, gather + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
         s2 += kHeadBytes;
         const size_t s1 = s1_smem_bytes();
@@ -4056,18 +3265,17 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
             return cudaErrorInvalidValue;
         }
         plan->chunk = 0;
-        plan->nchunks = ipr;
-        plan->nspans = ipr;
+        plan->nchunks = 1;
+        plan->nspans = 1;
         plan->span = 1;
         plan->elems = 0;
         plan->stream = true;
         plan->cand_cap = cc;
         plan->gather_cap = gather;
-        plan->grid = grid;
-        plan->flat_ng = ng;
-        plan->flat_ngt = ngt;
-        plan->flat_pmax = pmax;
-        plan->items = (long long)grid * pmax;
+        plan->grid = (int)std::max<long long>(1, std::min<long long>((long long)sms, (units + kS1Warps - 1) / kS1Warps));
+        plan->slots = ng;
+        plan->unit_slots = U;
+        plan->items = a.B;
         plan->smem = s1;
         plan->smem2 = align16(s2);
         return cudaSuccess;
@@ -4127,8 +3335,16 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
         if ((e = grow(&ws.cand, &ws.cand_cap, (size_t)plan.items * (size_t)plan.cand_cap, false, stream)) !=
             cudaSuccess)
             return e;
-        if ((e = grow(&ws.chunk_info, &ws.chunk_info_cap, (size_t)plan.items, false, stream)) != cudaSuccess) return e;
-        if ((e = grow(&ws.item_tau, &ws.item_tau_cap, (size_t)plan.items, false, stream)) != cudaSuccess) return e;
+        if (plan.stream) {
+            // Per-row histograms and list counts, and the claim counter: zero once here, then
+            // left at zero by every call (finish kernel, last stage-1 warp).
+            if ((e = grow(&ws.rhist, &ws.rhist_cap, B * (size_t)kRowHistWords, true, stream)) != cudaSuccess) return e;
+            if ((e = grow(&ws.row_cnt, &ws.row_cnt_cap, B, true, stream)) != cudaSuccess) return e;
+            if (!ws.unit_next) {
+                size_t c2 = 0;
+                if ((e = grow(&ws.unit_next, &c2, 2, true, stream)) != cudaSuccess) return e;
+            }
+        }
     } else {
         // fmax: [B*nch] max keys + [B*nch] probability max keys; fsum: [B*nch] sums + [B*nch] stats.
         size_t cap_a = ws.full_cap, cap_b = ws.full_cap;
@@ -4201,10 +3417,13 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
     if (a.path != kFull) {
         w.cand = (uint2*)take((size_t)plan.items * (size_t)plan.cand_cap * sizeof(uint2));
         w.cand_cap = (size_t)plan.items * (size_t)plan.cand_cap;
-        w.chunk_info = (uint2*)take((size_t)plan.items * sizeof(uint2));
-        w.chunk_info_cap = (size_t)plan.items;
-        w.item_tau = (uint32_t*)take((size_t)plan.items * sizeof(uint32_t));
-        w.item_tau_cap = (size_t)plan.items;
+        if (plan.stream) {
+            w.rhist = (uint32_t*)take(B * (size_t)kRowHistWords * sizeof(uint32_t));
+            w.rhist_cap = B * (size_t)kRowHistWords;
+            w.row_cnt = (uint32_t*)take(B * sizeof(uint32_t));
+            w.row_cnt_cap = B;
+            w.unit_next = (unsigned long long*)take(2 * sizeof(unsigned long long));
+        }
     } else {
         w.fmax = (uint32_t*)take(2 * B * nch * sizeof(uint32_t));
         w.fsum = (double*)take(2 * B * nch * sizeof(double));
@@ -4230,13 +3449,20 @@ cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream) {
         return e;
     if (ws.row_tau && (e = cudaMemsetAsync(ws.row_tau, 0, sizeof(uint32_t) * ws.row_tau_cap, stream)) != cudaSuccess)
         return e;
+    if (ws.rhist && (e = cudaMemsetAsync(ws.rhist, 0, sizeof(uint32_t) * ws.rhist_cap, stream)) != cudaSuccess)
+        return e;
+    if (ws.row_cnt && (e = cudaMemsetAsync(ws.row_cnt, 0, sizeof(uint32_t) * ws.row_cnt_cap, stream)) != cudaSuccess)
+        return e;
+    if (ws.unit_next && (e = cudaMemsetAsync(ws.unit_next, 0, 2 * sizeof(unsigned long long), stream)) != cudaSuccess)
+        return e;
     return cudaSuccess;
 }
 
 void free_workspace(Workspace& ws) {
     cudaFree(ws.cand);
-    cudaFree(ws.chunk_info);
-    cudaFree(ws.item_tau);
+    cudaFree(ws.rhist);
+    cudaFree(ws.row_cnt);
+    cudaFree(ws.unit_next);
     cudaFree(ws.row_counter);
     cudaFree(ws.row_tau);
     cudaFree(ws.pen_ids);
@@ -4276,12 +3502,11 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.cand = ws.cand;
     p.cand_cap = plan.cand_cap;
     p.gather_cap = plan.gather_cap;
-    p.flat_ng = plan.flat_ng;
-    p.flat_grid = plan.grid;
-    p.flat_pmax = plan.flat_pmax;
-    p.flat_ngt = plan.flat_ngt;
-    p.chunk_info = ws.chunk_info;
-    p.item_tau = ws.item_tau;
+    p.flat_ng = plan.slots;
+    p.unit_slots = plan.unit_slots;
+    p.rhist = ws.rhist;
+    p.row_cnt = ws.row_cnt;
+    p.unit_next = ws.unit_next;
     p.row_counter = ws.row_counter;
     p.row_tau = ws.row_tau;
     p.err = ws.err;
@@ -4301,10 +3526,6 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.vocab_offset = a.vocab_offset;
     p.local_emit = a.local_emit ? 1 : 0;
     p.emit_out = ws.shard_send;
-    p.pf = kS1Prefetch;
-#ifdef VDXS_TIMING
-    if (const char* e = getenv("VDXS_PF")) p.pf = atoi(e);
-#endif
     return p;
 }
 
