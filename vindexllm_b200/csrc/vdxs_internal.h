@@ -35,6 +35,8 @@ struct Workspace {
     int32_t* pen_ids = nullptr;     // [rows * pen_stride] sorted unique history ids
     float* pen_vals = nullptr;      // [rows * pen_stride] penalised values
     int32_t* pen_cnt = nullptr;     // [rows]
+    uint32_t* pen_bits = nullptr;   // [rows * ceil(vocab / 32)] stream path penalised-id bitmaps, self-resetting
+    size_t pen_bits_cap = 0;
     size_t pen_cap = 0;             // rows * pen_stride
     size_t pen_rows_cap = 0;
     uint32_t* fmax = nullptr;       // [rows * nchunks] full path: chunk max keys

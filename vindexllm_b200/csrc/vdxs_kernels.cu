@@ -93,6 +93,8 @@ struct KParams {
     const float* pen_vals;
     const int32_t* pen_cnt;
     int pen_stride;
+    uint32_t* pen_bits;  // stream path: [B][pen_words] bitmap of the penalised ids (cleared by finish)
+    int pen_words;
     // workspace
     uint2* cand;        // stage-1 (key, index) candidates (stream path: [B][cand_cap], one list per row)
     int cand_cap;       // candidates a list may hold
@@ -643,7 +645,8 @@ __global__ void __launch_bounds__(NT) penalty_prep_kernel(const T* logits, int64
                                                           int64_t hist_stride,
                                                           const int32_t* hist_count, float penalty,
                                                           int32_t* pen_ids, float* pen_vals,
-                                                          int32_t* pen_cnt, int pen_stride) {
+                                                          int32_t* pen_cnt, int pen_stride, uint32_t* pen_bits,
+                                                          int pen_words) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     int32_t* a = (int32_t*)smem_raw;  // [P2]
     __shared__ int sh[NWARPS + 1];
@@ -700,6 +703,7 @@ __global__ void __launch_bounds__(NT) penalty_prep_kernel(const T* logits, int64
         }
         pen_ids[(int64_t)b * pen_stride + off] = id;
         pen_vals[(int64_t)b * pen_stride + off] = v;
+        if (pen_bits) atomicOr(&pen_bits[(int64_t)b * pen_words + (id >> 5)], 1u << (id & 31));
         ++off;
     }
     if (tid == 0) pen_cnt[b] = total;
@@ -2140,22 +2144,32 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
     // Slot enumeration, column-major over row segments: position g is segment
     // g / (B * U), row (g / U) % B, slot (g / (B * U)) * U + g % U of that row (positions past
     // the row's last slot are skipped).
-    const long long ne = (long long)p.B * nseg * U;
-    const long long nwarps = (long long)gridDim.x * kS1Warps;
+    const uint32_t ne = (uint32_t)p.B * (uint32_t)nseg * (uint32_t)U;  // below 2^31 (host check)
+    const uint32_t nwarps = gridDim.x * (uint32_t)kS1Warps;
 
     // Producer (lane 0): claims runs of positions and issues the ring's bulk copies in order.
     // Runs are U positions long until the remaining work nears two runs per warp, then
     // shrink to one slot, so that warps run out of work together.
-    long long cg = 0, ce = 0;  // the producer's claimed run [cg, ce)
-    long long ng0 = 0, nc = 0;  // the next run, claimed one run ahead: start (atomic result) and length
+    uint32_t cg = 0u, ce = 0u;   // the producer's claimed run [cg, ce)
+    uint32_t ng0 = 0u, nc = 0u;  // the next run, claimed one run ahead: start (atomic result) and length
     bool have_next = false;
-    uint32_t pn = 0;            // copies issued
+    uint32_t pn = 0;             // copies issued
     bool pr_done = false;
-    auto claim_next = [&](long long left_est) {
-        nc = max(1LL, min((long long)U, left_est / (2 * nwarps)));
-        ng0 = (long long)atomicAdd((unsigned long long*)p.unit_next, (unsigned long long)nc);
+    // Every warp's first run is assigned statically (warp w takes [w * c0, (w + 1) * c0)),
+    // so the launch does not start with every warp claiming from one counter; claims from
+    // the counter start after those runs.
+    const uint32_t c0 = max(1u, min((uint32_t)U, ne / (2u * nwarps)));
+    const uint32_t base = c0 * nwarps;
+    auto claim_next = [&](uint32_t left_est) {
+        nc = max(1u, min((uint32_t)U, left_est / (2u * nwarps)));
+        ng0 = base + (uint32_t)atomicAdd((unsigned long long*)p.unit_next, (unsigned long long)nc);
         have_next = true;
     };
+    {
+        ng0 = (blockIdx.x * (uint32_t)kS1Warps + (threadIdx.x >> 5)) * c0;
+        nc = c0;
+        have_next = true;
+    }
     // Position of cg within the enumeration: segment, row and slot offset, advanced
     // incrementally (one division per run).
     int cseg = 0, crow = 0, ct = 0;
@@ -2174,10 +2188,10 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
                     break;
                 }
                 claim_next(ne - ce);
-                const long long su = cg / U;
-                ct = (int)(cg - su * U);
-                cseg = (int)(su / p.B);
-                crow = (int)(su - (long long)cseg * p.B);
+                const uint32_t su = cg / (uint32_t)U;
+                ct = (int)(cg - su * (uint32_t)U);
+                cseg = (int)(su / (uint32_t)p.B);
+                crow = (int)(su - (uint32_t)cseg * (uint32_t)p.B);
             }
             const int q = cseg * U + ct;
             const int r = crow;
@@ -2233,8 +2247,6 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
     // Current row of the consumer (-1: none yet).
     int row = -1;
     const T* rowp = nullptr;
-    int npen = 0, pjp = 0;
-    const int32_t* pid = nullptr;
     uint32_t* rtp = nullptr;
     uint32_t* rh = nullptr;  // the row's histogram
     uint2* out = nullptr;
@@ -2332,17 +2344,17 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
         if (lane == 0 && tb > rtau) atomicMax(rtp, tb);
         row = -1;
     };
+    // The bound of the row that the next staged slot belongs to, read one slot early.
+    int pref_row = -1;
+    uint32_t pref_tau = 0u;
     auto enter_row = [&](int b) {
         row = b;
         rowp = (const T*)p.logits + (int64_t)b * p.stride;
-        npen = p.pen_cnt ? p.pen_cnt[b] : 0;
-        pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
-        pjp = 0;
         rtp = p.row_tau + (size_t)b * kTauStride;
         rh = p.rhist + (size_t)b * kRowHistWords;
         out = p.cand + (size_t)b * cap;
         rcnt = p.row_cnt + b;
-        rtau = ld_relaxed_u32(rtp);
+        rtau = b == pref_row ? pref_tau : ld_relaxed_u32(rtp);
         rtau_next = rtau;
         lbound = 0u;
         since = 0u;
@@ -2355,11 +2367,21 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
         const int s = (int)(cn % kS1Ring);
         unsigned char* slotp = ring + s * kS1SlotBytes;
         T* sl = (T*)slotp;
+        // The slot's (row, slot) entry was written by lane 0 before it issued the copy, in an
+        // earlier iteration whose warp barriers order it before these reads: read it, and
+        // the penalised-id bitmap words of this lane's group, before waiting for the copy.
+        const int b = wq[2 * s], q = wq[2 * s + 1];
+        uint32_t pbits[GE / 32];
+#pragma unroll
+        for (int w = 0; w < GE / 32; ++w) {
+            const int wi = (int)(((int64_t)q * SE + lane * GE) >> 5) + w;
+            pbits[w] = (p.pen_bits && b >= 0 && wi < p.pen_words) ? __ldcg(p.pen_bits + (size_t)b * p.pen_words + wi)
+                                                                   : 0u;
+        }
         if (!mbar_wait_bounded(&full[s], (cn / kS1Ring) & 1u)) {
             timed_out = true;
             break;
         }
-        const int b = wq[2 * s], q = wq[2 * s + 1];
         if (b < 0) break;  // no more units
         const bool first = b != row || q != last_q + 1;  // first slot of a claimed unit
         if (b != row) {
@@ -2377,23 +2399,15 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
             // copies) are read directly; positions past the row hold NaN (no element).
             for (int i = n_tma + lane; i < SE; i += 32) sl[i] = i < n ? rowp[start + i] : nan_bits<T>();
         }
-        if (npen > 0) {
-            // Penalised ids leave stage 1 (they re-enter with their penalised values in the
-            // finish kernel). The ids are sorted and this warp's slots of a row ascend.
-            for (;;) {
-                const int jj = pjp + lane;
-                const bool below = jj < npen && pid[jj] < start;
-                const unsigned m = __ballot_sync(FULL, below);
-                pjp += __popc(m);
-                if (m != FULL) break;
-            }
-            for (;;) {
-                const int jj = pjp + lane;
-                const bool in = jj < npen && pid[jj] < start + n;
-                if (in) sl[pid[jj] - start] = nan_bits<T>();
-                const unsigned m = __ballot_sync(FULL, in);
-                pjp += __popc(m);
-                if (m != FULL) break;
+        // Penalised ids leave stage 1 (they re-enter with their penalised values in the
+        // finish kernel): NaN in the staged slot.
+#pragma unroll
+        for (int w = 0; w < GE / 32; ++w) {
+            uint32_t bits = pbits[w];
+            while (bits) {
+                const int i = __ffs((int)bits) - 1;
+                bits &= bits - 1u;
+                sl[lane * GE + w * 32 + i] = nan_bits<T>();
             }
         }
         __syncwarp();
@@ -2402,6 +2416,13 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
             const unsigned char* g = slotp + lane * 128;
 #pragma unroll
             for (int c = 0; c < 8; ++c) v[c] = *reinterpret_cast<const uint4*>(g + ((c ^ sw) << 4));
+        }
+        {
+            const int nb = wq[2 * (int)((cn + 1) % kS1Ring)];  // written before the last release
+            if (nb >= 0 && nb != b && nb != pref_row) {
+                pref_row = nb;
+                pref_tau = ld_relaxed_u32(p.row_tau + (size_t)nb * kTauStride);
+            }
         }
         S1_T1(0, t_st);
         S1_T0(t_rs);
@@ -2885,10 +2906,16 @@ __global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
     VDXS_T0(t_fin);
     const int b = blockIdx.x;
     finish_row<T>(p, b, region, hist, sh);
-    // The row's stage-1 state is ready for the next call: bound, list count, histogram.
+    // The row's stage-1 state is ready for the next call: bound, list count, histogram,
+    // penalised-id bitmap words.
     if (threadIdx.x == 0) {
         p.row_tau[(size_t)b * kTauStride] = 0u;
         p.row_cnt[b] = 0u;
+    }
+    if (p.pen_bits) {
+        const int npen = p.pen_cnt[b];
+        const int32_t* pid = p.pen_ids + (int64_t)b * p.pen_stride;
+        for (int j = threadIdx.x; j < npen; j += NT) p.pen_bits[(size_t)b * p.pen_words + (pid[j] >> 5)] = 0u;
     }
     uint4* rh4 = reinterpret_cast<uint4*>(p.rhist + (size_t)b * kRowHistWords);
     for (int i = threadIdx.x; i < kRowHistWords / 4; i += NT) rh4[i] = make_uint4(0u, 0u, 0u, 0u);
@@ -3247,7 +3274,7 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         // near the end of the work.
         const int U = std::min(ng, 16);
         const long long units = (long long)a.B * ((ng + U - 1) / U);
-        if (units >= (1LL << 31)) {
+        if (units * U >= (1LL << 31)) {
             if (err) *err = "batch x vocab too large for the stream path";
             return cudaErrorInvalidValue;
         }
@@ -3359,6 +3386,11 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
         if ((e = grow(&ws.pen_vals, &cap_b, B * ps, false, stream)) != cudaSuccess) return e;
         ws.pen_cap = std::min(cap_a, cap_b);
         if ((e = grow(&ws.pen_cnt, &ws.pen_rows_cap, B, false, stream)) != cudaSuccess) return e;
+        if (plan.stream) {
+            // Zero once; the finish kernel clears the words it set.
+            const size_t words = B * (size_t)((a.V + 31) / 32);
+            if ((e = grow(&ws.pen_bits, &ws.pen_bits_cap, words, true, stream)) != cudaSuccess) return e;
+        }
     }
     if (a.local_emit) {
         if ((e = grow(&ws.shard_send, &ws.shard_send_cap, B * (size_t)(a.K + 1), false, stream)) != cudaSuccess)
@@ -3434,6 +3466,11 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
         w.pen_ids = (int32_t*)take(B * ps * sizeof(int32_t));
         w.pen_vals = (float*)take(B * ps * sizeof(float));
         w.pen_cnt = (int32_t*)take(B * sizeof(int32_t));
+        if (plan.stream) {
+            const size_t words = B * (size_t)((a.V + 31) / 32);
+            w.pen_bits = (uint32_t*)take(words * sizeof(uint32_t));
+            w.pen_bits_cap = words;
+        }
         w.pen_cap = B * ps;
         w.pen_rows_cap = B;
     }
@@ -3455,6 +3492,8 @@ cudaError_t reset_device_state(Workspace& ws, cudaStream_t stream) {
         return e;
     if (ws.unit_next && (e = cudaMemsetAsync(ws.unit_next, 0, 2 * sizeof(unsigned long long), stream)) != cudaSuccess)
         return e;
+    if (ws.pen_bits && (e = cudaMemsetAsync(ws.pen_bits, 0, sizeof(uint32_t) * ws.pen_bits_cap, stream)) != cudaSuccess)
+        return e;
     return cudaSuccess;
 }
 
@@ -3463,6 +3502,7 @@ void free_workspace(Workspace& ws) {
     cudaFree(ws.rhist);
     cudaFree(ws.row_cnt);
     cudaFree(ws.unit_next);
+    cudaFree(ws.pen_bits);
     cudaFree(ws.row_counter);
     cudaFree(ws.row_tau);
     cudaFree(ws.pen_ids);
@@ -3498,6 +3538,10 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
         p.pen_vals = ws.pen_vals;
         p.pen_cnt = ws.pen_cnt;
         p.pen_stride = (int)std::min<int64_t>(a.hist_stride, kMaxHistory);
+        if (plan.stream) {
+            p.pen_bits = ws.pen_bits;
+            p.pen_words = (a.V + 31) / 32;
+        }
     }
     p.cand = ws.cand;
     p.cand_cap = plan.cand_cap;
@@ -3549,7 +3593,7 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         if (e != cudaSuccess) return e;
         penalty_prep_kernel<T><<<a.B, NT, sm, a.stream>>>((const T*)a.logits, a.stride, a.V, a.vocab_offset, a.hist,
                                                            a.hist_stride, a.hist_count, a.penalty, ws.pen_ids,
-                                                           ws.pen_vals, ws.pen_cnt, ps);
+                                                           ws.pen_vals, ws.pen_cnt, ps, p.pen_bits, p.pen_words);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         count(a);
     }
