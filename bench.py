@@ -189,7 +189,7 @@ def preroll(torch, us):
     torch.cuda._sleep(int(us * 2000))  # ~2 GHz SM clock: cycles for `us` microseconds
 
 
-def timed_loop(torch, ctx, step, steps, flush, stream, clocks, staged_every=4, pre_us=None):
+def timed_loop(torch, ctx, step, steps, flush, stream, clocks, staged_every=4, pre_us=None, align=None):
     """Runs `steps` timed steps with CUDA events around each on `stream`; the library
     records the stage events around its dominant pass on every `staged_every`-th step.
     Returns (per-step ms, mean dominant-kernel ms, launches)."""
@@ -204,6 +204,8 @@ def timed_loop(torch, ctx, step, steps, flush, stream, clocks, staged_every=4, p
     launches0 = ctx.launch_count()
     with clocks.region():
         preroll(torch, pre_us if pre_us is not None else min(200000, 60 * steps + 2000))
+        if align is not None:
+            align()  # a device-side collective after the pre-roll lines the ranks' timelines up
         for j in range(steps):
             if j in kb:
                 ctx.set_stage_events(kb[j], ke[j])
@@ -395,8 +397,12 @@ def run_ours(args, rank, world, local):
     torch.cuda.synchronize()
     # Clocks are sampled on rank 0 only: a polling thread on every rank adds host jitter.
     clocks = ClockSampler(local, enabled=(rank == 0)).start()
+    align = None
+    if world > 1:
+        one = torch.ones(1, device=dev)
+        align = lambda: dist.all_reduce(one)  # noqa: E731
     per_step, kern_ms, launches = timed_loop(torch, ctx, lambda j: step(args.warmup + j), args.steps, flush, stream,
-                                             clocks)
+                                             clocks, align=align)
     ctx.device_status()
     if world > 1:
         dist.barrier()

@@ -288,11 +288,35 @@ VDXS_API int32_t vdxs_decode_step(vdxs_context* ctx, const vdxs_config* cfg, con
 typedef struct vdxs_comm vdxs_comm;
 
 #define VDXS_NCCL_UNIQUE_ID_BYTES 128
+#define VDXS_COMM_DEFAULT_TIMEOUT_MS 60000
 /* Creates an NCCL unique id on one rank; broadcast the 128 bytes to the others. */
 VDXS_API int32_t vdxs_comm_unique_id(uint8_t out_id[VDXS_NCCL_UNIQUE_ID_BYTES]);
+/* vdxs_comm_create_ex with timeout_ms = VDXS_COMM_DEFAULT_TIMEOUT_MS. */
 VDXS_API int32_t vdxs_comm_create(vdxs_context* ctx, int32_t nranks, int32_t rank,
                                   const uint8_t unique_id[VDXS_NCCL_UNIQUE_ID_BYTES],
                                   vdxs_comm** out);
+/* Failure detection for the one collective this library adds (the reference has none;
+ * its sampler runs on one host thread). The communicator is created non-blocking and
+ * every host-side wait on it (its initialisation, each collective's enqueue, finalisation
+ * and vdxs_comm_wait) runs under timeout_ms: when a rank does not join, stops, or NCCL
+ * reports an asynchronous error, the communicator is aborted (ncclCommAbort, which also
+ * ends NCCL kernels waiting for a peer) and the call returns VDXS_E_TIMEOUT or
+ * VDXS_E_NCCL. An aborted communicator refuses every later call with VDXS_E_NCCL and
+ * launches nothing; destroy it and create a new one. */
+VDXS_API int32_t vdxs_comm_create_ex(vdxs_context* ctx, int32_t nranks, int32_t rank,
+                                     const uint8_t unique_id[VDXS_NCCL_UNIQUE_ID_BYTES],
+                                     int32_t timeout_ms, vdxs_comm** out);
+/* Aborts the communicator now: for a caller that learns on the host (a heartbeat, a
+ * store) that a peer left. */
+VDXS_API int32_t vdxs_comm_abort(vdxs_comm* comm);
+/* VDXS_OK while the communicator is usable; VDXS_E_NCCL after an asynchronous NCCL error
+ * (for example a peer process that died) or an abort. Does not wait. */
+VDXS_API int32_t vdxs_comm_status(vdxs_comm* comm);
+/* Waits for `stream` (the stream of this rank's sharded calls) for at most timeout_ms
+ * (<= 0: the communicator's timeout), watching the communicator for asynchronous errors;
+ * on either failure the communicator is aborted, so NCCL kernels waiting for a peer
+ * return, and VDXS_E_TIMEOUT or VDXS_E_NCCL is returned. */
+VDXS_API int32_t vdxs_comm_wait(vdxs_comm* comm, void* stream, int32_t timeout_ms);
 VDXS_API int32_t vdxs_comm_destroy(vdxs_comm* comm);
 
 VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm,

@@ -50,6 +50,10 @@ SIGNATURES = {
     "vdxs_sampler_get_history": (i32, [vp, i32, vp, i32, P(i32), P(i32)]),
     "vdxs_comm_unique_id": (i32, [vp]),
     "vdxs_comm_create": (i32, [vp, i32, i32, vp, P(vp)]),
+    "vdxs_comm_create_ex": (i32, [vp, i32, i32, vp, i32, P(vp)]),
+    "vdxs_comm_abort": (i32, [vp]),
+    "vdxs_comm_status": (i32, [vp]),
+    "vdxs_comm_wait": (i32, [vp, vp, i32]),
     "vdxs_comm_destroy": (i32, [vp]),
     "vdxs_sample_sharded": (i32, [vp, vp, P(VdxsConfig), vp, i32, i32, i32, i64, i64, i64, vp, i64, vp,
                                   vp, vp, vp, vp]),

@@ -18,6 +18,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 using namespace vdxs;
@@ -888,7 +889,9 @@ namespace {
 struct NcclApi {
     void* handle = nullptr;
     ncclResult_t (*GetUniqueId)(ncclUniqueId*) = nullptr;
-    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*) = nullptr;
+    ncclResult_t (*CommFinalize)(ncclComm_t) = nullptr;
     ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
     ncclResult_t (*CommAbort)(ncclComm_t) = nullptr;
     ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
@@ -907,12 +910,15 @@ NcclApi& nccl() {
         if (!h) return;
         api.handle = h;
         api.GetUniqueId = (decltype(api.GetUniqueId))dlsym(h, "ncclGetUniqueId");
-        api.CommInitRank = (decltype(api.CommInitRank))dlsym(h, "ncclCommInitRank");
+        api.CommInitRankConfig = (decltype(api.CommInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
+        api.CommGetAsyncError = (decltype(api.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+        api.CommFinalize = (decltype(api.CommFinalize))dlsym(h, "ncclCommFinalize");
         api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
         api.CommAbort = (decltype(api.CommAbort))dlsym(h, "ncclCommAbort");
         api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
         api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
-        api.ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllGather && api.GetErrorString;
+        api.ok = api.GetUniqueId && api.CommInitRankConfig && api.CommGetAsyncError && api.CommFinalize &&
+                 api.CommDestroy && api.CommAbort && api.AllGather && api.GetErrorString;
     });
     return api;
 }
@@ -924,7 +930,50 @@ struct vdxs_comm {
     ncclComm_t comm = nullptr;
     int nranks = 0;
     int rank = 0;
+    int timeout_ms = 0;    // deadline of every host-side wait on the communicator
+    bool aborted = false;  // ncclCommAbort was called: the communicator is unusable
 };
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+// Aborts the communicator (NCCL stops its kernels and proxy threads); it stays unusable.
+void comm_abort(vdxs_comm* c) {
+    if (c->comm && !c->aborted) {
+        DeviceGuard g(c->ctx->device);
+        nccl().CommAbort(c->comm);
+    }
+    c->aborted = true;
+}
+
+// Polls the non-blocking communicator until its pending host-side operation (init,
+// enqueue, finalize) is done. Returns VDXS_OK, VDXS_E_NCCL (asynchronous error) or
+// VDXS_E_TIMEOUT; the communicator is aborted on both failures.
+int32_t comm_settle(vdxs_comm* c, const char* what) {
+    NcclApi& n = nccl();
+    const auto t0 = Clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = n.CommGetAsyncError(c->comm, &st);
+        if (r != ncclSuccess) st = r;
+        if (st == ncclSuccess) return VDXS_OK;
+        if (st != ncclInProgress) {
+            comm_abort(c);
+            return fail(c->ctx, VDXS_E_NCCL, "%s: %s; the communicator was aborted", what, n.GetErrorString(st));
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() > c->timeout_ms) {
+            comm_abort(c);
+            return fail(c->ctx, VDXS_E_TIMEOUT,
+                        "%s did not complete within %d ms (a rank did not join or stopped); the communicator "
+                        "was aborted",
+                        what, c->timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(200));
+    }
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -940,11 +989,14 @@ VDXS_API int32_t vdxs_comm_unique_id(uint8_t out_id[VDXS_NCCL_UNIQUE_ID_BYTES]) 
     return VDXS_OK;
 }
 
-VDXS_API int32_t vdxs_comm_create(vdxs_context* ctx, int32_t nranks, int32_t rank,
-                                  const uint8_t unique_id[VDXS_NCCL_UNIQUE_ID_BYTES], vdxs_comm** out) {
+VDXS_API int32_t vdxs_comm_create_ex(vdxs_context* ctx, int32_t nranks, int32_t rank,
+                                     const uint8_t unique_id[VDXS_NCCL_UNIQUE_ID_BYTES], int32_t timeout_ms,
+                                     vdxs_comm** out) {
     if (!ctx || !unique_id || !out) return fail(ctx, VDXS_E_INVALID_ARG, "NULL argument");
+    *out = nullptr;
     if (nranks < 1 || rank < 0 || rank >= nranks)
         return fail(ctx, VDXS_E_INVALID_ARG, "rank %d / nranks %d invalid", rank, nranks);
+    if (timeout_ms < 1) return fail(ctx, VDXS_E_INVALID_ARG, "timeout_ms must be >= 1 (got %d)", timeout_ms);
     NcclApi& n = nccl();
     if (!n.ok) return fail(ctx, VDXS_E_NCCL, "libnccl.so.2 could not be loaded");
     DeviceGuard g(ctx->device);
@@ -954,13 +1006,78 @@ VDXS_API int32_t vdxs_comm_create(vdxs_context* ctx, int32_t nranks, int32_t ran
     c->ctx = ctx;
     c->nranks = nranks;
     c->rank = rank;
-    ncclResult_t r = n.CommInitRank(&c->comm, nranks, id, rank);
-    if (r != ncclSuccess) {
+    c->timeout_ms = timeout_ms;
+    // Non-blocking: the init returns at once and is polled against the deadline, so a
+    // rank that never joins ends in VDXS_E_TIMEOUT instead of a hang.
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = n.CommInitRankConfig(&c->comm, nranks, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress) {
+        if (c->comm) n.CommAbort(c->comm);
         delete c;
-        return fail(ctx, VDXS_E_NCCL, "ncclCommInitRank: %s", n.GetErrorString(r));
+        return fail(ctx, VDXS_E_NCCL, "ncclCommInitRankConfig: %s", n.GetErrorString(r));
+    }
+    const int32_t rc = comm_settle(c, "communicator initialisation");
+    if (rc != VDXS_OK) {
+        const std::string msg = ctx->last_error;
+        delete c;
+        return fail(ctx, rc, "%s", msg.c_str());
     }
     *out = c;
     ok(ctx);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_comm_create(vdxs_context* ctx, int32_t nranks, int32_t rank,
+                                  const uint8_t unique_id[VDXS_NCCL_UNIQUE_ID_BYTES], vdxs_comm** out) {
+    return vdxs_comm_create_ex(ctx, nranks, rank, unique_id, VDXS_COMM_DEFAULT_TIMEOUT_MS, out);
+}
+
+VDXS_API int32_t vdxs_comm_abort(vdxs_comm* c) {
+    if (!c) return fail(nullptr, VDXS_E_INVALID_ARG, "communicator is NULL");
+    comm_abort(c);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_comm_status(vdxs_comm* c) {
+    if (!c) return fail(nullptr, VDXS_E_INVALID_ARG, "communicator is NULL");
+    if (c->aborted) return fail(c->ctx, VDXS_E_NCCL, "the communicator was aborted");
+    ncclResult_t st = ncclSuccess;
+    ncclResult_t r = nccl().CommGetAsyncError(c->comm, &st);
+    if (r != ncclSuccess) st = r;
+    if (st == ncclSuccess || st == ncclInProgress) return VDXS_OK;
+    return fail(c->ctx, VDXS_E_NCCL, "communicator error: %s", nccl().GetErrorString(st));
+}
+
+VDXS_API int32_t vdxs_comm_wait(vdxs_comm* c, void* stream, int32_t timeout_ms) {
+    if (!c) return fail(nullptr, VDXS_E_INVALID_ARG, "communicator is NULL");
+    if (c->aborted) return fail(c->ctx, VDXS_E_NCCL, "the communicator was aborted");
+    DeviceGuard g(c->ctx->device);
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int limit = timeout_ms > 0 ? timeout_ms : c->timeout_ms;
+    NcclApi& n = nccl();
+    const auto t0 = Clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(st);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) return cuda_fail(c->ctx, q, "stream query");
+        ncclResult_t as = ncclSuccess;
+        ncclResult_t r = n.CommGetAsyncError(c->comm, &as);
+        if (r != ncclSuccess) as = r;
+        if (as != ncclSuccess && as != ncclInProgress) {
+            comm_abort(c);
+            return fail(c->ctx, VDXS_E_NCCL, "communicator error while waiting: %s; the communicator was aborted",
+                        n.GetErrorString(as));
+        }
+        if (std::chrono::duration_cast<std::chrono::milliseconds>(Clock::now() - t0).count() > limit) {
+            comm_abort(c);
+            return fail(c->ctx, VDXS_E_TIMEOUT,
+                        "the stream did not complete within %d ms (a peer stopped in a collective?); the "
+                        "communicator was aborted",
+                        limit);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
     return VDXS_OK;
 }
 
@@ -969,7 +1086,14 @@ VDXS_API int32_t vdxs_comm_destroy(vdxs_comm* c) {
     NcclApi& n = nccl();
     if (c->comm && n.ok) {
         DeviceGuard g(c->ctx->device);
-        n.CommDestroy(c->comm);
+        if (!c->aborted) {
+            // Flush the pending operations under the deadline, then free.
+            ncclResult_t r = n.CommFinalize(c->comm);
+            if ((r == ncclSuccess || r == ncclInProgress) && comm_settle(c, "communicator finalisation") == VDXS_OK)
+                n.CommDestroy(c->comm);
+            else
+                comm_abort(c);
+        }
     }
     delete c;
     return VDXS_OK;
@@ -985,6 +1109,11 @@ VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm, const v
                                  history_stride, d_history_count, d_out_tokens);
     if (rc != VDXS_OK) return rc;
     if (!comm) return fail(ctx, VDXS_E_INVALID_ARG, "communicator is NULL");
+    if (comm->aborted) return fail(ctx, VDXS_E_NCCL, "the communicator was aborted; create a new one");
+    if ((rc = vdxs_comm_status(comm)) != VDXS_OK) {
+        comm_abort(comm);
+        return fail(ctx, rc, "%s (nothing was launched); the communicator was aborted", vdxs_last_error(ctx));
+    }
     if (vocab_offset < 0 || vocab_total < vocab_offset + vocab_shard || vocab_total > INT32_MAX)
         return fail(ctx, VDXS_E_INVALID_ARG, "shard [%lld, %lld) does not fit vocab_total %lld",
                     (long long)vocab_offset, (long long)(vocab_offset + vocab_shard), (long long)vocab_total);
@@ -1024,7 +1153,13 @@ VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm, const v
     if ((e = launch_sample(a, plan, ctx->ws, &msg)) != cudaSuccess) return cuda_fail(ctx, e, "local select launch");
     const size_t words = (size_t)batch * (size_t)(a.K + 1) * 2;
     ncclResult_t r = n.AllGather(ctx->ws.shard_send, ctx->ws.shard_recv, words, ncclUint32, comm->comm, a.stream);
-    if (r != ncclSuccess) return fail(ctx, VDXS_E_NCCL, "ncclAllGather: %s", n.GetErrorString(r));
+    if (r == ncclInProgress) {
+        // Non-blocking communicator: wait (under the deadline) until the enqueue is done.
+        if ((rc = comm_settle(comm, "ncclAllGather enqueue")) != VDXS_OK) return rc;
+    } else if (r != ncclSuccess) {
+        comm_abort(comm);
+        return fail(ctx, VDXS_E_NCCL, "ncclAllGather: %s; the communicator was aborted", n.GetErrorString(r));
+    }
     if ((e = launch_merge_draw(a, comm->nranks, ctx->ws, &msg)) != cudaSuccess)
         return cuda_fail(ctx, e, "merge launch");
     ok(ctx);

@@ -2160,8 +2160,9 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
     // the counter start after those runs.
     const uint32_t c0 = max(1u, min((uint32_t)U, ne / (2u * nwarps)));
     const uint32_t base = c0 * nwarps;
+    const uint32_t guide_full = (uint32_t)U * 2u * nwarps;  // below this, runs shrink
     auto claim_next = [&](uint32_t left_est) {
-        nc = max(1u, min((uint32_t)U, left_est / (2u * nwarps)));
+        nc = left_est >= guide_full ? (uint32_t)U : max(1u, left_est / (2u * nwarps));
         ng0 = base + (uint32_t)atomicAdd((unsigned long long*)p.unit_next, (unsigned long long)nc);
         have_next = true;
     };
@@ -2469,16 +2470,13 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
                     ++counted;
                 }
             };
-            // The same count for a warp-uniform step: lanes with equal bins add together.
+            // The same count for one element per lane.
             auto count_step = [&](bool valid, uint32_t k) {
-                const bool cnt_it = valid && (k >> 20) > tbin;
-                const unsigned cm = __ballot_sync(FULL, cnt_it);
-                if (cm == 0u) return;
-                const unsigned same = __match_any_sync(FULL, cnt_it ? (k >> 20) : 0xFFFFFFFFu);
-                if (cnt_it && (__ffs((int)same) - 1) == lane) red_add_u32(rh + (k >> 20), (uint32_t)__popc(same));
-                const unsigned sameg = __match_any_sync(FULL, cnt_it ? (k >> 26) : 0xFFFFFFFFu);
-                if (cnt_it && (__ffs((int)sameg) - 1) == lane) red_add_u32(rh + kTBins + (k >> 26), (uint32_t)__popc(sameg));
-                counted += (uint32_t)(cnt_it ? 1 : 0);
+                if (valid && (k >> 20) > tbin) {
+                    red_add_u32(rh + (k >> 20), 1u);
+                    red_add_u32(rh + kTBins + (k >> 26), 1u);
+                    ++counted;
+                }
             };
             auto put = [&](uint32_t pos, uint32_t k, uint32_t ix) {
                 rkey[pos] = k;
@@ -3299,7 +3297,9 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         plan->stream = true;
         plan->cand_cap = cc;
         plan->gather_cap = gather;
-        plan->grid = (int)std::max<long long>(1, std::min<long long>((long long)sms, (units + kS1Warps - 1) / kS1Warps));
+        // One CTA per SM unless the work is below about four slots per warp.
+        const long long slots = (long long)a.B * ng;
+        plan->grid = (int)std::max<long long>(1, std::min<long long>((long long)sms, slots / (4LL * kS1Warps)));
         plan->slots = ng;
         plan->unit_slots = U;
         plan->items = a.B;

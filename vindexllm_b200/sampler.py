@@ -303,13 +303,15 @@ def broadcast_unique_id(rank: int, src: int = 0) -> bytes:
 class ShardComm:
     """An NCCL communicator owned by the library (vdxs_comm)."""
 
-    def __init__(self, ctx: SamplerContext, nranks: int, rank: int, unique_id: bytes):
+    def __init__(self, ctx: SamplerContext, nranks: int, rank: int, unique_id: bytes, timeout_ms: int = 60000):
+        """Creates the communicator (non-blocking NCCL init under `timeout_ms`: a rank that
+        never joins raises VdxsError with VDXS_E_TIMEOUT instead of hanging)."""
         self.ctx = ctx
         self.lib = ctx.lib
         assert len(unique_id) == 128
         buf = (C.c_uint8 * 128).from_buffer_copy(unique_id)
         h = C.c_void_p()
-        check(self.lib.vdxs_comm_create(ctx.handle, nranks, rank, buf, C.byref(h)), ctx.handle)
+        check(self.lib.vdxs_comm_create_ex(ctx.handle, nranks, rank, buf, int(timeout_ms), C.byref(h)), ctx.handle)
         self._h = h
         self.nranks = nranks
         self.rank = rank
@@ -325,6 +327,18 @@ class ShardComm:
         if getattr(self, "_h", None):
             self.lib.vdxs_comm_destroy(self._h)
             self._h = None
+
+    def abort(self):
+        """vdxs_comm_abort: for a caller that learned on the host that a peer left."""
+        check(self.lib.vdxs_comm_abort(self._h), self.ctx.handle)
+
+    def status(self):
+        """vdxs_comm_status: raises VdxsError after an asynchronous NCCL error or an abort."""
+        check(self.lib.vdxs_comm_status(self._h), self.ctx.handle)
+
+    def wait(self, stream=None, timeout_ms: int = 0):
+        """vdxs_comm_wait: bounded wait for the stream; aborts the communicator on failure."""
+        check(self.lib.vdxs_comm_wait(self._h, _stream_ptr(stream), int(timeout_ms)), self.ctx.handle)
 
     def sample(self, cfg: VdxsConfig, logits_shard, vocab_offset: int, vocab_total: int, uniforms=None,
                history=None, history_count=None, want_flags: bool = False, stream=None, tokens=None):
