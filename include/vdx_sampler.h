@@ -282,7 +282,9 @@ VDXS_API int32_t vdxs_decode_step(vdxs_context* ctx, const vdxs_config* cfg, con
  * of every row. Each rank selects its local top-k (lowest global index wins ties),
  * the (value, global index) candidates are all-gathered with NCCL, and every rank
  * runs the identical merge, top-p and draw, so all ranks return the same tokens.
- * Ties are canonical (lowest global index); history ids are global.
+ * Ties are canonical (lowest global index); history ids are global. The sharded call
+ * serves 0 < top_k <= 1024 and greedy (temperature 0); other configurations return
+ * VDXS_E_UNSUPPORTED.
  * NCCL is loaded at run time (libnccl.so.2) on the first communicator creation.
  * ---------------------------------------------------------------------------- */
 typedef struct vdxs_comm vdxs_comm;

@@ -93,8 +93,6 @@ int32_t resolve_config(vdxs_context* ctx, const vdxs_config* cfg, int64_t vocab_
     } else if (cfg->top_k > 0 && (int64_t)cfg->top_k < vocab_total) {  // :327
         a->path = kTopK;
         a->K = cfg->top_k;
-        if (a->K > kMaxTopK)
-            return fail(ctx, VDXS_E_UNSUPPORTED, "top_k=%d exceeds the supported maximum %d", a->K, kMaxTopK);
     } else {
         a->path = kFull;
         a->K = 0;
@@ -1121,6 +1119,8 @@ VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm, const v
     if ((rc = resolve_config(ctx, cfg, vocab_total, &a)) != VDXS_OK) return rc;
     if (a.path == kFull)
         return fail(ctx, VDXS_E_UNSUPPORTED, "the vocab-sharded path needs 0 < top_k < vocab_total or temperature 0");
+    if (a.path == kTopK && a.K > kMaxTopK)
+        return fail(ctx, VDXS_E_UNSUPPORTED, "the vocab-sharded path serves top_k <= %d (got %d)", kMaxTopK, a.K);
     if (a.path != kGreedy && !d_uniform)
         return fail(ctx, VDXS_E_INVALID_ARG, "uniform pointer is NULL but temperature != 0");
     NcclApi& n = nccl();

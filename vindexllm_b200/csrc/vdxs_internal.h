@@ -10,7 +10,7 @@
 namespace vdxs {
 
 constexpr int kThreads = 256;        // threads per CTA in every sampling kernel
-constexpr int kMaxTopK = 1024;       // largest top_k served by the top-k path
+constexpr int kMaxTopK = 1024;       // largest top_k served by the stream path (larger: the large top-k kernel)
 constexpr int kMaxHistory = 8192;    // largest history stride served by the penalty prep
 constexpr int kFaithfulSub = 512;    // elements per sub-tile of the min-buffer emulation
 constexpr int kFaithfulSlots = 12;  // candidate ring slots of the min-buffer emulation
@@ -45,6 +45,8 @@ struct Workspace {
     uint2* shard_send = nullptr;    // [rows * K] sharded: local candidates
     uint2* shard_recv = nullptr;    // [ranks * rows * K]
     size_t shard_send_cap = 0, shard_recv_cap = 0;
+    uint64_t* lk_buf = nullptr;     // top_k above the stream path's maximum: per-CTA sort buffers and slots
+    size_t lk_cap = 0;              // 64-bit words
     int32_t* err = nullptr;         // device error word (0 = ok)
     // host-buffer entry point staging
     void* d_logits = nullptr;
@@ -102,6 +104,7 @@ struct LaunchPlan {
     int elems = 32;   // stream path: warp list registers R (0 = wide stream path)
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
     bool cluster = false; // top-k path, small batches: one thread-block cluster per row
+    bool large = false;   // top-k path, top_k above kMaxTopK: one CTA per row, global workspace
     int cluster_ctas = 8; // CTAs per cluster
     int grid = 0;         // stream kernel grid (CTAs)
     int cand_cap = 0;     // top-k path: candidates each stage-1 list may hold (stream path: per row)

@@ -4,11 +4,15 @@
 // [B, V] device-resident logits.
 //
 //   penalty_prep_kernel   Sampler.pas:285-303  history ids -> sorted unique (id, f^n(x))
-//   topk_hist_kernel      Sampler.pas:305-383  top_k <= 128: persistent CTAs stream flat
-//                         pieces of rows through per-warp TMA rings, filter against a
-//                         threshold taken from a key histogram (raised as candidates are
-//                         counted and shared per row), and write each piece's candidates.
-//   topk_wide_kernel      the same stage 1 for 128 < top_k <= 1024, appending raw lists.
+//   topk_stream_kernel    Sampler.pas:305-383  top_k <= 1024 and greedy: one 16-warp CTA
+//                         per SM; warps claim row segments from a global counter, stream
+//                         them through per-warp bulk-copy rings, filter against a per-row
+//                         bound taken from a shared key histogram, and append candidates
+//                         to one list per row.
+//   topk_large_kernel     1024 < top_k < V: one CTA per row, radix select over the row in
+//                         global memory, a single-CTA radix sort of the K survivors, the
+//                         reference's sequential walk; faithful rows re-run the min-buffer
+//                         with a tournament tree (vdxs_large_topk.cuh).
 //   finish_kernel         Sampler.pas:305-459  one CTA per row (programmatic dependent
 //                         launch): gathers the candidates at the row's bound plus the
 //                         penalised history entries, selects the exact top-K, then exp /
@@ -126,6 +130,8 @@ struct KParams {
     int64_t vocab_offset;
     int local_emit;
     uint2* emit_out;  // [B][K+1]
+    // top_k above the stream path's maximum: per-CTA global workspace (lk_cta_words(K) words each)
+    uint64_t* lk_buf;
 };
 
 // ---------------------------------------------------------------------------------
@@ -1540,6 +1546,8 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     const uint32_t gmax = block_max_u32(lm, sh + 32);
     finish_select<T>(p, b, ckey, cidx, n2, gmax, 0, [&](int) -> uint32_t { return 0u; }, region, hist, sh);
 }
+
+#include "vdxs_large_topk.cuh"
 
 // ---------------------------------------------------------------------------------
 // Warp-level select (one warp, warp-private histogram; __syncwarp only). Same result
@@ -3307,8 +3315,31 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         plan->smem2 = align16(s2);
         return cudaSuccess;
     }
-    if (err) *err = "top_k too large for the shared-memory plan (top_k=" + std::to_string(K) + ")";
-    return cudaErrorInvalidValue;
+    {
+        // top_k above the stream path's maximum: one CTA per row of a persistent grid, each
+        // with 24 bytes of global workspace per slot (at most 1 GiB in all).
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        const size_t sm = lk_smem_bytes(K);
+        if ((int64_t)sm + 1024 > smem_optin) {
+            if (err) *err = "shared-memory plan exceeds the device limit";
+            return cudaErrorInvalidValue;
+        }
+        const int64_t per_cta = 8 * lk_cta_words(K);
+        const int64_t by_mem = std::max<int64_t>(1, (1LL << 30) / per_cta);
+        plan->large = true;
+        plan->stream = false;
+        plan->grid = (int)std::min<int64_t>({(int64_t)a.B, 2LL * sms, by_mem});
+        plan->chunk = 0;
+        plan->nchunks = 1;
+        plan->nspans = 1;
+        plan->span = 1;
+        plan->items = 0;
+        plan->cand_cap = 0;
+        plan->smem = align16(sm);
+        return cudaSuccess;
+    }
 }
 
 cudaError_t plan_full(const SampleArgs& a, LaunchPlan* plan, std::string*) {
@@ -3386,12 +3417,16 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
         if ((e = grow(&ws.pen_vals, &cap_b, B * ps, false, stream)) != cudaSuccess) return e;
         ws.pen_cap = std::min(cap_a, cap_b);
         if ((e = grow(&ws.pen_cnt, &ws.pen_rows_cap, B, false, stream)) != cudaSuccess) return e;
-        if (plan.stream) {
-            // Zero once; the finish kernel clears the words it set.
+        if (plan.stream || plan.large) {
+            // Zero once; the finish kernel (the large top-k kernel) clears the words it set.
             const size_t words = B * (size_t)((a.V + 31) / 32);
             if ((e = grow(&ws.pen_bits, &ws.pen_bits_cap, words, true, stream)) != cudaSuccess) return e;
         }
     }
+    if (plan.large &&
+        (e = grow(&ws.lk_buf, &ws.lk_cap, (size_t)plan.grid * (size_t)lk_cta_words(a.K), false, stream)) !=
+            cudaSuccess)
+        return e;
     if (a.local_emit) {
         if ((e = grow(&ws.shard_send, &ws.shard_send_cap, B * (size_t)(a.K + 1), false, stream)) != cudaSuccess)
             return e;
@@ -3466,13 +3501,17 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
         w.pen_ids = (int32_t*)take(B * ps * sizeof(int32_t));
         w.pen_vals = (float*)take(B * ps * sizeof(float));
         w.pen_cnt = (int32_t*)take(B * sizeof(int32_t));
-        if (plan.stream) {
+        if (plan.stream || plan.large) {
             const size_t words = B * (size_t)((a.V + 31) / 32);
             w.pen_bits = (uint32_t*)take(words * sizeof(uint32_t));
             w.pen_bits_cap = words;
         }
         w.pen_cap = B * ps;
         w.pen_rows_cap = B;
+    }
+    if (plan.large) {
+        w.lk_cap = (size_t)plan.grid * (size_t)lk_cta_words(a.K);
+        w.lk_buf = (uint64_t*)take(w.lk_cap * sizeof(uint64_t));
     }
     if (off <= cap) ws = w;
     return off;
@@ -3512,6 +3551,7 @@ void free_workspace(Workspace& ws) {
     cudaFree(ws.fsum);
     cudaFree(ws.shard_send);
     cudaFree(ws.shard_recv);
+    cudaFree(ws.lk_buf);
     cudaFree(ws.err);
     cudaFree(ws.d_logits);
     cudaFree(ws.d_hist);
@@ -3538,7 +3578,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
         p.pen_vals = ws.pen_vals;
         p.pen_cnt = ws.pen_cnt;
         p.pen_stride = (int)std::min<int64_t>(a.hist_stride, kMaxHistory);
-        if (plan.stream) {
+        if (plan.stream || plan.large) {
             p.pen_bits = ws.pen_bits;
             p.pen_words = (a.V + 31) / 32;
         }
@@ -3570,6 +3610,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.vocab_offset = a.vocab_offset;
     p.local_emit = a.local_emit ? 1 : 0;
     p.emit_out = ws.shard_send;
+    p.lk_buf = ws.lk_buf;
     return p;
 }
 
@@ -3681,6 +3722,16 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         }
         count(a, 2);
         return cudaSuccess;
+    }
+    if (plan.large) {
+        if ((e = cudaFuncSetAttribute(topk_large_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)plan.smem)) != cudaSuccess)
+            return e;
+        if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
+        topk_large_kernel<T><<<plan.grid, NT, plan.smem, a.stream>>>(p);
+        if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        count(a);
+        return mark(a, a.ev_end);
     }
     if (err) *err = "no top-k plan for this call";
     return cudaErrorInvalidValue;
