@@ -3242,8 +3242,9 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     const int pen_stride = a.penalty_on ? (int)std::min<int64_t>(a.hist_stride, kMaxHistory) : 0;
     const size_t esz = a.dtype == VDXS_DTYPE_BF16 ? 2 : 4;
     const bool faithful = a.tie_mode == VDXS_TIES_FAITHFUL && a.path == kTopK && !a.local_emit;
-    if (a.B <= kClusterMaxRows) {
-        // Small batches: one cluster per row when a row's 1/CL fits in shared memory.
+    if (a.B <= kClusterMaxRows && K <= kMaxTopK) {
+        // Small batches: one cluster per row when a row's 1/CL fits in shared memory (its
+        // stage 2 holds up to kMaxTopK survivors, like the finish kernel's).
         for (const int CL : {kClusterCTAs}) {
             const int64_t L = ((V + CL - 1) / CL + 15) / 16 * 16;
             const int cap = std::max(K, 512);
