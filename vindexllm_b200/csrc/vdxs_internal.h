@@ -13,7 +13,7 @@ constexpr int kThreads = 256;        // threads per CTA in every sampling kernel
 constexpr int kMaxTopK = 1024;       // largest top_k served by the stream path (larger: the large top-k kernel)
 constexpr int kMaxHistory = 8192;    // largest history stride served by the penalty prep
 constexpr int kFaithfulSub = 512;    // elements per sub-tile of the min-buffer emulation
-constexpr int kFaithfulSlots = 12;  // candidate ring slots of the min-buffer emulation
+constexpr int kFaithfulSlots = 12;  // candidate regions of the min-buffer emulation, in units of kFaithfulSub entries
 constexpr int kTauStride = 32;       // words between rows of the stream path's row bounds (one L2 line)
 
 enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };

@@ -901,61 +901,45 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
 // ---------------------------------------------------------------------------------
 // Faithful emulation of the reference min-buffer (Sampler.pas:341-383) over one row,
 // followed by the reference's sequential double arithmetic (Sampler.pas:385-459).
-// `work` must hold faithful_bytes(K) bytes (8*K for the buffer, the candidate ring,
+// `work` must hold faithful_bytes(K) bytes (8*K for the buffer, the candidate regions,
 // then the stage-2 tail).
 // ---------------------------------------------------------------------------------
 template <typename T>
 __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigned char* work,
                              uint32_t* shu) {
-    // The first K elements fill the buffer in slot order (Sampler.pas:352-356); that is
-    // one parallel pass. The rest of the row runs as a pipeline inside the CTA:
-    // - producer warps 1..7 each take every 7th sub-tile of kFaithfulSub elements,
-    //   overlay the penalised values, and compact, in index order, the elements above
-    //   the scanner's last published buffer minimum into one of kFaithfulSlots ring
-    //   slots. The minimum only grows, so it is a lower bound on the minimum that each
-    //   element meets and nothing the reference would insert is dropped;
-    // - warp 0 (the scanner) replays the candidates in index order: an element strictly
-    //   above the minimum replaces the minimum's slot, and the lowest slot holding the
-    //   minimum value becomes the next one. Lane l keeps the minimum of the slots
-    //   s = l (mod 32); an insertion rescans only the owning lane's slots, and two warp
-    //   reductions give the new (minimum, lowest slot).
-    // Slots are handed over by flags; every wait is bounded and an abort flag ends both
-    // sides.
-    __shared__ volatile float s_mv;
-    __shared__ volatile int s_ready[kFaithfulSlots];
-    __shared__ volatile int s_scanned, s_abort;
-    __shared__ int s_cnt[kFaithfulSlots];
+    // The first K elements fill the buffer in slot order (Sampler.pas:352-356): one
+    // parallel pass. The rest of the row is taken in pieces of geometrically growing
+    // length, in lockstep:
+    // - every warp filters a contiguous share of the piece (penalised values overlaid)
+    //   against the buffer minimum at the piece's start and compacts, in index order,
+    //   the elements above it into its own region. The minimum only grows, so nothing
+    //   the reference inserts is dropped;
+    // - warp 0 replays the regions in warp order: an element strictly above the current
+    //   minimum replaces the minimum's slot, and the lowest slot holding the minimum
+    //   value becomes the next one. Lane l keeps the minimum of the slots s = l (mod 32).
+    //   For top_k <= 64 (at most two slots per lane) the slot keys stay in registers and
+    //   an insertion costs one warp reduction and two ballots; otherwise the warp rescans
+    //   the owning lane's slots and two pairs of warp reductions give the new minimum.
+    // A piece whose share overflows a region is filtered again at the shortest length,
+    // where a share (kFaithfulSub elements) always fits.
+    constexpr int CW = kFaithfulSlots * kFaithfulSub / NWARPS;  // region entries per warp
+    constexpr int RS = kFaithfulSub / 32;                        // elements per lane per step
+    static_assert(CW >= kFaithfulSub, "a shortest-piece share must fit a region");
+    __shared__ float s_mv;
+    __shared__ int s_cnt[NWARPS];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = p.K, V = p.V;
     const T* row = (const T*)p.logits + (int64_t)b * p.stride;
     float* sval = (float*)work;
     int32_t* sidx = (int32_t*)(sval + K);
-    float* rval = (float*)(sidx + K);                                   // [slots][sub]
-    int32_t* ridx = (int32_t*)(rval + kFaithfulSlots * kFaithfulSub);  // [slots][sub]
-    unsigned char* tail = (unsigned char*)(ridx + kFaithfulSlots * kFaithfulSub);
+    float* rval = (float*)(sidx + K);                 // [NWARPS][CW]
+    int32_t* ridx = (int32_t*)(rval + NWARPS * CW);  // [NWARPS][CW]
+    unsigned char* tail = (unsigned char*)(ridx + NWARPS * CW);
     tail = (unsigned char*)(((uintptr_t)tail + 15) & ~(uintptr_t)15);
     const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
     const int32_t* pid = p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr;
     const float* pvl = p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr;
-    const int nsub = (int)(((int64_t)V - K + kFaithfulSub - 1) / kFaithfulSub);  // K < V
-    // Bounded wait of one thread until *f >= target; false on abort or timeout.
-    auto wait_at_least = [&](volatile int* f, int target, bool nap) -> bool {
-        const uint64_t t0 = global_ns();
-        while (*f < target) {
-            if (s_abort) return false;
-            if (global_ns() - t0 > 2000000000ull) {
-                s_abort = 1;
-                return false;
-            }
-            if (nap) __nanosleep(64);
-        }
-        __threadfence_block();
-        return true;
-    };
-    // Slots per lane (lane l owns slots l, l + 32, ...). After an insertion the whole warp
-    // rescans the owner's slots (lane u reads slot owner + 32*u) and two warp reductions
-    // give the owner's (minimum key, lowest slot).
-    const int RL = (K + 31) / 32;
+    const int RL = (K + 31) / 32;  // slots per lane (lane l owns slots l, l + 32, ...)
     // Minimum of the slots this lane owns; the first slot wins ties (strict '<'). Eight
     // slots are loaded at a time so that their latencies overlap.
     auto lane_min = [&](int& bs) -> uint32_t {
@@ -981,11 +965,6 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
         sval[s] = ld_elem(row, s);
         sidx[s] = s;
     }
-    if (tid < kFaithfulSlots) s_ready[tid] = 0;
-    if (tid == 0) {
-        s_scanned = 0;
-        s_abort = 0;
-    }
     __syncthreads();
     for (int j = tid; j < npen; j += NT) {  // penalised ids ascend
         const int id = pid[j];
@@ -993,189 +972,254 @@ __device__ void faithful_row(const KParams& p, int b, uint32_t flags_in, unsigne
         sval[id] = pvl[j];
     }
     __syncthreads();
-    // Scanner state: per lane the key and slot of its minimum; warp-uniform the buffer
-    // minimum mv and its slot ms.
+    // Scanner state (warp 0): per lane the key and slot of its minimum; warp-uniform the
+    // buffer minimum mv and its slot ms.
     uint32_t kv = 0xFFFFFFFFu;
     int bs = INT_MAX, ms = 0;
     float mv = -INFINITY;
+    // top_k <= 64: the keys of slots lane and lane + 32 (0xFFFFFFFF: no slot).
+    const bool regs = RL <= 2;
+    uint32_t k0 = 0xFFFFFFFFu, k1 = 0xFFFFFFFFu;
     if (warp == 0) {
         kv = lane_min(bs);
         const uint32_t mk = __reduce_min_sync(FULL, kv);
         ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
         mv = key2f(mk);
         if (lane == 0) s_mv = mv;
+        if (regs) {
+            if (lane < K) k0 = f2key(sval[lane]);
+            if (lane + 32 < K) k1 = f2key(sval[lane + 32]);
+        }
     }
     __syncthreads();
     VDXS_T0(t_floop);
-    if (warp == 0) {
-        // Every sub-tile that is ready is replayed before the minimum and the scanned
-        // count are published, so the handoff cost is paid once per batch.
-        int t = 0;
-        while (t < nsub) {
-            bool ok = true;
-            VDXS_T0(t_sw);
-            if (lane == 0) ok = wait_at_least(&s_ready[t % kFaithfulSlots], t + 1, false);
-            ok = __shfl_sync(FULL, ok, 0);
-            if (!ok) break;
-            const int tl = t + lane;
-            const bool rdy = lane < kFaithfulSlots && tl < nsub && s_ready[tl % kFaithfulSlots] >= tl + 1;
-            const int nready = __ffs(~__ballot_sync(FULL, rdy) | (1u << 31)) - 1;  // >= 1
-            __threadfence_block();
-            __syncwarp();
-            VDXS_T1(25, t_sw);
-            VDXS_T0(t_ss);
-            // The ready sub-tiles' candidate lists are replayed as one stream, 32 at a
-            // time: lane k holds the end of sub-tile t + k's list in the stream.
-            const uint32_t cnt_k = lane < nready ? (uint32_t)s_cnt[(t + lane) % kFaithfulSlots] : 0u;
-            uint32_t end_k = cnt_k;
-#pragma unroll
-            for (int d = 1; d < 32; d <<= 1) {
-                const uint32_t o = __shfl_up_sync(FULL, end_k, d);
-                if (lane >= d) end_k += o;
-            }
-            const int total = (int)__shfl_sync(FULL, end_k, 31);
-#ifdef VDXS_TIMING
-            if (lane == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
-#endif
-            for (int c0 = 0; c0 < total; c0 += 32) {
-                const int c = c0 + lane;
-                const bool valid = c < total;
-                // Sub-tile of stream position c: the number of list ends at or below c.
-                int k = 0;
-                uint32_t start = 0u;
-                for (int j = 0; j < nready; ++j) {
-                    const uint32_t e = __shfl_sync(FULL, end_k, j);
-                    if (e <= (uint32_t)c) {
-                        k = j + 1;
-                        start = e;
-                    }
-                }
-                float v = 0.0f;
-                int32_t gi = 0;
-                if (valid) {
-                    const int sl = (t + k) % kFaithfulSlots;
-                    v = rval[sl * kFaithfulSub + (c - (int)start)];
-                    gi = ridx[sl * kFaithfulSub + (c - (int)start)];
-                }
-                unsigned pend = __ballot_sync(FULL, valid && v > mv);
-                while (pend) {
-                    const int l = __ffs(pend) - 1;
-                    if (lane == l) {
-                        sval[ms] = v;
-                        sidx[ms] = gi;
-                    }
-                    __syncwarp();
-#ifdef VDXS_TIMING
-                    if (lane == 0) atomicAdd(&g_phase_count[24], 1ull);
-#endif
-                    // The owner's slots are rescanned by the whole warp (lane u reads slot
-                    // owner + 32*u), then the buffer minimum over the lanes' minima.
-                    const int owner = ms & 31, s2 = owner + 32 * lane;
-                    const uint32_t ok = lane < RL && s2 < K ? f2key(sval[s2]) : 0xFFFFFFFFu;
-                    const uint32_t omk = __reduce_min_sync(FULL, ok);
-                    const uint32_t obs = __reduce_min_sync(FULL, ok == omk ? (uint32_t)s2 : 0xFFFFFFFFu);
-                    if (lane == owner) {
-                        kv = omk;
-                        bs = (int)obs;
-                    }
-                    const uint32_t mk = __reduce_min_sync(FULL, kv);
-                    ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
-                    mv = key2f(mk);
-                    pend &= ~(1u << l);
-                    pend &= __ballot_sync(FULL, valid && v > mv);
-                }
-            }
-            t += nready;
-            __syncwarp();
-            VDXS_T1(26, t_ss);
-            if (lane == 0) {
-                s_mv = mv;
-                __threadfence_block();
-                s_scanned = t;  // slots of sub-tiles below t may be refilled
-            }
-        }
-    } else {
-        // Producer warp w takes sub-tiles w-1, w-1+7, ...; the loads of its next sub-tile
-        // are issued as soon as the current one is published.
-        constexpr int NPW = NWARPS - 1;
-        constexpr int RS = kFaithfulSub / 32;
-        int jc = 0;  // penalty cursor: entries before it lie below the current sub-tile
-        float v[RS];
-        int t = warp - 1;
-        int64_t a = (int64_t)K + (int64_t)t * kFaithfulSub;
-#pragma unroll
-        for (int r = 0; r < RS; ++r) {
-            const int64_t i = a + r * 32 + lane;
-            v[r] = (t < nsub && i < V) ? ld_elem(row, i) : 0.0f;
-        }
-        while (t < nsub) {
-            const int sl = t % kFaithfulSlots;
-            while (npen) {
+    // Two step kinds: vector steps of SPAN elements (16-byte loads, VL per lane; they
+    // need a 16-byte aligned start and a whole step inside the share) and scalar steps
+    // of kFaithfulSub elements (any alignment; row tails). A "safe" piece uses scalar
+    // steps only and is at most kMinPiece long, so no share outgrows its region.
+    constexpr int E = 16 / (int)sizeof(T);  // elements per 16-byte load
+    constexpr int VL = 8;                   // 16-byte loads per lane per vector step
+    constexpr int SPAN = 32 * VL * E;       // elements per vector step
+    constexpr int kMinPiece = NWARPS * kFaithfulSub;
+    const uintptr_t rowaddr = (uintptr_t)row;
+    auto aligned_at = [&](int64_t i) { return ((rowaddr + (uintptr_t)i * sizeof(T)) & 15u) == 0u; };
+    int64_t pos = K;
+    bool safe = true;
+    // The first piece is safe and ends at a 16-byte aligned element, so that vector
+    // pieces (whose lengths are multiples of SPAN) start aligned.
+    int64_t first_end = min((int64_t)V, pos + kMinPiece);
+    while (first_end > pos + 1 && first_end < V && !aligned_at(first_end)) --first_end;
+    int L = (int)(first_end - pos);
+    while (pos < V) {
+        VDXS_T0(t_pf);
+        const int len = (int)min((int64_t)L, (int64_t)V - pos);
+        const int gran = safe ? kFaithfulSub : SPAN;
+        // Warp shares are whole steps.
+        const int per = ((len + NWARPS - 1) / NWARPS + gran - 1) / gran * gran;
+        const int64_t s0 = pos + (int64_t)warp * per;
+        const int64_t s1 = min(s0 + per, pos + len);
+        const float tau = s_mv;
+        float* cv = rval + warp * CW;
+        int32_t* ci = ridx + warp * CW;
+        int cnt = 0;
+        int jc = npen ? lower_bound_i32(pid, npen, s0) : 0;  // first penalised id of the share
+        // Overlays the penalised values of ids in [lo, lo + n) onto f (f[e] holds element
+        // lo + lane * EL + e).
+        auto overlay = [&](float* f, int EL, int64_t lo, int n) {
+            while (jc < npen) {
                 const int j = jc + lane;
                 const int id = j < npen ? pid[j] : INT_MAX;
-                const bool in = id >= a && id < a + kFaithfulSub;
-                const unsigned mb = __ballot_sync(FULL, id < a), mi = __ballot_sync(FULL, in);
+                const bool in = id >= lo && id < lo + n;
+                const unsigned mb = __ballot_sync(FULL, id < lo), mi = __ballot_sync(FULL, in);
                 const float pv = in ? pvl[j] : 0.0f;
                 for (unsigned m = mi; m; m &= m - 1) {
                     const int l = __ffs(m) - 1;
-                    const int off = (int)(__shfl_sync(FULL, id, l) - a);
+                    const int off = (int)(__shfl_sync(FULL, id, l) - lo);
                     const float val = __shfl_sync(FULL, pv, l);
-                    // Select form (no store indexed by a run-time value, so v stays in
+                    // Select form (no store indexed by a run-time value, so f stays in
                     // registers).
-                    const int hit = lane == (off & 31) ? (off >> 5) : -1;
+                    const int tl = off / EL, te = off - (off / EL) * EL;
 #pragma unroll
-                    for (int r = 0; r < RS; ++r) v[r] = r == hit ? val : v[r];
+                    for (int e = 0; e < 8; ++e)
+                        if (e < EL) f[e] = (lane == tl && e == te) ? val : f[e];
                 }
                 const int adv = __popc(mb | mi);
                 jc += adv;
                 if (adv < 32) break;
             }
-            bool ok = true;
-            float tau = 0.0f;
-            if (lane == 0) {
-                ok = wait_at_least(&s_scanned, t - kFaithfulSlots + 1, true);
-                tau = s_mv;
-            }
-            ok = __shfl_sync(FULL, ok, 0);
-            tau = __shfl_sync(FULL, tau, 0);
-            if (!ok) break;
-            float* cv = rval + sl * kFaithfulSub;
-            int32_t* ci = ridx + sl * kFaithfulSub;
-            int cnt = 0;
+        };
+        int64_t a = s0;
+        while (a < s1) {
+            if (!safe && a + SPAN <= s1 && aligned_at(a)) {
+                uint4 r4[VL];
 #pragma unroll
-            for (int r = 0; r < RS; ++r) {
-                const int64_t i = a + r * 32 + lane;
-                const bool c = i < V && v[r] > tau;
-                const unsigned m = __ballot_sync(FULL, c);
-                if (c) {
-                    const int pos = cnt + __popc(m & lanemask_lt());
-                    cv[pos] = v[r];
-                    ci[pos] = (int32_t)i;
+                for (int r = 0; r < VL; ++r) r4[r] = ld_stream16(row + a + (int64_t)(r * 32 + lane) * E);
+#pragma unroll
+                for (int r = 0; r < VL; ++r) {
+                    const int64_t br = a + (int64_t)r * 32 * E;
+                    float f[8];
+                    unpack(r4[r], f, T());
+                    if (npen) overlay(f, E, br, 32 * E);
+                    uint32_t cm = 0u;
+#pragma unroll
+                    for (int e = 0; e < E; ++e)
+                        if (f[e] > tau) cm |= 1u << e;
+                    if (!__any_sync(FULL, cm != 0u)) continue;
+                    const int c = __popc(cm);
+                    int ex = c;
+#pragma unroll
+                    for (int d = 1; d < 32; d <<= 1) {
+                        const int o = __shfl_up_sync(FULL, ex, d);
+                        if (lane >= d) ex += o;
+                    }
+                    const int tot = __shfl_sync(FULL, ex, 31);
+                    ex -= c;
+                    if (cm) {
+                        int k = cnt + ex;
+#pragma unroll
+                        for (int e = 0; e < E; ++e)
+                            if ((cm >> e) & 1u) {
+                                if (k < CW) {
+                                    cv[k] = f[e];
+                                    ci[k] = (int32_t)(br + lane * E + e);
+                                }
+                                ++k;
+                            }
+                    }
+                    cnt += tot;
                 }
-                cnt += __popc(m);
-            }
-            __syncwarp();
-            if (lane == 0) {
-                s_cnt[sl] = cnt;
-                __threadfence_block();
-                s_ready[sl] = t + 1;
-            }
-            t += NPW;
-            a += (int64_t)NPW * kFaithfulSub;
+                a += SPAN;
+            } else {
+                float v[RS];
 #pragma unroll
-            for (int r = 0; r < RS; ++r) {
-                const int64_t i = a + r * 32 + lane;
-                v[r] = (t < nsub && i < V) ? ld_elem(row, i) : 0.0f;
+                for (int r = 0; r < RS; ++r) {
+                    const int64_t i = a + r * 32 + lane;
+                    v[r] = i < s1 ? ld_elem(row, i) : 0.0f;
+                }
+                if (npen) {
+                    // Element a + r * 32 + lane: overlay one 32-element row at a time.
+#pragma unroll
+                    for (int r = 0; r < RS; ++r) {
+                        float f1[8];
+                        f1[0] = v[r];
+                        overlay(f1, 1, a + r * 32, 32);
+                        v[r] = f1[0];
+                    }
+                }
+#pragma unroll
+                for (int r = 0; r < RS; ++r) {
+                    const int64_t i = a + r * 32 + lane;
+                    const bool c = i < s1 && v[r] > tau;
+                    const unsigned m = __ballot_sync(FULL, c);
+                    if (c) {
+                        const int q = cnt + __popc(m & lanemask_lt());
+                        if (q < CW) {
+                            cv[q] = v[r];
+                            ci[q] = (int32_t)i;
+                        }
+                    }
+                    cnt += __popc(m);
+                }
+                a += kFaithfulSub;
             }
         }
+        VDXS_T1(25, t_pf);
+        VDXS_T0(t_pw);
+        if (lane == 0) s_cnt[warp] = cnt;
+        __syncthreads();
+        VDXS_T1(26, t_pw);
+        int total = 0;
+        bool over = false;
+#pragma unroll
+        for (int w = 0; w < NWARPS; ++w) {
+            total += s_cnt[w];
+            over |= s_cnt[w] > CW;
+        }
+        if (over) {
+            // Again as a safe piece: every share is one scalar step, which always fits.
+            L = kMinPiece;
+            safe = true;
+            __syncthreads();
+            continue;
+        }
+        VDXS_T0(t_pr);
+        if (warp == 0) {
+            for (int w = 0; w < NWARPS; ++w) {
+                const int nw = s_cnt[w];
+                for (int c0 = 0; c0 < nw; c0 += 32) {
+                    const int c = c0 + lane;
+                    const bool valid = c < nw;
+                    const float v = valid ? rval[w * CW + c] : 0.0f;
+                    const int32_t gi = valid ? ridx[w * CW + c] : 0;
+                    unsigned pend = __ballot_sync(FULL, valid && v > mv);
+                    while (pend) {
+                        VDXS_T0(t_in);
+                        const int l = __ffs(pend) - 1;
+                        const float nv = __shfl_sync(FULL, v, l);
+                        const int32_t ngi = __shfl_sync(FULL, gi, l);
+#ifdef VDXS_TIMING
+                        if (lane == 0) atomicAdd(&g_phase_count[24], 1ull);
+#endif
+                        if (regs) {
+                            // The owner updates its key in registers; the lowest slot holding
+                            // the minimum key is in the lowest lane holding it as its first
+                            // slot, else in the lowest lane holding it as its second.
+                            if (lane == (ms & 31)) {
+                                sval[ms] = nv;
+                                sidx[ms] = ngi;
+                                const uint32_t nk = f2key(nv);
+                                if (ms >= 32) k1 = nk;
+                                else k0 = nk;
+                                kv = min(k0, k1);
+                            }
+                            const uint32_t mk = __reduce_min_sync(FULL, kv);
+                            const unsigned first = __ballot_sync(FULL, k0 == mk);
+                            ms = first ? __ffs(first) - 1 : __ffs(__ballot_sync(FULL, k1 == mk)) + 31;
+                            mv = key2f(mk);
+                        } else {
+                            if (lane == (ms & 31)) {
+                                sval[ms] = nv;
+                                sidx[ms] = ngi;
+                            }
+                            __syncwarp();
+                            // The owner's slots are rescanned by the whole warp (lane u reads
+                            // slot owner + 32*u), then the buffer minimum over the lanes' minima.
+                            const int owner = ms & 31, s2 = owner + 32 * lane;
+                            const uint32_t ok = lane < RL && s2 < K ? f2key(sval[s2]) : 0xFFFFFFFFu;
+                            const uint32_t omk = __reduce_min_sync(FULL, ok);
+                            const uint32_t obs = __reduce_min_sync(FULL, ok == omk ? (uint32_t)s2 : 0xFFFFFFFFu);
+                            if (lane == owner) {
+                                kv = omk;
+                                bs = (int)obs;
+                            }
+                            const uint32_t mk = __reduce_min_sync(FULL, kv);
+                            ms = (int)__reduce_min_sync(FULL, kv == mk ? (uint32_t)bs : 0xFFFFFFFFu);
+                            mv = key2f(mk);
+                        }
+                        pend &= ~(1u << l);
+                        pend &= __ballot_sync(FULL, valid && v > mv);
+                        VDXS_T1(28, t_in);
+                    }
+                }
+            }
+            if (lane == 0) s_mv = mv;
+        }
+        VDXS_T1(27, t_pr);
+#ifdef VDXS_TIMING
+        if (tid == 0) atomicAdd(&g_phase_count[23], (unsigned long long)total);
+#endif
+        __syncthreads();
+        pos += len;
+        if (safe) {
+            // Back to vector pieces (lengths in whole vector steps per warp).
+            safe = false;
+            L = NWARPS * SPAN;
+        } else if (total < 4 * CW) {
+            // Candidates per piece stay near K when the length tracks the position.
+            L = (int)min((int64_t)L * 2, (int64_t)1 << 24);
+        }
     }
-    __syncthreads();
     VDXS_T1(22, t_floop);
-    if (s_abort) {
-        // A wait ran out: report it; the token of this row is not valid.
-        if (tid == 0) atomicExch(p.err, kErrTimeout);
-        return;
-    }
 
     // Sequential stage 2 in slot order (Sampler.pas:385-459).
     int P2 = 32;
