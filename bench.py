@@ -294,7 +294,10 @@ def run_config_block(torch, ctx, dev, stream, clocks, peak, steps, warmup):
             for i in range(W):
                 step(i)
             torch.cuda.synchronize()
-            per, kern, launches = timed_loop(torch, ctx, lambda j: step(W + j), S, None, stream, clocks)
+            # The stage events (two extra records around the kernel) go on every 25th step:
+            # at ~19 us per step they would otherwise weigh on the mean they help explain.
+            per, kern, launches = timed_loop(torch, ctx, lambda j: step(W + j), S, None, stream, clocks,
+                                             staged_every=25)
             got = tok[W:, 0].cpu().numpy()
             xh = host_bits(torch, xs[W:])
             par = oracle_parity(cfg, xh, u_all[W:, 0].cpu().numpy(), None, None, mode, got, list(range(S)))
