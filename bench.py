@@ -10,8 +10,9 @@ configuration defined for 1..8 GPUs, so every N runs the same total work (strong
 scaling). At N=1 it is sampled unsharded; at N>1 each rank holds a contiguous vocab
 shard, selects its local top-k, and the candidates are all-gathered with NCCL.
 
-Rank 0 prints one JSON line. ``value`` is device-timed (inputs resident in HBM, L2
-flushed between steps, CUDA events around each step, max over ranks); ``e2e`` goes
+Rank 0 prints one JSON line. ``value`` is device-timed (inputs resident in HBM; the L2
+is flushed between steps unless a step's input is at least twice the L2, and config.l2
+says which; CUDA events around each step, max over ranks); ``e2e`` goes
 through the host-buffer C-ABI call with the host->device copy of the logits and the
 device->host copy of the tokens inside the timed region; ``cpu_baseline`` and
 ``--impl reference`` time the C++ restatement of TVdxSampler on the host cores.
@@ -152,7 +153,20 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
-def workload_config(name, world, spec, tie_mode):
+L2_BYTES = 126 << 20  # B200 L2
+
+
+def l2_policy(step_bytes):
+    """(flush between steps?, description): a step that reads at least twice the L2
+    needs no flush (what one step leaves in L2 is long evicted when the next step reaches
+    it); a smaller one gets a 256 MiB write between steps, outside the step events."""
+    if step_bytes >= 2 * L2_BYTES:
+        return False, (f"no flush: each step reads {step_bytes / 2**20:.0f} MiB of logits, "
+                       f"{step_bytes / L2_BYTES:.1f}x the 126 MiB L2")
+    return True, "flushed between steps (256 MiB write, outside the per-step CUDA events)"
+
+
+def workload_config(name, world, spec, tie_mode, l2_desc):
     cfg = {"workload": f"{name}: batch={spec['batch']} vocab=262144 {spec['dtype']} T={spec['temperature']} "
                        f"top_k={spec['top_k']} top_p={spec['top_p']} penalty={spec['repeat_penalty']} "
                        f"window={spec['window']} ({'vocab-sharded over %d GPUs' % world if world > 1 else 'unsharded'})",
@@ -160,7 +174,7 @@ def workload_config(name, world, spec, tie_mode):
            "top_p": spec["top_p"], "temperature": spec["temperature"],
            "parallelism": f"vocab-shard{world}" if world > 1 else "single",
            "tie_mode": "canonical" if world > 1 else tie_mode,
-           "l2": "flushed between steps (256 MiB write, outside the per-step CUDA events)"}
+           "l2": l2_desc}
     return cfg
 
 
@@ -313,11 +327,14 @@ def run_config_block(torch, ctx, dev, stream, clocks, peak, steps, warmup):
 
             def step(i, x=x, h=h, c=c, u_all=u_all, tok=tok, cfg=cfg):
                 ctx.sample(cfg, x, u_all[i], h, c, tokens=tok)
+            do_flush, l2 = l2_policy(x.numel() * x.element_size())
+            fl_buf = flush if do_flush else None
             for i in range(warmup):
                 step(i)
-                flush.zero_()
+                if fl_buf is not None:
+                    fl_buf.zero_()
             torch.cuda.synchronize()
-            per, kern, launches = timed_loop(torch, ctx, lambda j: step(warmup + j), S, flush, stream, clocks)
+            per, kern, launches = timed_loop(torch, ctx, lambda j: step(warmup + j), S, fl_buf, stream, clocks)
             # One more step outside the timed region, with flags: parity and emulated rows.
             tk, fl, _, _ = ctx.sample(cfg, x, u_all[S + warmup], h, c, want_flags=True)
             torch.cuda.synchronize()
@@ -327,7 +344,7 @@ def run_config_block(torch, ctx, dev, stream, clocks, peak, steps, warmup):
             par = oracle_parity(cfg, xh, u_all[S + warmup].cpu().numpy(), None if h is None else h.cpu().numpy(),
                                 None if c is None else c.cpu().numpy(), mode, tk.cpu().numpy(), subset_rows(B))
             esz = x.element_size()
-            nsteps, l2 = S, "flushed between steps (256 MiB write, outside the per-step events)"
+            nsteps = S
             del x
         ms = statistics.mean(per)
         alg = B * V * esz
@@ -389,11 +406,15 @@ def run_ours(args, rank, world, local):
         else:
             ctx.sample(cfg, x, u_all[i], hist, hcnt, tokens=tokens)
 
-    flush = torch.empty(16 if args.no_flush else 256 << 20, dtype=torch.uint8, device=dev)
+    do_flush, l2_desc = l2_policy(x.numel() * esz)
+    if args.no_flush:
+        do_flush, l2_desc = False, "no flush (--no-flush: profiling only)"
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if do_flush else None
     stream = torch.cuda.current_stream()
     for i in range(args.warmup):
         step(i)
-        flush.zero_()
+        if flush is not None:
+            flush.zero_()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -593,7 +614,7 @@ def run_ours(args, rank, world, local):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": spec["dtype"],
                 "data": "synthetic (seeded; distribution of the named BASELINE config)",
-                "config": workload_config(name, world, spec, args.tie_mode),
+                "config": workload_config(name, world, spec, args.tie_mode, l2_desc),
                 "latency_us": dict(lat_summary(step_max.tolist()), mean=round(ms_per_step * 1e3, 2)),
                 "latency_note": "per step: the slowest rank's CUDA-event time; mean = max over ranks of the "
                                 "summed timed region / steps" if world > 1 else "per step: CUDA-event time",
@@ -680,7 +701,8 @@ def run_reference(args, rank, world):
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": spec["dtype"],
             "data": "synthetic (seeded; distribution of the named BASELINE config)",
-            "config": workload_config(name, world, spec, "faithful"),
+            "config": workload_config(name, world, spec, "faithful",
+                                      l2_policy(B * (V // world) * (2 if spec["dtype"] == "bf16" else 4))[1]),
             "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": nt, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
