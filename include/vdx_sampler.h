@@ -355,6 +355,38 @@ VDXS_API int32_t vdxs_set_stage_events(vdxs_context* ctx, void* ev_begin, void* 
  * created (NCCL's own kernels are not counted). */
 VDXS_API int32_t vdxs_get_launch_count(const vdxs_context* ctx, int64_t* out);
 
+/* ----------------------------------------------------------------------------
+ * Unembedding in front of the sampler. Replaces TVdxModel.UnembedToLogits
+ * (src/VindexLLM.Model.pas:1258-1271: the tied-embedding matvec of
+ * shaders/matvec_q4_0.comp:45-88 on the normed hidden vector) followed by
+ * TVdxSampler.Process, so the logits never leave the GPU. The weights are the
+ * reference's Q4_0 blocks (18 bytes per 32 elements: fp16 scale, 16 bytes of
+ * nibbles, element j low nibble of byte j, element j + 16 high nibble), row-major
+ * [out_dim][in_dim / 32]. The logits equal the shader's bit for bit: per row 64
+ * partial sums over elements t, t + 64, ... with every product and sum rounded to
+ * fp32 (no fused multiply-add), then the pairwise tree over strides 32..1.
+ * ---------------------------------------------------------------------------- */
+typedef struct vdxs_q4_0_weights vdxs_q4_0_weights;
+/* Repacks the device Q4_0 matrix once into the library's lane-major layout (the same
+ * number of bytes) on the context's device; synchronises `stream`. in_dim must be a
+ * multiple of 32. The source may be freed afterwards. No reference counterpart (the
+ * reference uploads its GGUF blocks once, Model.pas:978-982). */
+VDXS_API int32_t vdxs_q4_0_prepare(vdxs_context* ctx, const void* d_q4_0, int32_t in_dim,
+                                   int32_t out_dim, void* stream, vdxs_q4_0_weights** out);
+VDXS_API int32_t vdxs_q4_0_release(vdxs_q4_0_weights* w);
+/* logits[batch][out_dim] = hidden[batch][in_dim] x weights^T (the shader's arithmetic).
+ * Batches above 8 rows are computed 8 rows at a time. */
+VDXS_API int32_t vdxs_unembed_q4_0(vdxs_context* ctx, const vdxs_q4_0_weights* w,
+                                   const float* d_hidden, int32_t batch, float* d_logits,
+                                   void* stream);
+/* vdxs_unembed_q4_0 into a context-owned logits buffer, then vdxs_sample on it. */
+VDXS_API int32_t vdxs_sample_unembed_q4_0(vdxs_context* ctx, const vdxs_config* cfg,
+                                          const vdxs_q4_0_weights* w, const float* d_hidden,
+                                          int32_t batch, const int32_t* d_history,
+                                          int64_t history_stride, const int32_t* d_history_count,
+                                          const float* d_uniform, int32_t* d_out_tokens,
+                                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif

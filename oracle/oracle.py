@@ -72,6 +72,9 @@ def lib():
                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                         C.c_void_p, C.c_void_p, C.c_int32, C.c_int32]
         L.vdxo_sample_batch.restype = C.c_int32
+        L.vdxo_matvec_q4_0.argtypes = [C.c_void_p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32, C.c_void_p,
+                                       C.c_int32]
+        L.vdxo_matvec_q4_0.restype = C.c_int32
         _lib = L
     return _lib
 
@@ -187,3 +190,19 @@ def sample_batch(cfg: VdxsConfig, logits: np.ndarray, uniforms: np.ndarray, hist
     if rc != 0:
         raise ValueError("vdxo_sample_batch rejected its arguments")
     return tokens, flags, oi, op
+
+
+def matvec_q4_0(weights: np.ndarray, x: np.ndarray, nthreads: int = 1) -> np.ndarray:
+    """Unembedding as shaders/matvec_q4_0.comp computes it: ``weights`` is [out_dim,
+    in_dim / 32 * 18] uint8 (Q4_0 blocks, row-major), ``x`` is [batch, in_dim] float32;
+    returns [batch, out_dim] float32."""
+    w = np.ascontiguousarray(weights, np.uint8)
+    xx = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    batch, in_dim = xx.shape
+    out_dim = w.shape[0]
+    assert w.shape[1] == in_dim // 32 * 18 and in_dim % 32 == 0
+    out = np.empty((batch, out_dim), np.float32)
+    rc = lib().vdxo_matvec_q4_0(_ptr(w), _ptr(xx), batch, in_dim, out_dim, _ptr(out), nthreads)
+    if rc != 0:
+        raise ValueError("vdxo_matvec_q4_0: bad arguments")
+    return out

@@ -638,3 +638,80 @@ int32_t vdxo_sample_batch(const vdxs_config* cfg, int32_t tie_mode, const void* 
 }
 
 }  // extern "C"
+
+// ---- unembedding: shaders/matvec_q4_0.comp:45-88 -------------------------------------
+namespace {
+
+// IEEE binary16 -> binary32 (unpackHalf2x16, exact for every encoding).
+float half_to_float(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t ex = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+    uint32_t bits;
+    if (ex == 0) {
+        if (man == 0) {
+            bits = sign;
+        } else {  // subnormal: normalise
+            int e = -1;
+            uint32_t m = man;
+            do {
+                ++e;
+                m <<= 1;
+            } while ((m & 0x400u) == 0);
+            bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((m & 0x3FFu) << 13);
+        }
+    } else if (ex == 0x1F) {
+        bits = sign | 0x7F800000u | (man << 13);
+    } else {
+        bits = sign | ((ex + 127 - 15) << 23) | (man << 13);
+    }
+    float f;
+    std::memcpy(&f, &bits, 4);
+    return f;
+}
+
+// One output row (matvec_q4_0.comp:45-88): 64 invocations each accumulate the elements
+// tid, tid + 64, ... in order (acc += qval * scale * x, evaluated left to right with
+// every operation rounded to float), then the shared-memory tree over strides 32..1.
+float matvec_q4_0_row(const uint8_t* w, const float* x, int in_dim, int row) {
+    const size_t blocks_per_row = (size_t)in_dim >> 5;
+    const size_t row_byte_off = (size_t)row * blocks_per_row * 18u;
+    float partial[64];
+    for (int tid = 0; tid < 64; ++tid) {
+        float acc = 0.0f;
+        for (int elem = tid; elem < in_dim; elem += 64) {
+            const size_t blk_off = row_byte_off + (size_t)(elem >> 5) * 18u;
+            const int in_blk = elem & 31;
+            const int byte_idx = in_blk & 15;
+            const int is_high = in_blk >> 4;
+            const float scale = half_to_float((uint16_t)(w[blk_off] | (w[blk_off + 1] << 8)));
+            const uint32_t raw = w[blk_off + 2 + byte_idx];
+            const uint32_t nibble = (raw >> (is_high * 4)) & 0x0Fu;
+            const float qval = (float)((int)nibble - 8);
+            const float qs = qval * scale;  // exact: a 4-bit integer times an fp16 value
+            const float t = qs * x[elem];
+            acc = acc + t;
+        }
+        partial[tid] = acc;
+    }
+    for (int stride = 32; stride > 0; stride >>= 1)
+        for (int tid = 0; tid < stride; ++tid) partial[tid] = partial[tid] + partial[tid + stride];
+    return partial[0];
+}
+
+}  // namespace
+
+int32_t vdxo_matvec_q4_0(const uint8_t* weights, const float* x, int32_t batch, int32_t in_dim,
+                         int32_t out_dim, float* out, int32_t nthreads) {
+    if (!weights || !x || !out || batch <= 0 || in_dim <= 0 || (in_dim & 31) || out_dim <= 0) return -1;
+    if (nthreads <= 0) nthreads = 1;
+    auto work = [&](int t) {
+        for (int r = t; r < out_dim; r += nthreads)
+            for (int b = 0; b < batch; ++b)
+                out[(size_t)b * out_dim + r] = matvec_q4_0_row(weights, x + (size_t)b * in_dim, in_dim, r);
+    };
+    std::vector<std::thread> th;
+    for (int t = 1; t < nthreads; ++t) th.emplace_back(work, t);
+    work(0);
+    for (auto& h : th) h.join();
+    return 0;
+}

@@ -64,6 +64,16 @@ VDXO_API int32_t vdxo_sample_batch(const vdxs_config* cfg, int32_t tie_mode,
                                    int32_t* out_idx, float* out_prob, int32_t out_k,
                                    int32_t nthreads);
 
+/* The tied-embedding unembedding of TVdxModel.UnembedToLogits (Model.pas:1258-1271) as
+ * shaders/matvec_q4_0.comp computes it (:45-88): out[r] = row r of the Q4_0 matrix
+ * (18-byte blocks: fp16 scale, 16 bytes of nibbles) times x, summed by 64 partial sums
+ * (element e goes to partial e mod 64, in order) and a pairwise tree (strides 32..1).
+ * `batch` input vectors of in_dim floats give batch rows of out_dim floats. in_dim must
+ * be a multiple of 32. Returns 0, or -1 on bad arguments. */
+VDXO_API int32_t vdxo_matvec_q4_0(const uint8_t* weights, const float* x, int32_t batch,
+                                  int32_t in_dim, int32_t out_dim, float* out,
+                                  int32_t nthreads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -60,6 +60,10 @@ SIGNATURES = {
     "vdxs_device_status": (i32, [vp, vp]),
     "vdxs_set_stage_events": (i32, [vp, vp, vp]),
     "vdxs_get_launch_count": (i32, [vp, P(i64)]),
+    "vdxs_q4_0_prepare": (i32, [vp, vp, i32, i32, vp, P(vp)]),
+    "vdxs_q4_0_release": (i32, [vp]),
+    "vdxs_unembed_q4_0": (i32, [vp, vp, vp, i32, vp, vp]),
+    "vdxs_sample_unembed_q4_0": (i32, [vp, P(VdxsConfig), vp, vp, i32, vp, i64, vp, vp, vp, vp]),
 }
 
 

@@ -21,7 +21,7 @@ BUILD_DIR = os.path.join(HERE, "_build")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
               "-I" + INCLUDE, "--expt-relaxed-constexpr"]
-SOURCES = ["vdxs_kernels.cu", "vdxs_api.cpp"]
+SOURCES = ["vdxs_kernels.cu", "vdxs_unembed.cu", "vdxs_api.cpp"]
 
 
 def _nvcc() -> str:

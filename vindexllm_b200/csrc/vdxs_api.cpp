@@ -1167,3 +1167,100 @@ VDXS_API int32_t vdxs_sample_sharded(vdxs_context* ctx, vdxs_comm* comm, const v
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------
+// Unembedding: TVdxModel.UnembedToLogits (Model.pas:1258-1271) with the tied Q4_0
+// embedding matvec of shaders/matvec_q4_0.comp (:45-88), in front of the sampler.
+// ---------------------------------------------------------------------------------
+struct vdxs_q4_0_weights {
+    int device = 0;
+    int in_dim = 0;
+    int out_dim = 0;
+    uint32_t* nib = nullptr;
+    uint16_t* scales = nullptr;
+};
+
+extern "C" {
+
+VDXS_API int32_t vdxs_q4_0_prepare(vdxs_context* ctx, const void* d_q4_0, int32_t in_dim, int32_t out_dim,
+                                   void* stream, vdxs_q4_0_weights** out) {
+    if (!ctx) return fail(nullptr, VDXS_E_INVALID_ARG, "context is NULL");
+    if (!d_q4_0 || !out) return fail(ctx, VDXS_E_INVALID_ARG, "weights or output pointer is NULL");
+    *out = nullptr;
+    if (in_dim <= 0 || (in_dim % 32) != 0)
+        return fail(ctx, VDXS_E_INVALID_ARG, "in_dim %d is not a positive multiple of 32 (Q4_0 blocks)", in_dim);
+    if (out_dim <= 0) return fail(ctx, VDXS_E_INVALID_ARG, "out_dim must be >= 1 (got %d)", out_dim);
+    if (unembed_chunk_rows(in_dim) < 1)
+        return fail(ctx, VDXS_E_UNSUPPORTED, "in_dim %d: one input vector does not fit the matvec's shared memory",
+                    in_dim);
+    DeviceGuard g(ctx->device);
+    auto* w = new vdxs_q4_0_weights();
+    w->device = ctx->device;
+    w->in_dim = in_dim;
+    w->out_dim = out_dim;
+    const size_t nw = (size_t)q4_0_words_per_lane(in_dim);
+    cudaError_t e = cudaMalloc((void**)&w->nib, (size_t)out_dim * nw * 32 * sizeof(uint32_t));
+    if (e == cudaSuccess) e = cudaMalloc((void**)&w->scales, (size_t)out_dim * nw * 8 * sizeof(uint16_t));
+    if (e == cudaSuccess) e = q4_0_repack((const uint8_t*)d_q4_0, in_dim, out_dim, w->nib, w->scales, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) {
+        cudaFree(w->nib);
+        cudaFree(w->scales);
+        delete w;
+        return e == cudaErrorMemoryAllocation ? fail(ctx, VDXS_E_NO_MEMORY, "Q4_0 weight allocation failed")
+                                              : cuda_fail(ctx, e, "Q4_0 repack");
+    }
+    ctx->launches += 1;
+    *out = w;
+    ok(ctx);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_q4_0_release(vdxs_q4_0_weights* w) {
+    if (!w) return VDXS_OK;
+    DeviceGuard g(w->device);
+    cudaFree(w->nib);
+    cudaFree(w->scales);
+    delete w;
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_unembed_q4_0(vdxs_context* ctx, const vdxs_q4_0_weights* w, const float* d_hidden,
+                                   int32_t batch, float* d_logits, void* stream) {
+    if (!ctx) return fail(nullptr, VDXS_E_INVALID_ARG, "context is NULL");
+    if (!w || !d_hidden || !d_logits) return fail(ctx, VDXS_E_INVALID_ARG, "weights, hidden or logits pointer is NULL");
+    if (batch < 1) return fail(ctx, VDXS_E_INVALID_ARG, "batch must be >= 1 (got %d)", batch);
+    if (w->device != ctx->device)
+        return fail(ctx, VDXS_E_INVALID_ARG, "weights live on device %d, the context on device %d", w->device,
+                    ctx->device);
+    DeviceGuard g(ctx->device);
+    int launches = 0;
+    cudaError_t e = q4_0_matvec(w->nib, w->scales, w->in_dim, w->out_dim, d_hidden, batch, d_logits,
+                                (cudaStream_t)stream, &launches);
+    ctx->launches += launches;
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "unembedding matvec");
+    ok(ctx);
+    return VDXS_OK;
+}
+
+VDXS_API int32_t vdxs_sample_unembed_q4_0(vdxs_context* ctx, const vdxs_config* cfg, const vdxs_q4_0_weights* w,
+                                          const float* d_hidden, int32_t batch, const int32_t* d_history,
+                                          int64_t history_stride, const int32_t* d_history_count,
+                                          const float* d_uniform, int32_t* d_out_tokens, void* stream) {
+    if (!ctx) return fail(nullptr, VDXS_E_INVALID_ARG, "context is NULL");
+    if (!w) return fail(ctx, VDXS_E_INVALID_ARG, "weights pointer is NULL");
+    if (batch < 1) return fail(ctx, VDXS_E_INVALID_ARG, "batch must be >= 1 (got %d)", batch);
+    DeviceGuard g(ctx->device);
+    // The logits stay in a context buffer; for decode batches they are still in L2 when
+    // the sampler streams them.
+    cudaError_t e = grow_dev(&ctx->ws.unembed_logits, &ctx->ws.unembed_cap, (size_t)batch * (size_t)w->out_dim,
+                             (cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(ctx, VDXS_E_NO_MEMORY, "logits buffer allocation failed");
+    int32_t rc = vdxs_unembed_q4_0(ctx, w, d_hidden, batch, ctx->ws.unembed_logits, stream);
+    if (rc != VDXS_OK) return rc;
+    return vdxs_sample_ex(ctx, cfg, ctx->ws.unembed_logits, VDXS_DTYPE_F32, batch, w->out_dim, w->out_dim, d_history,
+                          history_stride, d_history_count, d_uniform, d_out_tokens, nullptr, nullptr, nullptr, 0,
+                          stream);
+}
+
+}  // extern "C"

@@ -18,6 +18,10 @@ constexpr int kTauStride = 32;       // words between rows of the stream path's 
 
 enum Path : int { kGreedy = 0, kTopK = 1, kFull = 2 };
 
+// Unembedding matvec (vdxs_unembed.cu): input rows per launch and their shared memory.
+constexpr int kMaxUnembedBatch = 8;
+constexpr size_t kUnembedSmemBytes = 200 * 1024;
+
 // Device workspace owned by a context (TVdxSampler.EnsureWorkspace analogue,
 // Sampler.pas:250-263). Grown on demand; never shrunk until the context dies.
 struct Workspace {
@@ -47,6 +51,8 @@ struct Workspace {
     size_t shard_send_cap = 0, shard_recv_cap = 0;
     uint64_t* lk_buf = nullptr;     // top_k above the stream path's maximum: per-CTA sort buffers and slots
     size_t lk_cap = 0;              // 64-bit words
+    float* unembed_logits = nullptr;  // vdxs_sample_unembed_q4_0: [rows * vocab] logits
+    size_t unembed_cap = 0;
     int32_t* err = nullptr;         // device error word (0 = ok)
     // host-buffer entry point staging
     void* d_logits = nullptr;
@@ -125,6 +131,14 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
                              cudaStream_t stream, std::string* err);
 cudaError_t launch_sample(const SampleArgs& a, const LaunchPlan& plan, Workspace& ws, std::string* err);
 cudaError_t launch_merge_draw(const SampleArgs& a, int ranks, Workspace& ws, std::string* err);
+// Unembedding (vdxs_unembed.cu): Q4_0 repack and the matvec in the reference shader's order.
+int q4_0_words_per_lane(int in_dim);
+size_t q4_0_packed_bytes(int in_dim, int out_dim);
+int unembed_chunk_rows(int in_dim);
+cudaError_t q4_0_repack(const uint8_t* src, int in_dim, int out_dim, uint32_t* nib, uint16_t* scales,
+                        cudaStream_t stream);
+cudaError_t q4_0_matvec(const uint32_t* nib, const uint16_t* scales, int in_dim, int out_dim, const float* x,
+                        int batch, float* out, cudaStream_t stream, int* launches);
 // Device-resident decode state (one thread per row).
 cudaError_t launch_device_uniforms(uint64_t* prng, int batch, float* out, cudaStream_t stream);
 cudaError_t launch_history_push(int32_t* hist, int32_t* pos, int32_t* count, int window, const int32_t* tokens,

@@ -3597,6 +3597,7 @@ void free_workspace(Workspace& ws) {
     cudaFree(ws.shard_send);
     cudaFree(ws.shard_recv);
     cudaFree(ws.lk_buf);
+    cudaFree(ws.unembed_logits);
     cudaFree(ws.err);
     cudaFree(ws.d_logits);
     cudaFree(ws.d_hist);

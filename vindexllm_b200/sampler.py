@@ -354,3 +354,57 @@ class ShardComm:
                                           _dptr(uniforms), _dptr(tokens), _dptr(flags), _stream_ptr(stream))
         check(rc, self.ctx.handle)
         return (tokens, flags) if want_flags else tokens
+
+
+class Q4Weights:
+    """A Q4_0 unembedding matrix prepared on a context's device (vdxs_q4_0_prepare):
+    TVdxModel.UnembedToLogits (src/VindexLLM.Model.pas:1258-1271) with the matvec of
+    shaders/matvec_q4_0.comp, in front of the sampler."""
+
+    def __init__(self, ctx: SamplerContext, q4_0, in_dim: int, out_dim: int, stream=None):
+        """``q4_0``: a uint8 CUDA tensor holding [out_dim, in_dim / 32 * 18] Q4_0 blocks."""
+        assert q4_0.is_cuda and q4_0.is_contiguous() and q4_0.numel() == out_dim * (in_dim // 32) * 18
+        self.ctx = ctx
+        self.lib = ctx.lib
+        self.in_dim, self.out_dim = in_dim, out_dim
+        h = C.c_void_p()
+        check(self.lib.vdxs_q4_0_prepare(ctx.handle, _dptr(q4_0), in_dim, out_dim, _stream_ptr(stream),
+                                         C.byref(h)), ctx.handle)
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.lib.vdxs_q4_0_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def unembed(self, hidden, logits=None, stream=None):
+        """logits [batch, out_dim] float32 = hidden [batch, in_dim] x weights^T."""
+        import torch
+        assert hidden.is_cuda and hidden.dtype == torch.float32 and hidden.is_contiguous()
+        hidden = hidden.reshape(-1, self.in_dim)
+        if logits is None:
+            logits = torch.empty(hidden.shape[0], self.out_dim, dtype=torch.float32, device=hidden.device)
+        check(self.lib.vdxs_unembed_q4_0(self.ctx.handle, self._h, _dptr(hidden), hidden.shape[0], _dptr(logits),
+                                         _stream_ptr(stream)), self.ctx.handle)
+        return logits
+
+    def sample(self, cfg: VdxsConfig, hidden, uniforms=None, history=None, history_count=None, tokens=None,
+               stream=None):
+        """vdxs_sample_unembed_q4_0: unembedding and sampling in one call; returns tokens."""
+        import torch
+        assert hidden.is_cuda and hidden.dtype == torch.float32 and hidden.is_contiguous()
+        hidden = hidden.reshape(-1, self.in_dim)
+        B = hidden.shape[0]
+        if tokens is None:
+            tokens = torch.empty(B, dtype=torch.int32, device=hidden.device)
+        hs = history.shape[1] if history is not None else 1
+        check(self.lib.vdxs_sample_unembed_q4_0(self.ctx.handle, C.byref(cfg), self._h, _dptr(hidden), B,
+                                                _dptr(history), hs, _dptr(history_count), _dptr(uniforms),
+                                                _dptr(tokens), _stream_ptr(stream)), self.ctx.handle)
+        return tokens

@@ -142,3 +142,28 @@ def make_uniforms(name: str, steps: int, batch: int | None = None) -> np.ndarray
     B = CONFIGS[name]["batch"] if batch is None else batch
     seeds = np.arange(B, dtype=np.uint64) + np.uint64(_SEED_BASE[name] * 7 + 1)
     return uniform_streams(seeds, steps)
+
+
+# Unembedding inputs (TVdxModel.UnembedToLogits, Model.pas:1258-1271): a tied Gemma-3
+# sized embedding (262144 x 2560) in Q4_0 and normed hidden vectors. No checkpoint is
+# available, so the blocks are seeded: fp16 scales ~ |N(0, 0.02)|, uniform nibbles.
+HIDDEN = 2560
+
+
+def make_q4_0(vocab: int = VOCAB, hidden: int = HIDDEN, seed: int = 7000, device: str = "cuda"):
+    """[vocab, hidden / 32 * 18] uint8 Q4_0 blocks as a torch tensor on ``device`` (seeded
+    per device): fp16 scale, then 16 bytes whose low nibbles are elements 0..15 and high
+    nibbles elements 16..31 of the block."""
+    import torch
+    assert hidden % 32 == 0
+    g = torch.Generator(device=device).manual_seed(seed)
+    nb = hidden // 32
+    out = torch.randint(0, 256, (vocab, nb, 18), dtype=torch.uint8, device=device, generator=g)
+    scales = (torch.randn((vocab, nb), device=device, generator=g).abs() * 0.02).to(torch.float16)
+    out[:, :, 0:2] = scales.view(torch.uint8).reshape(vocab, nb, 2)
+    return out.reshape(vocab, nb * 18)
+
+
+def make_hidden(batch: int, hidden: int = HIDDEN, seed: int = 7100) -> np.ndarray:
+    """[batch, hidden] float32 hidden vectors (RMS-normed scale: ~N(0, 1) entries)."""
+    return np.random.default_rng(seed).normal(size=(batch, hidden)).astype(np.float32)
