@@ -59,41 +59,94 @@ __global__ void q4_0_repack_kernel(const uint8_t* __restrict__ src, int nb, int 
     }
 }
 
+// Packed fp32 pairs (sm_100 f32x2): both halves rounded to nearest, exactly as two
+// scalar operations.
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+    uint64_t d;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float lo2(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float hi2(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+
+// Each lane carries its two partial sums (even blocks, odd blocks) as one packed pair, so
+// a block pair costs two scalar multiplies and one packed add per input vector (a packed
+// multiply feeding a packed add was contracted into a fused multiply-add by the
+// compiler, which changes the rounding the shader's sums have). The input
+// vectors sit in shared memory as pairs (x[64k + l], x[64k + 32 + l]); a missing odd
+// block (an odd block count) has x = 0, weight 0 and adds +0.0, which leaves a
+// round-to-nearest sum started at +0 unchanged.
 template <int B>
 __global__ void __launch_bounds__(kUThreads) q4_0_matvec_kernel(const uint32_t* __restrict__ nib,
                                                                 const uint16_t* __restrict__ scales,
                                                                 const float* __restrict__ x, int in_dim,
                                                                 int out_dim, float* __restrict__ out) {
-    extern __shared__ float xs[];  // [B][in_dim]
-    const int nb = in_dim >> 5, nw = (nb + 7) >> 3;
-    for (int i = threadIdx.x; i < B * in_dim; i += kUThreads) xs[i] = x[i];
+    extern __shared__ float2 xs2[];  // [B][npairs][32]
+    const int nb = in_dim >> 5, nw = (nb + 7) >> 3, npairs = (nb + 1) >> 1;
+    for (int i = threadIdx.x; i < B * npairs * 32; i += kUThreads) {
+        const int l = i & 31, k = (i >> 5) % npairs, b = (i >> 5) / npairs;
+        const int e0 = 64 * k + l, e1 = e0 + 32;
+        xs2[i] = make_float2(x[(int64_t)b * in_dim + e0], e1 < in_dim ? x[(int64_t)b * in_dim + e1] : 0.0f);
+    }
     __syncthreads();
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * kUWarps;
+    const uint64_t kMagic8 = pk2(-8388616.0f, -8388616.0f);  // -(2^23 + 8)
+    // A row's words are read kWChunk at a time, all loads of a chunk issued before any is
+    // used; lane c of the warp also loads the chunk's c-th group of eight scales, which
+    // reaches the other lanes by shuffles.
+    constexpr int kWChunk = 16;
     for (int row = blockIdx.x * kUWarps + (threadIdx.x >> 5); row < out_dim; row += warps) {
         const uint32_t* nr = nib + (int64_t)row * nw * 32 + lane;
         const uint4* sr = reinterpret_cast<const uint4*>(scales + (int64_t)row * nw * 8);
-        float acc_even[B], acc_odd[B];
+        uint64_t acc[B];
 #pragma unroll
-        for (int b = 0; b < B; ++b) acc_even[b] = acc_odd[b] = 0.0f;
-        for (int w = 0; w < nw; ++w) {
-            const uint32_t word = __ldg(nr + w * 32);
-            const uint4 s4 = __ldg(sr + w);
-            const uint32_t sw[4] = {s4.x, s4.y, s4.z, s4.w};
+        for (int b = 0; b < B; ++b) acc[b] = 0ull;  // (+0, +0)
+        for (int w0 = 0; w0 < nw; w0 += kWChunk) {
+            const int nc = min(kWChunk, nw - w0);
+            uint32_t words[kWChunk];
 #pragma unroll
-            for (int m = 0; m < 8; ++m) {
-                const int j = 8 * w + m;
-                if (j < nb) {
-                    const uint16_t hb = (uint16_t)(sw[m >> 1] >> (16 * (m & 1)));
-                    const float scale = __half2float(__ushort_as_half(hb));
-                    const float qval = (float)((int)((word >> (4 * m)) & 15u) - 8);
-                    const float qs = __fmul_rn(qval, scale);  // exact
-                    const float* xj = xs + 32 * j + lane;
+            for (int c = 0; c < kWChunk; ++c) words[c] = c < nc ? __ldg(nr + (w0 + c) * 32) : 0u;
+            const uint4 s4 = lane < nc ? __ldg(sr + w0 + lane) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-                    for (int b = 0; b < B; ++b) {
-                        const float t = __fmul_rn(qs, xj[b * in_dim]);
-                        if (m & 1) acc_odd[b] = __fadd_rn(acc_odd[b], t);
-                        else acc_even[b] = __fadd_rn(acc_even[b], t);
+            for (int c = 0; c < kWChunk; ++c) {
+                if (c >= nc) break;
+                const int w = w0 + c;
+                const uint32_t sw[4] = {__shfl_sync(FULLMASK, s4.x, c), __shfl_sync(FULLMASK, s4.y, c),
+                                        __shfl_sync(FULLMASK, s4.z, c), __shfl_sync(FULLMASK, s4.w, c)};
+                const uint32_t word = words[c];
+#pragma unroll
+                for (int m = 0; m < 8; m += 2) {
+                    const int k = 4 * w + (m >> 1);  // block pair (2k, 2k + 1)
+                    if (k < npairs) {
+                        // nibble - 8 for both blocks: 2^23 + nibble as a float, minus 2^23 + 8.
+                        const float fa = __uint_as_float(0x4B000000u | ((word >> (4 * m)) & 15u));
+                        const float fb = __uint_as_float(0x4B000000u | ((word >> (4 * m + 4)) & 15u));
+                        const uint64_t q = add2(pk2(fa, fb), kMagic8);
+                        const uint32_t sp = sw[m >> 1];  // scales of blocks 8w + m and 8w + m + 1
+                        const float s0 = __half2float(__ushort_as_half((unsigned short)(sp & 0xFFFFu)));
+                        const float s1 = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
+                        const uint64_t qs = mul2(q, pk2(s0, s1));  // exact
+                        const float2* xk = xs2 + k * 32 + lane;
+#pragma unroll
+                        for (int b = 0; b < B; ++b) {
+                            const float2 xv = xk[b * npairs * 32];
+                            // Scalar products (.rn: never contracted into a fused multiply-add
+                            // with the sum), then one packed add.
+                            const float t0 = __fmul_rn(lo2(qs), xv.x);
+                            const float t1 = __fmul_rn(hi2(qs), xv.y);
+                            acc[b] = add2(acc[b], pk2(t0, t1));
+                        }
                     }
                 }
             }
@@ -101,7 +154,7 @@ __global__ void __launch_bounds__(kUThreads) q4_0_matvec_kernel(const uint32_t* 
 #pragma unroll
         for (int b = 0; b < B; ++b) {
             // Stride 32: partial[l] + partial[l + 32]; then strides 16 .. 1.
-            float p = __fadd_rn(acc_even[b], acc_odd[b]);
+            float p = __fadd_rn(lo2(acc[b]), hi2(acc[b]));
 #pragma unroll
             for (int s = 16; s > 0; s >>= 1) p = __fadd_rn(p, __shfl_down_sync(FULLMASK, p, s));
             if (lane == 0) out[(int64_t)b * out_dim + row] = p;
@@ -112,7 +165,7 @@ __global__ void __launch_bounds__(kUThreads) q4_0_matvec_kernel(const uint32_t* 
 template <int B>
 cudaError_t launch_matvec(const uint32_t* nib, const uint16_t* scales, const float* x, int in_dim, int out_dim,
                           float* out, cudaStream_t stream) {
-    const size_t smem = (size_t)B * in_dim * sizeof(float);
+    const size_t smem = (size_t)B * (((in_dim >> 5) + 1) / 2) * 32 * sizeof(float2);
     cudaError_t e = cudaFuncSetAttribute(q4_0_matvec_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 148, per_sm = 1;
@@ -131,8 +184,10 @@ cudaError_t launch_matvec(const uint32_t* nib, const uint16_t* scales, const flo
 int q4_0_words_per_lane(int in_dim) { return ((in_dim >> 5) + 7) >> 3; }
 
 int unembed_chunk_rows(int in_dim) {
-    // The chunk's input vectors live in shared memory (at most kUnembedSmemBytes).
-    return std::min(kMaxUnembedBatch, (int)(kUnembedSmemBytes / ((size_t)4 * std::max(in_dim, 1))));
+    // The chunk's input vectors live in shared memory as float2 pairs of 64-element
+    // groups (at most kUnembedSmemBytes).
+    const size_t per_row = (size_t)(((in_dim >> 5) + 1) / 2) * 32 * 8;
+    return std::min(kMaxUnembedBatch, (int)(kUnembedSmemBytes / std::max<size_t>(per_row, 1)));
 }
 
 size_t q4_0_packed_bytes(int in_dim, int out_dim) {
