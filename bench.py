@@ -361,6 +361,60 @@ def run_config_block(torch, ctx, dev, stream, clocks, peak, steps, warmup):
     return out
 
 
+def run_unembed_block(torch, ctx, dev, stream, clocks, peak, steps=50):
+    """The unembedding in front of the sampler (vdxs_sample_unembed_q4_0): a Gemma-3 sized
+    tied embedding (262144 x 2560, Q4_0, 377 MB: above L2, no flush) times fresh hidden
+    vectors each step, then c0's sampling configuration. The matvec alone is timed in a
+    second loop for its fraction of the HBM peak (weight bytes per launch)."""
+    import numpy as np
+    from oracle import oracle
+    from vindexllm_b200 import abi, synth
+    from vindexllm_b200.sampler import Q4Weights
+    V, H = synth.VOCAB, synth.HIDDEN
+    wq = synth.make_q4_0(V, H, device=str(dev))
+    w = Q4Weights(ctx, wq, H, V)
+    wq_host = wq.cpu().numpy()
+    del wq
+    wbytes = V * (H // 32) * 18
+    cfg = synth.sampler_config("c0")
+    ctx.set_tie_mode(abi.TIES_FAITHFUL)
+    out = {}
+    for B in (1, 8):
+        W = 5
+        xs = torch.as_tensor(synth.make_hidden((steps + W + 1) * B, H), device=dev).view(steps + W + 1, B, H)
+        us = torch.as_tensor(synth.make_uniforms("c0", steps + W + 1, batch=B), device=dev)
+        tok = torch.empty(B, dtype=torch.int32, device=dev)
+        logits = torch.empty(B, V, dtype=torch.float32, device=dev)
+        for i in range(W):
+            w.sample(cfg, xs[i], us[i], tokens=tok)
+        torch.cuda.synchronize()
+        per, _, launches = timed_loop(torch, ctx, lambda j: w.sample(cfg, xs[W + j], us[W + j], tokens=tok), steps,
+                                      None, stream, clocks, staged_every=steps + 1)
+        mv, _, _ = timed_loop(torch, ctx, lambda j: w.unembed(xs[W + j], logits), steps, None, stream, clocks,
+                              staged_every=steps + 1)
+        # One more step outside the timed regions, against the oracle (the shader's matvec,
+        # then the restated sampler).
+        xl = xs[steps + W]
+        got = w.sample(cfg, xl, us[steps + W]).cpu().numpy()
+        ol = oracle.matvec_q4_0(wq_host, xl.cpu().numpy(), nthreads=max(1, min(32, os.cpu_count() or 1)))
+        ot = oracle.sample_batch(cfg, ol, us[steps + W].cpu().numpy(), None, None, abi.TIES_FAITHFUL,
+                                 nthreads=B)[0]
+        ms = statistics.mean(per)
+        mv_ms = statistics.mean(mv)
+        out[f"unembed_c0_b{B}"] = {
+            "batch": B, "hidden": H, "vocab": V, "weights": "Q4_0 tied embedding, 377 MB (seeded)",
+            "api": "vdxs_sample_unembed_q4_0", "steps": steps, "l2": "weights 3x the L2, no flush",
+            "tokens_per_s": round(B / (ms / 1e3), 1), "ms_per_step": round(ms, 5), "latency_us": lat_summary(per),
+            "dominant_kernel": {"name": "vdxs::q4_0_matvec_kernel (shader-order Q4_0 matvec)",
+                                "ms": round(mv_ms, 5), "frac": round(wbytes / (mv_ms / 1e3) / 1e9 / peak, 4),
+                                "alg_bytes": wbytes},
+            "gpu_launches_per_step": round(launches / steps, 2),
+            "parity": {"rows": B, "mismatches": int((got != ot).sum()), "oracle": "vdxo_matvec_q4_0 + vdxo_sample_batch"}}
+        del xs
+    w.close()
+    return out
+
+
 def run_ours(args, rank, world, local):
     import numpy as np
     import torch
@@ -606,6 +660,7 @@ def run_ours(args, rank, world, local):
     configs = None
     if world == 1 and not args.profile and not args.no_configs:
         configs = run_config_block(torch, ctx, dev, stream, clocks, peak, args.config_steps, 3)
+        configs.update(run_unembed_block(torch, ctx, dev, stream, clocks, peak))
         ctx.set_tie_mode(mode)
     clocks.stop()
 
