@@ -18,11 +18,12 @@ def _weights(ctx, V, H, seed):
     return wq, Q4Weights(ctx, wq, H, V)
 
 
-@pytest.mark.parametrize("H", [64, 96, 2560])
+@pytest.mark.parametrize("H", [64, 96, 1152, 2560, 3840])
 @pytest.mark.parametrize("B", [1, 3, 8, 11])
 def test_unembed_logits_bit_exact(gpu_ctx, oracle_mod, H, B):
-    """Odd block counts (H = 96: the last partials take one term fewer), batches across
-    the 8-row launch chunks."""
+    """Odd block counts (H = 96: the last partials take one term fewer), the hidden sizes
+    with specialised kernels (1152: a padded last word, 2560, 3840), batches across the
+    8/4/2/1-row launch chunks."""
     import torch
     V = 3001
     wq, w = _weights(gpu_ctx, V, H, seed=H + B)

@@ -24,6 +24,8 @@
 
 namespace vdxs {
 
+int q4_0_words_per_lane(int in_dim);
+
 namespace {
 
 constexpr unsigned FULLMASK = 0xFFFFFFFFu;
@@ -86,7 +88,7 @@ __device__ __forceinline__ float hi2(uint64_t v) { return __uint_as_float((uint3
 // vectors sit in shared memory as pairs (x[64k + l], x[64k + 32 + l]); a missing odd
 // block (an odd block count) has x = 0, weight 0 and adds +0.0, which leaves a
 // round-to-nearest sum started at +0 unchanged.
-template <int B>
+template <int B, int NW>
 __global__ void __launch_bounds__(kUThreads) q4_0_matvec_kernel(const uint32_t* __restrict__ nib,
                                                                 const uint16_t* __restrict__ scales,
                                                                 const float* __restrict__ x, int in_dim,
@@ -112,41 +114,60 @@ __global__ void __launch_bounds__(kUThreads) q4_0_matvec_kernel(const uint32_t* 
         uint64_t acc[B];
 #pragma unroll
         for (int b = 0; b < B; ++b) acc[b] = 0ull;  // (+0, +0)
-        for (int w0 = 0; w0 < nw; w0 += kWChunk) {
-            const int nc = min(kWChunk, nw - w0);
-            uint32_t words[kWChunk];
+        // One block pair (2k, 2k + 1): nibbles m, m + 1 of `word`, scales in `sp`.
+        auto pair = [&](uint32_t word, int m, uint32_t sp, int k) {
+            // nibble - 8 for both blocks: 2^23 + nibble as a float, minus 2^23 + 8.
+            const float fa = __uint_as_float(0x4B000000u | ((word >> (4 * m)) & 15u));
+            const float fb = __uint_as_float(0x4B000000u | ((word >> (4 * m + 4)) & 15u));
+            const uint64_t q = add2(pk2(fa, fb), kMagic8);
+            const float s0 = __half2float(__ushort_as_half((unsigned short)(sp & 0xFFFFu)));
+            const float s1 = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
+            const uint64_t qs = mul2(q, pk2(s0, s1));  // exact
+            const float2* xk = xs2 + k * 32 + lane;
 #pragma unroll
-            for (int c = 0; c < kWChunk; ++c) words[c] = c < nc ? __ldg(nr + (w0 + c) * 32) : 0u;
-            const uint4 s4 = lane < nc ? __ldg(sr + w0 + lane) : make_uint4(0u, 0u, 0u, 0u);
+            for (int b = 0; b < B; ++b) {
+                const float2 xv = xk[b * npairs * 32];
+                // Scalar products (.rn: never contracted into a fused multiply-add with the
+                // sum), then one packed add.
+                const float t0 = __fmul_rn(lo2(qs), xv.x);
+                const float t1 = __fmul_rn(hi2(qs), xv.y);
+                acc[b] = add2(acc[b], pk2(t0, t1));
+            }
+        };
+        if constexpr (NW > 0) {
+            // Words per lane known at compile time: all loads first, then fully unrolled
+            // pairs; only the last word can hold padding blocks.
+            uint32_t words[NW];
 #pragma unroll
-            for (int c = 0; c < kWChunk; ++c) {
-                if (c >= nc) break;
-                const int w = w0 + c;
+            for (int c = 0; c < NW; ++c) words[c] = __ldg(nr + c * 32);
+            const uint4 s4 = lane < NW ? __ldg(sr + lane) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int c = 0; c < NW; ++c) {
                 const uint32_t sw[4] = {__shfl_sync(FULLMASK, s4.x, c), __shfl_sync(FULLMASK, s4.y, c),
                                         __shfl_sync(FULLMASK, s4.z, c), __shfl_sync(FULLMASK, s4.w, c)};
-                const uint32_t word = words[c];
 #pragma unroll
                 for (int m = 0; m < 8; m += 2) {
-                    const int k = 4 * w + (m >> 1);  // block pair (2k, 2k + 1)
-                    if (k < npairs) {
-                        // nibble - 8 for both blocks: 2^23 + nibble as a float, minus 2^23 + 8.
-                        const float fa = __uint_as_float(0x4B000000u | ((word >> (4 * m)) & 15u));
-                        const float fb = __uint_as_float(0x4B000000u | ((word >> (4 * m + 4)) & 15u));
-                        const uint64_t q = add2(pk2(fa, fb), kMagic8);
-                        const uint32_t sp = sw[m >> 1];  // scales of blocks 8w + m and 8w + m + 1
-                        const float s0 = __half2float(__ushort_as_half((unsigned short)(sp & 0xFFFFu)));
-                        const float s1 = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
-                        const uint64_t qs = mul2(q, pk2(s0, s1));  // exact
-                        const float2* xk = xs2 + k * 32 + lane;
+                    const int k = 4 * c + (m >> 1);
+                    if (c < NW - 1 || k < npairs) pair(words[c], m, sw[m >> 1], k);
+                }
+            }
+        } else {
+            for (int w0 = 0; w0 < nw; w0 += kWChunk) {
+                const int nc = min(kWChunk, nw - w0);
+                uint32_t words[kWChunk];
 #pragma unroll
-                        for (int b = 0; b < B; ++b) {
-                            const float2 xv = xk[b * npairs * 32];
-                            // Scalar products (.rn: never contracted into a fused multiply-add
-                            // with the sum), then one packed add.
-                            const float t0 = __fmul_rn(lo2(qs), xv.x);
-                            const float t1 = __fmul_rn(hi2(qs), xv.y);
-                            acc[b] = add2(acc[b], pk2(t0, t1));
-                        }
+                for (int c = 0; c < kWChunk; ++c) words[c] = c < nc ? __ldg(nr + (w0 + c) * 32) : 0u;
+                const uint4 s4 = lane < nc ? __ldg(sr + w0 + lane) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+                for (int c = 0; c < kWChunk; ++c) {
+                    if (c >= nc) break;
+                    const int w = w0 + c;
+                    const uint32_t sw[4] = {__shfl_sync(FULLMASK, s4.x, c), __shfl_sync(FULLMASK, s4.y, c),
+                                            __shfl_sync(FULLMASK, s4.z, c), __shfl_sync(FULLMASK, s4.w, c)};
+#pragma unroll
+                    for (int m = 0; m < 8; m += 2) {
+                        const int k = 4 * w + (m >> 1);
+                        if (k < npairs) pair(words[c], m, sw[m >> 1], k);
                     }
                 }
             }
@@ -162,21 +183,34 @@ __global__ void __launch_bounds__(kUThreads) q4_0_matvec_kernel(const uint32_t* 
     }
 }
 
-template <int B>
-cudaError_t launch_matvec(const uint32_t* nib, const uint16_t* scales, const float* x, int in_dim, int out_dim,
-                          float* out, cudaStream_t stream) {
+template <int B, int NW>
+cudaError_t launch_matvec_nw(const uint32_t* nib, const uint16_t* scales, const float* x, int in_dim, int out_dim,
+                             float* out, cudaStream_t stream) {
     const size_t smem = (size_t)B * (((in_dim >> 5) + 1) / 2) * 32 * sizeof(float2);
-    cudaError_t e = cudaFuncSetAttribute(q4_0_matvec_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    void (*kern)(const uint32_t*, const uint16_t*, const float*, int, int, float*) = q4_0_matvec_kernel<B, NW>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     int dev = 0, sms = 148, per_sm = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, q4_0_matvec_kernel<B>, kUThreads, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kUThreads, smem);
     if (e != cudaSuccess) return e;
     const int64_t want = ((int64_t)out_dim + kUWarps - 1) / kUWarps;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * std::max(per_sm, 1)));
-    q4_0_matvec_kernel<B><<<grid, kUThreads, smem, stream>>>(nib, scales, x, in_dim, out_dim, out);
+    kern<<<grid, kUThreads, smem, stream>>>(nib, scales, x, in_dim, out_dim, out);
     return cudaGetLastError();
+}
+
+// Words per lane specialised for the hidden sizes 1152, 2560 and 3840 (5, 10, 15).
+template <int B>
+cudaError_t launch_matvec(const uint32_t* nib, const uint16_t* scales, const float* x, int in_dim, int out_dim,
+                          float* out, cudaStream_t stream) {
+    switch (q4_0_words_per_lane(in_dim)) {
+        case 5: return launch_matvec_nw<B, 5>(nib, scales, x, in_dim, out_dim, out, stream);
+        case 10: return launch_matvec_nw<B, 10>(nib, scales, x, in_dim, out_dim, out, stream);
+        case 15: return launch_matvec_nw<B, 15>(nib, scales, x, in_dim, out_dim, out, stream);
+        default: return launch_matvec_nw<B, 0>(nib, scales, x, in_dim, out_dim, out, stream);
+    }
 }
 
 }  // namespace
@@ -209,23 +243,22 @@ cudaError_t q4_0_matvec(const uint32_t* nib, const uint16_t* scales, int in_dim,
     // Batches above kMaxUnembedBatch are cut into chunks (the weights are read per chunk).
     const int per = unembed_chunk_rows(in_dim);
     if (per < 1) return cudaErrorInvalidValue;
-    for (int b0 = 0; b0 < batch; b0 += per) {
-        const int nbch = std::min(per, batch - b0);
+    for (int b0 = 0; b0 < batch;) {
+        // Chunks of 8, 4, 2 or 1 rows (at most `per`).
+        const int left = std::min(per, batch - b0);
+        const int nbch = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
         const float* xb = x + (int64_t)b0 * in_dim;
         float* ob = out + (int64_t)b0 * out_dim;
         cudaError_t e;
         switch (nbch) {
             case 1: e = launch_matvec<1>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
             case 2: e = launch_matvec<2>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
-            case 3: e = launch_matvec<3>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
             case 4: e = launch_matvec<4>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
-            case 5: e = launch_matvec<5>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
-            case 6: e = launch_matvec<6>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
-            case 7: e = launch_matvec<7>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
             default: e = launch_matvec<8>(nib, scales, xb, in_dim, out_dim, ob, stream); break;
         }
         if (e != cudaSuccess) return e;
         if (launches) ++*launches;
+        b0 += nbch;
     }
     return cudaSuccess;
 }
