@@ -2943,9 +2943,13 @@ __global__ void __launch_bounds__(NT, 1) row_cluster_kernel(KParams p) {
     VDXS_T1(23, t_c4);
 }
 
-// Per-row finish (one CTA per row), launched as a programmatic dependent of topk_hist_kernel.
-template <typename T>
-__global__ void __launch_bounds__(NT) finish_kernel(KParams p) {
+// Per-row finish (one CTA per row), launched as a programmatic dependent of the stream
+// kernel. MINB = 4 caps it at 64 registers, so that four finish CTAs fit an SM and a
+// batch of 512 rows finishes in one wave on 148 SMs (c4: 139 -> 133 us per step); it
+// spills in the faithful emulation, so batches that fit three CTAs per SM keep the
+// uncapped build (MINB = 1).
+template <typename T, int MINB>
+__global__ void __launch_bounds__(NT, MINB) finish_kernel(KParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint32_t* hist = (uint32_t*)smem_raw;
     uint32_t* sh = hist + kHistWords;
@@ -3727,7 +3731,11 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         void (*k1)(KParams) = vec ? topk_stream_kernel<T, true> : topk_stream_kernel<T, false>;
         if ((e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan.smem)) != cudaSuccess)
             return e;
-        if ((e = cudaFuncSetAttribute(finish_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        int sms = 148, dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        void (*kf)(KParams) = a.B > 3 * sms ? finish_kernel<T, 4> : finish_kernel<T, 1>;
+        if ((e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)plan.smem2)) != cudaSuccess)
             return e;
         if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
@@ -3764,7 +3772,7 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
             at[0].val.programmaticStreamSerializationAllowed = 1;
             lc.attrs = at;
             lc.numAttrs = 1;
-            if ((e = cudaLaunchKernelEx(&lc, finish_kernel<T>, p)) != cudaSuccess) return e;
+            if ((e = cudaLaunchKernelEx(&lc, kf, p)) != cudaSuccess) return e;
         }
         count(a, 2);
         return cudaSuccess;
