@@ -788,7 +788,54 @@ __device__ bool stage2_canonical(const KParams& p, int b, const uint32_t* sk, co
     // Each thread owns EPT consecutive walk positions (P2 <= 1024 = EPT * NT).
     constexpr int EPT = 1024 / NT;
     const int i0 = EPT * tid;
-    if (exact) {
+    if (exact && P2 <= 64) {
+        // Up to 64 survivors: warp 0 alone, two walk positions per lane, a shuffled scan
+        // and ballots (the sums are exact, so their order does not matter).
+        if (tid < 32) {
+            const int lane = tid, w0 = 2 * tid;
+            const double a0 = w0 < nsel ? (double)q[w0] : 0.0;
+            const double a1 = w0 + 1 < nsel ? (double)q[w0 + 1] : 0.0;
+            double incl = a0 + a1;
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const double y = __shfl_up_sync(FULL, incl, d);
+                if (lane >= d) incl += y;
+            }
+            const double tot = __shfl_sync(FULL, incl, 31);
+            double pre0 = __shfl_up_sync(FULL, incl, 1);
+            if (lane == 0) pre0 = 0.0;
+            const double pre1 = pre0 + a0;
+            // Prefix sum before walk position i (uniform i): tot when i is past the lanes.
+            auto pre_at = [&](int i) -> double {
+                const double v = __shfl_sync(FULL, (i & 1) ? pre1 : pre0, (i >> 1) & 31);
+                return i >= 64 ? tot : v;
+            };
+            auto first = [&](bool f0, bool f1) -> int {
+                const unsigned b0 = __ballot_sync(FULL, f0), b1 = __ballot_sync(FULL, f1);
+                const int p0 = b0 ? 2 * (__ffs(b0) - 1) : INT_MAX;
+                const int p1 = b1 ? 2 * (__ffs(b1) - 1) + 1 : INT_MAX;
+                return min(p0, p1);
+            };
+            double lsum = tot;
+            int m = nsel;
+            if (p.top_p < 1.0f) {
+                const double target = (double)p.top_p * tot;
+                const int f = first(w0 < nsel && !(pre0 < target && a0 > 0.0),
+                                    w0 + 1 < nsel && !(pre1 < target && a1 > 0.0));
+                m = min(f, nsel);
+                lsum = pre_at(m);
+            }
+            const double t = (double)u * lsum;
+            const int jj = first(w0 < m && pre0 + a0 > t, w0 + 1 < m && pre1 + a1 > t);
+            const double before = pre_at(jj == INT_MAX ? 0 : jj);
+            if (lane == 0) {
+                s_i[0] = jj == INT_MAX ? -1 : jj;
+                s_d[0] = t;
+                s_d[1] = lsum;
+                s_d[2] = jj == INT_MAX ? 0.0 : before;
+            }
+        }
+    } else if (exact) {
         double a[EPT];
         double part = 0.0;
 #pragma unroll
