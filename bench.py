@@ -479,8 +479,12 @@ def run_ours(args, rank, world, local):
     if world > 1:
         one = torch.ones(1, device=dev)
         align = lambda: dist.all_reduce(one)  # noqa: E731
+    # A sharded step takes the host longer to enqueue (NCCL's non-blocking enqueue and
+    # four launches) than the device needs to run it: the pre-roll must cover the
+    # enqueue of every timed step, or later steps measure the host instead.
+    pre_us = min(200000, (400 if world > 1 else 60) * args.steps + 2000)
     per_step, kern_ms, launches = timed_loop(torch, ctx, lambda j: step(args.warmup + j), args.steps, flush, stream,
-                                             clocks, align=align)
+                                             clocks, pre_us=pre_us, align=align)
     ctx.device_status()
     if world > 1:
         dist.barrier()
