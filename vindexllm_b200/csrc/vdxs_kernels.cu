@@ -1603,18 +1603,41 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
             }
         };
         if (!incomplete) {
-            // The whole CTA walks the list, four loads in flight per thread.
+            // The whole CTA walks the list, eight loads in flight per thread; a warp reserves
+            // the slots of its eight entries at once (one shared atomic per step).
+            constexpr int GU = 8;
             const int c = (int)craw;
             const uint2* src = p.cand + (size_t)b * cc;
-            for (int j0 = 0; j0 < c; j0 += 4 * NT) {
-                uint2 e[4];
+            for (int j0 = 0; j0 < c; j0 += GU * NT) {
+                uint2 e[GU];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < GU; ++u) {
                     const int j = j0 + u * NT + tid;
                     e[u] = j < c ? __ldcg(src + j) : make_uint2(0u, 0u);
                 }
+                unsigned m[GU];
+                uint32_t tot = 0u;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) put(j0 + u * NT + tid < c && e[u].x >= tb, e[u].x, e[u].y);
+                for (int u = 0; u < GU; ++u) {
+                    m[u] = __ballot_sync(FULL, j0 + u * NT + tid < c && e[u].x >= tb);
+                    tot += (uint32_t)__popc(m[u]);
+                }
+                if (tot == 0u) continue;
+                uint32_t base = 0u;
+                if (lane == 0) base = atomicAdd(&sh[40], tot);
+                base = __shfl_sync(FULL, base, 0);
+#pragma unroll
+                for (int u = 0; u < GU; ++u) {
+                    if ((m[u] >> lane) & 1u) {
+                        const uint32_t pos = base + __popc(m[u] & lanemask_lt());
+                        if (pos < (uint32_t)gcap) {
+                            ckey[pos] = e[u].x;
+                            cidx[pos] = e[u].y;
+                        }
+                        lm = max(lm, e[u].x);
+                    }
+                    base += (uint32_t)__popc(m[u]);
+                }
             }
         }
         for (int j0 = 0; j0 < npen; j0 += NT) {
