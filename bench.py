@@ -5,7 +5,7 @@
 
 One step = one sampling pass of the hot path over one batch of seeded synthetic logits
 (the whole [B, V] batch, or each rank's vocab shard for N > 1). The default workload is
-BASELINE config c4 (B=512, V=262144 fp32, T=1, top-k 64, top-p 0.95): the only
+Benchmark configuration c4 (B=512, V=262144 fp32, T=1, top-k 64, top-p 0.95): the only
 configuration defined for 1..8 GPUs, so every N runs the same total work (strong
 scaling). At N=1 it is sampled unsharded; at N>1 each rank holds a contiguous vocab
 shard, selects its local top-k, and the candidates are all-gathered with NCCL.
@@ -270,7 +270,7 @@ def subset_rows(B, n=64):
 
 
 # Configurations timed in the same run as the headline line (N=1 only), each with its own
-# oracle parity check: every BASELINE target in one driver record.
+# oracle parity check: every target of the benchmark configurations in one JSON line.
 CONFIG_BLOCK = [
     ("c0", "faithful", None),
     ("c1", "faithful", None),
@@ -672,7 +672,7 @@ def run_ours(args, rank, world, local):
         line = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": spec["dtype"],
-                "data": "synthetic (seeded; distribution of the named BASELINE config)",
+                "data": "synthetic (seeded; distribution of the named benchmark configuration)",
                 "config": workload_config(name, world, spec, args.tie_mode, l2_desc),
                 "latency_us": dict(lat_summary(step_max.tolist()), mean=round(ms_per_step * 1e3, 2)),
                 "latency_note": "per step: the slowest rank's CUDA-event time; mean = max over ranks of the "
@@ -759,7 +759,7 @@ def run_reference(args, rank, world):
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": spec["dtype"],
-            "data": "synthetic (seeded; distribution of the named BASELINE config)",
+            "data": "synthetic (seeded; distribution of the named benchmark configuration)",
             "config": workload_config(name, world, spec, "faithful",
                                       l2_policy(B * (V // world) * (2 if spec["dtype"] == "bf16" else 4))[1]),
             "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": nt, "kind": "port",

@@ -1,4 +1,4 @@
-// vdxs_unembed.cu - the unembedding matvec in front of the sampler (SURVEY row (f)1):
+// vdxs_unembed.cu - the unembedding matvec in front of the sampler:
 // TVdxModel.UnembedToLogits (src/VindexLLM.Model.pas:1258-1271) multiplies the normed
 // hidden vector by the tied Q4_0 embedding with shaders/matvec_q4_0.comp (:45-88), and
 // the logits go to TVdxSampler.Process.
