@@ -114,3 +114,28 @@ def test_large_topk_host_entry(gpu_ctx, oracle_mod):
     host = gpu_ctx.sample_host(cfg, x, u)
     o = oracle_run(oracle_mod, cfg, x, u, mode=abi.TIES_FAITHFUL)
     assert (host == o[0]).all()
+
+
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("dtype", ["f32", "bf16"])
+def test_large_topk_stage1_lists(gpu_ctx, oracle_mod, mode, dtype):
+    """32 K <= V: the stream kernel's row lists feed the large top-k kernel. Batches of
+    24 rows (several warps per row, lists that hold every element taken while the bounds
+    rose) with smooth rows, rows of many ties at the bound (long lists), and a row whose
+    list overflows (every element ties: the kernel re-selects from the whole row)."""
+    import torch
+    V, B = 262144, 24
+    rng = np.random.default_rng(77 + (1 if dtype == "bf16" else 0))
+    x = (rng.normal(size=(B, V)) * 2.0).astype(np.float32)
+    x[B // 3: 2 * B // 3] = np.round(x[B // 3: 2 * B // 3] * 2) / 2
+    x[-1] = 0.5
+    xt = _t(x)
+    if dtype == "bf16":
+        xt = xt.to(torch.bfloat16)
+    hist = rng.integers(0, V, size=(B, 64)).astype(np.int32)
+    cnt = rng.integers(0, 65, size=B).astype(np.int32)
+    u = rng.random(B).astype(np.float32)
+    for cfg in [default_config(temperature=1.0, top_k=2000, top_p=0.9, repeat_penalty=1.2),
+                default_config(temperature=0.8, top_k=4096, top_p=1.0, min_p=0.01),
+                default_config(temperature=1.3, top_k=8192, top_p=0.95)]:
+        _check(gpu_ctx, oracle_mod, cfg, xt, u, hist, cnt, mode, label=f"lists {dtype} {cfg.as_dict()}")

@@ -135,18 +135,20 @@ def test_noalloc_rejects_oversized_requests():
 
 def test_noalloc_large_top_k():
     """top_k above 1024 (the large top-k kernel) takes its per-CTA workspace from the same
-    fixed array: one row of c4 with K = 65536 (1.5 MiB) gives the context entry's token."""
+    fixed array: rows of c4 with K = 65536 (1.5 MiB per CTA, whole-row select) and K = 2000
+    (stage-1 row lists first) give the context entry's tokens."""
     import torch
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from vindexllm_b200.sampler import SamplerContext
     lib = _lib.load()
-    cfg = synth.sampler_config("c4", top_k=65536)
     ctx = SamplerContext(0)
-    for mode in (abi.TIES_FAITHFUL, abi.TIES_CANONICAL):
-        ctx.set_tie_mode(mode)
-        x, h, c, u = _inputs("c4", 0, 2)
-        want = ctx.sample(cfg, x, u, h, c).cpu().numpy()
-        got = _noalloc(lib, cfg, mode, x, u, h, c)
-        assert (got == want).all(), f"mode {mode}"
+    for top_k in (65536, 2000):
+        cfg = synth.sampler_config("c4", top_k=top_k)
+        for mode in (abi.TIES_FAITHFUL, abi.TIES_CANONICAL):
+            ctx.set_tie_mode(mode)
+            x, h, c, u = _inputs("c4", 0, 2)
+            want = ctx.sample(cfg, x, u, h, c).cpu().numpy()
+            got = _noalloc(lib, cfg, mode, x, u, h, c)
+            assert (got == want).all(), f"top_k {top_k} mode {mode}"
     ctx.close()

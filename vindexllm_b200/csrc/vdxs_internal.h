@@ -111,6 +111,8 @@ struct LaunchPlan {
     bool stream = false;  // top-k path: persistent stream kernel + finish kernel
     bool cluster = false; // top-k path, small batches: one thread-block cluster per row
     bool large = false;   // top-k path, top_k above kMaxTopK: one CTA per row, global workspace
+    int large_grid = 0;   // large top-k kernel grid (CTAs)
+    size_t large_smem = 0;  // large top-k kernel shared memory
     int cluster_ctas = 8; // CTAs per cluster
     int grid = 0;         // stream kernel grid (CTAs)
     int cand_cap = 0;     // top-k path: candidates each stage-1 list may hold (stream path: per row)

@@ -132,6 +132,7 @@ struct KParams {
     uint2* emit_out;  // [B][K+1]
     // top_k above the stream path's maximum: per-CTA global workspace (lk_cta_words(K) words each)
     uint64_t* lk_buf;
+    int lk_list;  // the large top-k kernel selects from stage-1 lists (the stream kernel ran first)
 };
 
 // ---------------------------------------------------------------------------------
@@ -519,7 +520,7 @@ struct SmemPairSrc {  // stage 2: (key, index) pairs in shared memory, tie-break
     __device__ __forceinline__ uint32_t tb(int i) const { return t[i]; }
 };
 
-template <class Src>
+template <int UN = 4, class Src>
 __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, int tb_bits,
                                   uint32_t* hist, uint32_t* sh) {
     const int tid = threadIdx.x;
@@ -527,14 +528,14 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
     r.tie_cut = 0;
     for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
     __syncthreads();
-    // Every pass loads four elements per thread before it counts them, so that reads
-    // from global memory (a row source) overlap.
-    for (int i0 = tid; i0 < n; i0 += 4 * NT) {
-        uint32_t k[4];
+    // Every pass loads UN elements per thread before it counts them, so that reads from
+    // global memory (a row source) overlap.
+    for (int i0 = tid; i0 < n; i0 += UN * NT) {
+        uint32_t k[UN];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+        for (int u = 0; u < UN; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < UN; ++u)
             if (k[u]) atomicAdd(&hist[logbin(kmax - k[u])], 1u);
     }
     __syncthreads();
@@ -561,12 +562,12 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
         const uint32_t width = 1u << bits;
         for (int i = tid; i < 256; i += NT) hist[i] = 0u;
         __syncthreads();
-        for (int i0 = tid; i0 < n; i0 += 4 * NT) {
-            uint32_t k[4];
+        for (int i0 = tid; i0 < n; i0 += UN * NT) {
+            uint32_t k[UN];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+            for (int u = 0; u < UN; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < UN; ++u) {
                 const uint32_t dd = (kmax - k[u]) - dlo;
                 if (k[u] && dd < width) atomicAdd(&hist[dd >> shift], 1u);
             }
@@ -597,12 +598,12 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
         const uint32_t hi_mask = tbits >= 32 ? 0u : (0xFFFFFFFFu << tbits);
         for (int i = tid; i < 256; i += NT) hist[i] = 0u;
         __syncthreads();
-        for (int i0 = tid; i0 < n; i0 += 4 * NT) {
-            bool eq[4];
+        for (int i0 = tid; i0 < n; i0 += UN * NT) {
+            bool eq[UN];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) eq[u] = i0 + u * NT < n && src.key(i0 + u * NT) == r.kth_key;
+            for (int u = 0; u < UN; ++u) eq[u] = i0 + u * NT < n && src.key(i0 + u * NT) == r.kth_key;
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
+            for (int u = 0; u < UN; ++u) {
                 if (eq[u]) {
                     const uint32_t t = src.tb(i0 + u * NT);
                     if (((t ^ tlo) & hi_mask) == 0u) atomicAdd(&hist[(t >> shift) & ((1u << w) - 1u)], 1u);
@@ -1371,21 +1372,21 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
 
 // Writes every selected element of src to (ok, oi), returns the count (uniform).
-template <class Src, class IdxF>
+template <int UN = 4, class Src, class IdxF>
 __device__ int block_emit(const Src& src, int n, const SelectOut& s, uint32_t* ok, uint32_t* oi, int cap,
                           uint32_t* counter, IdxF idx_of) {
     const int tid = threadIdx.x;
     if (tid == 0) *counter = 0u;
     __syncthreads();
-    for (int i0 = tid; i0 - tid < n; i0 += 4 * NT) {
-        uint32_t k[4];
-        bool sel[4];
+    for (int i0 = tid; i0 - tid < n; i0 += UN * NT) {
+        uint32_t k[UN];
+        bool sel[UN];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+        for (int u = 0; u < UN; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
 #pragma unroll
-        for (int u = 0; u < 4; ++u) sel[u] = i0 + u * NT < n && selected(k[u], src.tb(i0 + u * NT), s);
+        for (int u = 0; u < UN; ++u) sel[u] = i0 + u * NT < n && selected(k[u], src.tb(i0 + u * NT), s);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < UN; ++u) {
             const unsigned m = __ballot_sync(FULL, sel[u]);
             if (m) {
                 uint32_t base = 0u;
@@ -1660,8 +1661,6 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     const uint32_t gmax = block_max_u32(lm, sh + 32);
     finish_select<T>(p, b, ckey, cidx, n2, gmax, 0, [&](int) -> uint32_t { return 0u; }, region, hist, sh);
 }
-
-#include "vdxs_large_topk.cuh"
 
 // ---------------------------------------------------------------------------------
 // Warp-level select (one warp, warp-private histogram; __syncwarp only). Same result
@@ -2125,6 +2124,8 @@ constexpr int kS1RaiseEvery = 4;                      // counted candidates betw
 constexpr int kRowHistWords = kTBins + kTGroups;      // per-row histogram in global memory
 constexpr int kS1WarpBytes = kS1Ring * kS1SlotBytes + 64 + 8 * kS1WCap + 4 * 256;
 static_assert(kS1WarpBytes % 16 == 0, "16-byte aligned warp areas");
+
+#include "vdxs_large_topk.cuh"
 
 __host__ __device__ constexpr size_t s1_smem_bytes() { return (size_t)kS1Warps * kS1WarpBytes; }
 template <typename T>
@@ -3407,7 +3408,15 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         // candidates taken while the bounds were still rising (about K times the log of
         // the row's units for random orders, more for rows with many ties at the bound).
         // A longer list is incomplete and its row takes the finish kernel's exact fallback.
-        const int cc = (int)std::min<int64_t>(std::max<int64_t>(32LL * K, 4096), (int64_t)ng * SE);
+        // Above top_k 256 no slot gives a local bound, so every warp's first slots of a row go
+        // to the list before the row's histogram holds K counts: the list also has room
+        // for four slots per warp working on the row.
+        int dev0 = 0, sms0 = 148;
+        cudaGetDevice(&dev0);
+        cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, dev0);
+        const int64_t wpr = ((int64_t)sms0 * kS1Warps + a.B - 1) / a.B;
+        const int64_t first_wave = K > 256 ? 4 * wpr * SE : 0;
+        const int cc = (int)std::min<int64_t>(std::max<int64_t>({32LL * K, 4096, first_wave}), (int64_t)ng * SE);
         const int gather = std::max(K <= 128 ? 4096 : 8192, K + pen_stride);
         size_t s2 = std::max(stage2_bytes(K, gather + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);
         s2 += kHeadBytes;
@@ -3436,7 +3445,8 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
     }
     {
         // top_k above the stream path's maximum: one CTA per row of a persistent grid, each
-        // with 24 bytes of global workspace per slot (at most 1 GiB in all).
+        // with 24 bytes of global workspace per slot (at most 1 GiB in all). When 32 K <= V
+        // the stream kernel runs first and the large kernel selects from its row lists.
         int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -3449,14 +3459,32 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         const int64_t by_mem = std::max<int64_t>(1, (1LL << 30) / per_cta);
         plan->large = true;
         plan->stream = false;
-        plan->grid = (int)std::min<int64_t>({(int64_t)a.B, 2LL * sms, by_mem});
+        plan->large_grid = (int)std::min<int64_t>({(int64_t)a.B, 2LL * sms, by_mem});
+        plan->large_smem = align16(sm);
         plan->chunk = 0;
         plan->nchunks = 1;
         plan->nspans = 1;
         plan->span = 1;
         plan->items = 0;
         plan->cand_cap = 0;
-        plan->smem = align16(sm);
+        if (32LL * K <= V) {
+            const int SE = esz == 4 ? s1_slot_elems<float>() : s1_slot_elems<uint16_t>();
+            const int ng = (int)((V + SE - 1) / SE);
+            const int U = std::min(ng, 16);
+            const long long units = (long long)a.B * ((ng + U - 1) / U);
+            const size_t s1 = s1_smem_bytes();
+            if (units * U < (1LL << 31) && (int64_t)s1 <= smem_optin) {
+                plan->stream = true;
+                const int64_t wpr = ((int64_t)sms * kS1Warps + a.B - 1) / a.B;
+                plan->cand_cap = (int)std::min<int64_t>(std::max<int64_t>(32LL * K, 4 * wpr * SE), (int64_t)ng * SE);
+                plan->items = a.B;
+                const long long slots = (long long)a.B * ng;
+                plan->grid = (int)std::max<long long>(1, std::min<long long>((long long)sms, slots / (4LL * kS1Warps)));
+                plan->slots = ng;
+                plan->unit_slots = U;
+                plan->smem = s1;
+            }
+        }
         return cudaSuccess;
     }
 }
@@ -3543,7 +3571,7 @@ cudaError_t ensure_workspace(Workspace& ws, const SampleArgs& a, const LaunchPla
         }
     }
     if (plan.large &&
-        (e = grow(&ws.lk_buf, &ws.lk_cap, (size_t)plan.grid * (size_t)lk_cta_words(a.K), false, stream)) !=
+        (e = grow(&ws.lk_buf, &ws.lk_cap, (size_t)plan.large_grid * (size_t)lk_cta_words(a.K), false, stream)) !=
             cudaSuccess)
         return e;
     if (a.local_emit) {
@@ -3629,7 +3657,7 @@ size_t carve_workspace(Workspace& ws, unsigned char* base, size_t cap, const Sam
         w.pen_rows_cap = B;
     }
     if (plan.large) {
-        w.lk_cap = (size_t)plan.grid * (size_t)lk_cta_words(a.K);
+        w.lk_cap = (size_t)plan.large_grid * (size_t)lk_cta_words(a.K);
         w.lk_buf = (uint64_t*)take(w.lk_cap * sizeof(uint64_t));
     }
     if (off <= cap) ws = w;
@@ -3731,6 +3759,7 @@ static KParams make_params(const SampleArgs& a, const LaunchPlan& plan, Workspac
     p.local_emit = a.local_emit ? 1 : 0;
     p.emit_out = ws.shard_send;
     p.lk_buf = ws.lk_buf;
+    p.lk_list = plan.large && plan.stream ? 1 : 0;
     return p;
 }
 
@@ -3828,7 +3857,15 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
             if ((e = cudaGetLastError()) != cudaSuccess) return e;
         }
         if ((e = mark(a, a.ev_end)) != cudaSuccess) return e;
-        {
+        if (plan.large) {
+            // top_k above the stream path's maximum: the large top-k kernel selects from the
+            // row lists stage 1 just wrote.
+            if ((e = cudaFuncSetAttribute(topk_large_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)plan.large_smem)) != cudaSuccess)
+                return e;
+            topk_large_kernel<T><<<plan.large_grid, NT, plan.large_smem, a.stream>>>(p);
+            if ((e = cudaGetLastError()) != cudaSuccess) return e;
+        } else {
             // Programmatic dependent launch: finish CTAs are scheduled as stage-1 CTAs
             // retire, hiding the launch gap; they wait for the whole grid in the kernel.
             // (A recorded event between the two launches makes it an ordinary launch.)
@@ -3847,12 +3884,12 @@ static cudaError_t launch_typed(const SampleArgs& a, const LaunchPlan& plan, Wor
         count(a, 2);
         return cudaSuccess;
     }
-    if (plan.large) {
+    if (plan.large && !plan.stream) {
         if ((e = cudaFuncSetAttribute(topk_large_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)plan.smem)) != cudaSuccess)
+                                      (int)plan.large_smem)) != cudaSuccess)
             return e;
         if ((e = mark(a, a.ev_begin)) != cudaSuccess) return e;
-        topk_large_kernel<T><<<plan.grid, NT, plan.smem, a.stream>>>(p);
+        topk_large_kernel<T><<<plan.large_grid, NT, plan.large_smem, a.stream>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
         count(a);
         return mark(a, a.ev_end);

@@ -64,6 +64,32 @@ struct PenRowSrc {
     __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
 };
 
+// A row's stage-1 list (every element at or above the row's bound, plus candidates taken
+// while the bounds were rising) followed by the row's penalised entries: entries below
+// the bound read as absent, and the tie-break and emitted index is the element's index.
+struct ListSrc {
+    const uint2* cand;
+    int n;
+    uint32_t bound;
+    const int32_t* pid;
+    const float* pvl;
+    int64_t offset;
+    __device__ __forceinline__ uint2 entry(int i) const {
+        if (i < n) return __ldcg(cand + i);
+        const float v = pvl[i - n];
+        return make_uint2(v == v ? f2key(v) : 0u, (uint32_t)(pid[i - n] + offset));
+    }
+    __device__ __forceinline__ uint32_t key(int i) const {
+        const uint32_t k = entry(i).x;
+        return k >= bound ? k : 0u;
+    }
+    __device__ __forceinline__ uint32_t tb(int i) const { return entry(i).y; }
+};
+struct ListIdx {
+    const ListSrc* src;
+    __device__ __forceinline__ uint32_t operator()(int i) const { return src->tb(i); }
+};
+
 // Stable LSD radix sort of n 64-bit keys into descending order, by the whole CTA.
 // a and b are global buffers of n keys; the result is in the returned one. dh: 8 x 256
 // digit counts, base: 256 bucket offsets, tab: kLkTab counts, sh: block scratch.
@@ -392,17 +418,34 @@ __global__ void __launch_bounds__(NT) topk_large_kernel(KParams p) {
                                p.pen_bits && npen > 0 ? p.pen_bits + (int64_t)b * p.pen_words : nullptr,
                                p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr,
                                p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr, npen};
-        // 1. Row maximum and the exact top K in (key desc, index asc) order.
-        uint32_t km = 0u;
-        for (int i0 = tid; i0 < V; i0 += 4 * NT) {
-            uint32_t k[4];
+        // 1. Row maximum and the exact top K in (key desc, index asc) order, from the row's
+        //    stage-1 list when stage 1 ran and the list is complete, else from the row.
+        auto top_k = [&](const auto& sel, int n, auto idx_of, int tbits, uint32_t* kmax_out) -> SelectOut {
+            uint32_t km = 0u;
+            for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+                uint32_t k[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < V ? src.key(i0 + u * NT) : 0u;
-            km = max(max(km, max(k[0], k[1])), max(k[2], k[3]));
+                for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? sel.key(i0 + u * NT) : 0u;
+                km = max(max(km, max(k[0], k[1])), max(k[2], k[3]));
+            }
+            *kmax_out = block_max_u32(km, sh + 32);
+            const SelectOut so = block_select(sel, n, K, *kmax_out, tbits, hist, sh);
+            sh[60] = (uint32_t)block_emit(sel, n, so, ck, ci, K, &sh[8], idx_of);
+            __syncthreads();
+            return so;
+        };
+        uint32_t kmax;
+        SelectOut s;
+        const uint32_t lcount = p.lk_list ? __ldcg(&p.row_cnt[b]) : 0u;
+        if (p.lk_list && lcount <= (uint32_t)p.cand_cap) {
+            const ListSrc ls{p.cand + (int64_t)b * p.cand_cap, (int)lcount,
+                             __ldcg(&p.row_tau[(int64_t)b * kTauStride]), src.pid, src.pvl, p.vocab_offset};
+            s = top_k(ls, (int)lcount + npen, ListIdx{&ls}, bits_for((uint32_t)(p.vocab_offset + V - 1)), &kmax);
+        } else {
+            s = top_k(src, V, OffsetIdx{(uint32_t)p.vocab_offset}, tbb, &kmax);
         }
-        const uint32_t kmax = block_max_u32(km, sh + 32);
-        const SelectOut s = block_select(src, V, K, kmax, tbb, hist, sh);
-        const int nsel = block_emit(src, V, s, ck, ci, K, &sh[8], OffsetIdx{(uint32_t)p.vocab_offset});
+        const int nsel = (int)sh[60];
+        __syncthreads();
         uint32_t kb = 0xFFFFFFFFu;
         for (int i = tid; i < nsel; i += NT) kb = min(kb, ck[i]);
         kb = block_min_u32(kb, sh + 32);
@@ -511,9 +554,18 @@ __global__ void __launch_bounds__(NT) topk_large_kernel(KParams p) {
                                sh + 32, sh_i);
         }
         __syncthreads();
-        // The row's penalised-id bitmap words are left at zero for the next call.
+        // The row's penalised-id bitmap words are left at zero for the next call, and after
+        // a stage-1 pass its bound, list count and key histogram as well.
         if (src.bits)
             for (int jx = tid; jx < npen; jx += NT) p.pen_bits[(int64_t)b * p.pen_words + (src.pid[jx] >> 5)] = 0u;
+        if (p.lk_list) {
+            if (tid == 0) {
+                p.row_tau[(int64_t)b * kTauStride] = 0u;
+                p.row_cnt[b] = 0u;
+            }
+            uint4* rh4 = reinterpret_cast<uint4*>(p.rhist + (int64_t)b * kRowHistWords);
+            for (int i = tid; i < kRowHistWords / 4; i += NT) rh4[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
         __syncthreads();
     }
 }
