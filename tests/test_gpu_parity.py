@@ -205,6 +205,19 @@ def test_benchmark_configs(gpu_ctx, oracle_mod, mode, name, batch, steps):
         compare(g, o, mode, strict_survivors=cfg.top_k <= 64, label=f"{name} mode{mode}")
 
 
+@pytest.mark.parametrize("mode", MODES)
+@pytest.mark.parametrize("name,batch,top_k", [("c4", 64, 128), ("c4", 64, 1024), ("c4", 32, 300),
+                                              ("c1", 16, 256), ("c2", 48, 700)])
+def test_small_batch_wide_topk(gpu_ctx, oracle_mod, mode, name, batch, top_k):
+    """Batches of 16-64 rows with top_k above 64: many stage-1 warps per row take their
+    first slots whole, so the row lists are long, and rows whose entries at or above the
+    row bound outgrow the finish gather select from the list."""
+    for cfg, x, h, c, u in _config_case(name, batch=batch, cfg_over=dict(top_k=top_k)):
+        g = gpu_run(gpu_ctx, cfg, x, u, h, c, mode, out_k=64)
+        o = oracle_run(oracle_mod, cfg, x, u, h, c, mode, out_k=64)
+        compare(g, o, mode, strict_survivors=False, label=f"{name} B{batch} K{top_k} mode{mode}")
+
+
 @pytest.mark.parametrize("cfg_over", [dict(top_k=1), dict(temperature=0.0)])
 def test_c2_greedy_runs(gpu_ctx, oracle_mod, cfg_over):
     import torch

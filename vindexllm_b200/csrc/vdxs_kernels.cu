@@ -1518,6 +1518,32 @@ struct RowKeySrc {  // a row in global memory (NaN: no element), tie-break = pos
     __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
 };
 
+// A row's stage-1 list (every element at or above the row's bound, plus candidates taken
+// while the bounds were rising) followed by the row's penalised entries: entries below
+// the bound read as absent, and the tie-break and emitted index is the element's index.
+struct ListSrc {
+    const uint2* cand;
+    int n;
+    uint32_t bound;
+    const int32_t* pid;
+    const float* pvl;
+    int64_t offset;
+    __device__ __forceinline__ uint2 entry(int i) const {
+        if (i < n) return __ldcg(cand + i);
+        const float v = pvl[i - n];
+        return make_uint2(v == v ? f2key(v) : 0u, (uint32_t)(pid[i - n] + offset));
+    }
+    __device__ __forceinline__ uint32_t key(int i) const {
+        const uint32_t k = entry(i).x;
+        return k >= bound ? k : 0u;
+    }
+    __device__ __forceinline__ uint32_t tb(int i) const { return entry(i).y; }
+};
+struct ListIdx {
+    const ListSrc* src;
+    __device__ __forceinline__ uint32_t operator()(int i) const { return src->tb(i); }
+};
+
 // Exact fallback of the finish for a row whose stage-1 lists are incomplete or do not
 // fit the gather: the top (K + npen) of the raw row (penalties not applied) contain the
 // top K of its non-penalised elements, so that select, with the penalised ids among it
@@ -1559,6 +1585,37 @@ __device__ __noinline__ void finish_row_exact(const KParams& p, int b, uint32_t*
     gm = block_max_u32(gm, sh + 32);
     const uint32_t cut = so.tie_cut ? so.kth_key : 0u;
     finish_select<T>(p, b, ckey, cidx, m + npen, gm, 1, [&](int) -> uint32_t { return cut; }, region, hist, sh);
+}
+
+// Exact select of the finish for a row whose stage-1 list is complete but whose entries
+// at or above the row bound tb do not fit the gather: the top K of the list's entries at
+// or above tb and the row's penalised entries (the list holds no penalised id) are the
+// top K of the row's candidates, and the select reads the list, not the row. Elements
+// equal to the select's boundary key that it left out are reported as a cut, as in
+// finish_row_exact.
+template <typename T>
+__device__ __noinline__ void finish_list_exact(const KParams& p, int b, uint32_t tb, int count, uint32_t* ckey,
+                                               int gcap, unsigned char* region, uint32_t* hist, uint32_t* sh) {
+    const int tid = threadIdx.x;
+    const int npen = p.pen_cnt ? p.pen_cnt[b] : 0;
+    uint32_t* cidx = ckey + gcap;
+    const ListSrc src{p.cand + (size_t)b * p.cand_cap, count, tb,
+                      p.pen_ids ? p.pen_ids + (int64_t)b * p.pen_stride : nullptr,
+                      p.pen_vals ? p.pen_vals + (int64_t)b * p.pen_stride : nullptr, p.vocab_offset};
+    const int n = count + npen;
+    uint32_t km = 0u;
+    for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+        uint32_t k[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+        km = max(max(km, max(k[0], k[1])), max(k[2], k[3]));
+    }
+    km = block_max_u32(km, sh + 32);
+    const SelectOut so = block_select(src, n, p.K, km, bits_for((uint32_t)(p.vocab_offset + p.V - 1)),
+                                               hist, sh);
+    const int m = block_emit(src, n, so, ckey, cidx, gcap, &sh[8], ListIdx{&src});
+    const uint32_t cut = so.tie_cut ? so.kth_key : 0u;
+    finish_select<T>(p, b, ckey, cidx, m, km, 1, [&](int) -> uint32_t { return cut; }, region, hist, sh);
 }
 
 template <typename T>
@@ -1651,11 +1708,18 @@ __device__ void finish_row(const KParams& p, int b, unsigned char* region, uint3
     }
     VDXS_T1(29, t_gather);
     const int n2 = (int)sh[40];
-    if (incomplete || n2 > gcap) {
+    if (incomplete) {
 #ifdef VDXS_TIMING
         if (tid == 0) atomicAdd(&g_phase_count[30], 1ull);
 #endif
         finish_row_exact<T>(p, b, ckey, gcap, region, hist, sh);
+        return;
+    }
+    if (n2 > gcap) {
+#ifdef VDXS_TIMING
+        if (tid == 0) atomicAdd(&g_phase_count[31], 1ull);
+#endif
+        finish_list_exact<T>(p, b, tb, (int)craw, ckey, gcap, region, hist, sh);
         return;
     }
     const uint32_t gmax = block_max_u32(lm, sh + 32);
@@ -3408,14 +3472,16 @@ cudaError_t plan_topk(const SampleArgs& a, int smem_optin, LaunchPlan* plan, std
         // candidates taken while the bounds were still rising (about K times the log of
         // the row's units for random orders, more for rows with many ties at the bound).
         // A longer list is incomplete and its row takes the finish kernel's exact fallback.
-        // Above top_k 256 no slot gives a local bound, so every warp's first slots of a row go
-        // to the list before the row's histogram holds K counts: the list also has room
-        // for four slots per warp working on the row.
+        // Above top_k 64 a slot's local bound (above 256: none) passes much of a slot, and
+        // every warp's first slots of a row go to the list before the row's histogram holds
+        // K counts (the raise lands two slots after it starts): with few slots per warp
+        // (small batches) those slots are much of the list, which has room for six slots
+        // per warp working on the row.
         int dev0 = 0, sms0 = 148;
         cudaGetDevice(&dev0);
         cudaDeviceGetAttribute(&sms0, cudaDevAttrMultiProcessorCount, dev0);
         const int64_t wpr = ((int64_t)sms0 * kS1Warps + a.B - 1) / a.B;
-        const int64_t first_wave = K > 256 ? 4 * wpr * SE : 0;
+        const int64_t first_wave = K > 64 ? 6 * wpr * SE : 0;
         const int cc = (int)std::min<int64_t>(std::max<int64_t>({32LL * K, 4096, first_wave}), (int64_t)ng * SE);
         const int gather = std::max(K <= 128 ? 4096 : 8192, K + pen_stride);
         size_t s2 = std::max(stage2_bytes(K, gather + pen_stride), faithful ? faithful_bytes(K) : (size_t)0);

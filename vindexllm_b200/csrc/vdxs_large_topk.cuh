@@ -64,32 +64,6 @@ struct PenRowSrc {
     __device__ __forceinline__ uint32_t tb(int i) const { return (uint32_t)i; }
 };
 
-// A row's stage-1 list (every element at or above the row's bound, plus candidates taken
-// while the bounds were rising) followed by the row's penalised entries: entries below
-// the bound read as absent, and the tie-break and emitted index is the element's index.
-struct ListSrc {
-    const uint2* cand;
-    int n;
-    uint32_t bound;
-    const int32_t* pid;
-    const float* pvl;
-    int64_t offset;
-    __device__ __forceinline__ uint2 entry(int i) const {
-        if (i < n) return __ldcg(cand + i);
-        const float v = pvl[i - n];
-        return make_uint2(v == v ? f2key(v) : 0u, (uint32_t)(pid[i - n] + offset));
-    }
-    __device__ __forceinline__ uint32_t key(int i) const {
-        const uint32_t k = entry(i).x;
-        return k >= bound ? k : 0u;
-    }
-    __device__ __forceinline__ uint32_t tb(int i) const { return entry(i).y; }
-};
-struct ListIdx {
-    const ListSrc* src;
-    __device__ __forceinline__ uint32_t operator()(int i) const { return src->tb(i); }
-};
-
 // Stable LSD radix sort of n 64-bit keys into descending order, by the whole CTA.
 // a and b are global buffers of n keys; the result is in the returned one. dh: 8 x 256
 // digit counts, base: 256 bucket offsets, tab: kLkTab counts, sh: block scratch.
