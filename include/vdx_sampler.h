@@ -173,7 +173,10 @@ VDXS_API int32_t vdxs_sample_host(vdxs_context* ctx, const vdxs_config* cfg,
  * workspace is a fixed 32 MiB device array built into the library, which every GPU
  * that loads the library holds until the process exits. Calls whose workspace would
  * exceed it return VDXS_E_UNSUPPORTED (batch 512 at vocab 262144 with top_k 64 fits;
- * batch 1024 with top_k 1024 does not). The call never allocates: no cudaMalloc,
+ * batch 1024 with top_k 1024 does not). Where vdxs_sample would use long candidate
+ * lists (small batches with top_k above 64) that do not fit, this call uses shorter
+ * ones: the same tokens, rows whose lists overflow take a slower exact select. The
+ * call never allocates: no cudaMalloc,
  * cudaFree or allocating library routine. Its first call on a device resolves the
  * array's device address (once per device, with that device current); make that
  * first call before any stream capture. All calls share the one array and it keeps

@@ -152,3 +152,23 @@ def test_noalloc_large_top_k():
             got = _noalloc(lib, cfg, mode, x, u, h, c)
             assert (got == want).all(), f"top_k {top_k} mode {mode}"
     ctx.close()
+
+
+def test_noalloc_small_batch_wide_topk():
+    """Batch 64 with top_k 1024: the context entry sizes the row lists for 37 stage-1 warps
+    per row (about 116 MB); the fixed array takes the shorter lists, whose overflowing rows
+    are selected from the whole row. Both give the same tokens."""
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from vindexllm_b200.sampler import SamplerContext
+    lib = _lib.load()
+    ctx = SamplerContext(0)
+    cfg = synth.sampler_config("c4", top_k=1024)
+    for mode in (abi.TIES_FAITHFUL, abi.TIES_CANONICAL):
+        ctx.set_tie_mode(mode)
+        x, h, c, u = _inputs("c4", 0, 64)
+        want = ctx.sample(cfg, x, u, h, c).cpu().numpy()
+        got = _noalloc(lib, cfg, mode, x, u, h, c)
+        assert (got == want).all(), f"mode {mode}"
+    ctx.close()

@@ -497,7 +497,17 @@ VDXS_API int32_t vdxs_sample_noalloc(const vdxs_config* cfg, int32_t tie_mode, c
     e = a.path == kFull ? plan_full(a, &plan, &msg) : plan_topk(a, optin, &plan, &msg);
     if (e != cudaSuccess) return fail(nullptr, VDXS_E_UNSUPPORTED, "%s", msg.c_str());
     Workspace ws;
-    const size_t need = carve_workspace(ws, (unsigned char*)scratch, kNoAllocScratchBytes, a, plan);
+    size_t need = carve_workspace(ws, (unsigned char*)scratch, kNoAllocScratchBytes, a, plan);
+    if (need > kNoAllocScratchBytes && plan.stream && plan.cand_cap > 4096) {
+        // Row lists sized for many stage-1 warps per row (small batches, wide top_k) may not
+        // fit the array: shorter lists give the same tokens (a row whose list overflows is
+        // selected from the whole row), only slower.
+        const int base = (int)std::min<int64_t>(std::max<int64_t>(32LL * a.K, 4096), (int64_t)plan.cand_cap);
+        if (base < plan.cand_cap) {
+            plan.cand_cap = base;
+            need = carve_workspace(ws, (unsigned char*)scratch, kNoAllocScratchBytes, a, plan);
+        }
+    }
     if (need > kNoAllocScratchBytes)
         return fail(nullptr, VDXS_E_UNSUPPORTED,
                     "this call needs %zu bytes of workspace; the allocation-free entry point has %zu "
