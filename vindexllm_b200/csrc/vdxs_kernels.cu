@@ -2168,7 +2168,8 @@ __device__ __forceinline__ uint16_t nan_bits<uint16_t>() { return (uint16_t)0x7F
 // as they are taken (not those in the bound's own bin, which cannot raise it), and the
 // first slot of each unit is filtered against the K-th largest of its chunk maxima as
 // well (top_k <= 256). A warp raises the row bound (row_tau, atomicMax) from the
-// histogram asynchronously: the two dependent reads overlap the next two slots.
+// histogram asynchronously: the group counts are read at the end of a slot, the bin
+// counts at the start of the next, and the raise completes at that slot's end.
 //
 // Output: one list per row. Candidates wait in a per-warp shared region and are written
 // out when it fills and at the end of each unit if they still reach the bound then. The
@@ -2184,7 +2185,7 @@ constexpr int kS1SlotBytes = 4096;                    // one bulk copy; a 128-by
 constexpr int kS1Ring = 2;                            // ring slots per warp
 constexpr int kS1WCap = 128;                          // region entries per warp
 constexpr int kS1CoopLanes = 8;                       // up to this many hot lanes: warp-cooperative test
-constexpr int kS1RaiseEvery = 4;                      // counted candidates between bound raises
+constexpr int kS1RaiseEvery = 1;                      // counted candidates between bound raises
 constexpr int kRowHistWords = kTBins + kTGroups;      // per-row histogram in global memory
 constexpr int kS1WarpBytes = kS1Ring * kS1SlotBytes + 64 + 8 * kS1WCap + 4 * 256;
 static_assert(kS1WarpBytes % 16 == 0, "16-byte aligned warp areas");
@@ -2757,11 +2758,14 @@ __global__ void __launch_bounds__(kS1Threads, 1) topk_stream_kernel(KParams p) {
                 S1_ADD(8, total);
             }
             since += __reduce_add_sync(FULL, counted);
-            if (since >= (uint32_t)kS1RaiseEvery) {
-                since = 0u;
-                raise_start();
-            }
             S1_T1(1, t_hot);
+        }
+        // A raise whose bin counts were requested at this slot's start completes here (the
+        // filter hid the read), and the next one can start at once: one raise per slot.
+        if (rs_state == 2) raise_step();
+        if (since >= (uint32_t)kS1RaiseEvery && rs_state == 0) {
+            since = 0u;
+            raise_start();
         }
 
         // ---- release the slot: its next bulk copy goes behind the warp's reads ----
