@@ -520,7 +520,7 @@ struct SmemPairSrc {  // stage 2: (key, index) pairs in shared memory, tie-break
     __device__ __forceinline__ uint32_t tb(int i) const { return t[i]; }
 };
 
-template <int UN = 4, class Src>
+template <class Src>
 __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, int tb_bits,
                                   uint32_t* hist, uint32_t* sh) {
     const int tid = threadIdx.x;
@@ -528,14 +528,14 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
     r.tie_cut = 0;
     for (int i = tid; i < kHistBins; i += NT) hist[i] = 0u;
     __syncthreads();
-    // Every pass loads UN elements per thread before it counts them, so that reads from
-    // global memory (a row source) overlap.
-    for (int i0 = tid; i0 < n; i0 += UN * NT) {
-        uint32_t k[UN];
+    // Every pass loads four elements per thread before it counts them, so that reads
+    // from global memory (a row source) overlap.
+    for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+        uint32_t k[4];
 #pragma unroll
-        for (int u = 0; u < UN; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
 #pragma unroll
-        for (int u = 0; u < UN; ++u)
+        for (int u = 0; u < 4; ++u)
             if (k[u]) atomicAdd(&hist[logbin(kmax - k[u])], 1u);
     }
     __syncthreads();
@@ -562,12 +562,12 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
         const uint32_t width = 1u << bits;
         for (int i = tid; i < 256; i += NT) hist[i] = 0u;
         __syncthreads();
-        for (int i0 = tid; i0 < n; i0 += UN * NT) {
-            uint32_t k[UN];
+        for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+            uint32_t k[4];
 #pragma unroll
-            for (int u = 0; u < UN; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+            for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
 #pragma unroll
-            for (int u = 0; u < UN; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 const uint32_t dd = (kmax - k[u]) - dlo;
                 if (k[u] && dd < width) atomicAdd(&hist[dd >> shift], 1u);
             }
@@ -598,12 +598,12 @@ __device__ SelectOut block_select(const Src& src, int n, int K, uint32_t kmax, i
         const uint32_t hi_mask = tbits >= 32 ? 0u : (0xFFFFFFFFu << tbits);
         for (int i = tid; i < 256; i += NT) hist[i] = 0u;
         __syncthreads();
-        for (int i0 = tid; i0 < n; i0 += UN * NT) {
-            bool eq[UN];
+        for (int i0 = tid; i0 < n; i0 += 4 * NT) {
+            bool eq[4];
 #pragma unroll
-            for (int u = 0; u < UN; ++u) eq[u] = i0 + u * NT < n && src.key(i0 + u * NT) == r.kth_key;
+            for (int u = 0; u < 4; ++u) eq[u] = i0 + u * NT < n && src.key(i0 + u * NT) == r.kth_key;
 #pragma unroll
-            for (int u = 0; u < UN; ++u) {
+            for (int u = 0; u < 4; ++u) {
                 if (eq[u]) {
                     const uint32_t t = src.tb(i0 + u * NT);
                     if (((t ^ tlo) & hi_mask) == 0u) atomicAdd(&hist[(t >> shift) & ((1u << w) - 1u)], 1u);
@@ -1372,21 +1372,21 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
 
 // Writes every selected element of src to (ok, oi), returns the count (uniform).
-template <int UN = 4, class Src, class IdxF>
+template <class Src, class IdxF>
 __device__ int block_emit(const Src& src, int n, const SelectOut& s, uint32_t* ok, uint32_t* oi, int cap,
                           uint32_t* counter, IdxF idx_of) {
     const int tid = threadIdx.x;
     if (tid == 0) *counter = 0u;
     __syncthreads();
-    for (int i0 = tid; i0 - tid < n; i0 += UN * NT) {
-        uint32_t k[UN];
-        bool sel[UN];
+    for (int i0 = tid; i0 - tid < n; i0 += 4 * NT) {
+        uint32_t k[4];
+        bool sel[4];
 #pragma unroll
-        for (int u = 0; u < UN; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
+        for (int u = 0; u < 4; ++u) k[u] = i0 + u * NT < n ? src.key(i0 + u * NT) : 0u;
 #pragma unroll
-        for (int u = 0; u < UN; ++u) sel[u] = i0 + u * NT < n && selected(k[u], src.tb(i0 + u * NT), s);
+        for (int u = 0; u < 4; ++u) sel[u] = i0 + u * NT < n && selected(k[u], src.tb(i0 + u * NT), s);
 #pragma unroll
-        for (int u = 0; u < UN; ++u) {
+        for (int u = 0; u < 4; ++u) {
             const unsigned m = __ballot_sync(FULL, sel[u]);
             if (m) {
                 uint32_t base = 0u;
