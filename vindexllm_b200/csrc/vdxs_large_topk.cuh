@@ -1,12 +1,15 @@
 // vdxs_large_topk.cuh - the top-k path for 1024 < top_k < V (Sampler.pas:327-459 with a
 // K-slot buffer larger than the shared-memory paths hold). Included by vdxs_kernels.cu
-// inside namespace vdxs, after the block primitives, block_select and block_emit.
+// inside namespace vdxs, after the block primitives, block_select, block_emit, the
+// stage-1 list source (ListSrc) and the stream kernel's constants.
 //
 // One 256-thread CTA per row (a persistent grid walks the rows), with a per-CTA
 // workspace in global memory of 24 bytes per slot:
 //   1. the row maximum, then an exact radix select of the K best (key desc, index asc)
-//      elements over the row in global memory (penalised values overlaid from the
-//      per-row bitmap and the sorted penalty lists) and their compaction;
+//      elements and their compaction, over the row's stage-1 list and penalised entries
+//      when the stream kernel ran first (32 K <= V) and the list is complete, else over
+//      the row in global memory (penalised values overlaid from the per-row bitmap and
+//      the sorted penalty lists);
 //   2. probabilities, min-p, a single-CTA LSD radix sort of (probability, ~index) keys,
 //      and the reference's sequential double walk (Sampler.pas:385-459) by one thread
 //      over values staged through shared memory: the canonical token;
